@@ -1,0 +1,346 @@
+#!/usr/bin/env python
+"""Benchmark: DiskLLM's sampler chain on batched logits, B200.
+
+Workload (the one the headline metric is quoted on): per GPU, a
+batch of 1024 rows x vocab 256000 fp32 logits drawn flat N(0, 0.5^2), repetition penalty 1.05
+over a 256-id uniform history, temperature 1.0, top-k off, top-p 0.99 (the reference's
+index-order prefix), one seeded uniform per row.  A step samples the whole batch: one launch
+of the fused kernel.  Inputs are 1.05 GB per GPU, larger than the 126 MB L2, so no flush is
+needed between steps.  Multi-GPU: one process per GPU, rows sharded (each rank samples its
+own 1024-row batch; no collective on the data path) -> weak scaling.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sampled rows/sec and achieved HBM GB/s vs ~8 TB/s at 1/2/4/8 B200"
+ROWS, VOCAB, HIST = 1024, 256000, 256
+PARAMS = dict(temperature=1.0, top_k=0, top_p=0.99, repetition=1.05)
+KERNEL = "sample_rows_kernel"
+
+
+def algo_bytes_per_row():
+    return VOCAB * 4 + HIST * 4  # logits + history ids (no mask in this configuration)
+
+
+def config_block(n):
+    return {
+        "workload": "cfg4_nucleus_b1024_v256000_fp32 (BASELINE config 4)",
+        "rows_per_gpu": ROWS, "global_batch": ROWS * n, "vocab": VOCAB, "history": HIST,
+        "params": PARAMS, "parallelism": f"row-sharded x{n} (no collective)",
+        "l2_policy": "inputs larger than L2 (1.05 GB per GPU vs 126 MB L2); no flush",
+    }
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", f"{KERNEL}_cfg4.md")
+    try:
+        txt = open(p).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch\s*[:=]\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+# ----------------------------------------------------------------------------------------------
+# clocks during the timed region (NVML polled every 20 ms)
+
+class ClockSampler:
+    def __init__(self, dev_index):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(dev_index).uuid)
+            h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                hh = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(hh)
+                u = u.decode() if isinstance(u, bytes) else u
+                if uuid in u:
+                    h = hh
+                    break
+            if h is None:
+                h = pynvml.nvmlDeviceGetHandleByIndex(dev_index)
+            self.h, self.nv = h, pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # reported in the JSON
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, reasons))
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"error": getattr(self, "err", "nvml unavailable")}
+        names = {"gpu_idle": 0x1, "sw_power_cap": 0x4, "hw_slowdown": 0x8,
+                 "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+                 "hw_power_brake_slowdown": 0x80}
+        seen = set()
+        for _, r in self.samples:
+            for k, bit in names.items():
+                if r & bit:
+                    seen.add(k)
+        mhz = [m for m, _ in self.samples]
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": self.max_mhz,
+                "samples": len(mhz), "reasons": sorted(seen)}
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU baseline: DiskLLM's own sampler.c (oracle/_ref, as built) or the restated port
+
+def host_rows(n, seed=404):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    lg = (rng.standard_normal((n, VOCAB), dtype=np.float32) * 0.5).astype(np.float32)
+    hist = [rng.integers(0, VOCAB, HIST) for _ in range(n)]
+    return lg, hist
+
+
+def cpu_run(lg, hist, threads):
+    """one pass of the CPU implementation over the rows; returns (seconds, kind)"""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+
+    import oracle as O
+
+    if O.have_reference():
+        _, secs = O.sample_reference(lg, PARAMS, hist=hist, threads=threads, stream=True)
+        return secs, "reference"
+    t0 = time.perf_counter()
+    O.sample_restated(lg, PARAMS, np.full(lg.shape[0], 0.5, np.float32), hist=hist, threads=threads)
+    return time.perf_counter() - t0, "port"
+
+
+def cpu_baseline(seconds=10.0):
+    threads = os.cpu_count() or 1
+    lg, hist = host_rows(64)
+    done, tot, kind = 0, 0.0, "port"
+    while tot < seconds:
+        s, kind = cpu_run(lg, hist, threads)
+        done += lg.shape[0]
+        tot += s
+    return {"value": done / tot, "unit": "rows/s", "cores": threads, "kind": kind,
+            "sample": f"{lg.shape[0]} rows of config 4 (V={VOCAB}, history {HIST}) repeated for "
+                      f"{tot:.1f} s on {threads} threads (one reference sampler per thread)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    per_step = max(64, 2 * threads)
+    lg, hist = host_rows(per_step)
+    kind = "port"
+    for _ in range(args.warmup):
+        cpu_run(lg, hist, threads)
+    tot = 0.0
+    for _ in range(args.steps):
+        s, kind = cpu_run(lg, hist, threads)
+        tot += s
+    value = per_step * args.steps / tot
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * tot / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.5^2) rows)",
+        "config": config_block(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": kind,
+                         "sample": f"{per_step} rows of config 4 per step, {threads} threads"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, dev):
+    import torch
+
+    from diskllm_b200 import capi
+    from diskllm_b200 import workloads as W
+
+    capi.load_library()
+    w = W.config4(device=dev, seed=404 + rank)
+    stream = torch.cuda.current_stream(dev)
+    tok = torch.empty(ROWS, dtype=torch.int32, device=dev)
+
+    def step():
+        capi.sample_batch(w.logits, w.uniforms, PARAMS, hist_ids=w.hist_ids, hist_off=w.hist_off,
+                          hist_max=HIST, token=tok)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    clocks = ClockSampler(dev.index)
+    barrier()
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+
+    # end to end through the public API with host buffers: pinned host -> device copy of the
+    # step's inputs, the sampler, device -> host copy of the sampled ids
+    h_logits = w.logits.cpu().pin_memory()
+    h_hid = w.hist_ids.cpu().pin_memory()
+    h_hoff = w.hist_off.cpu().pin_memory()
+    h_u = w.uniforms.cpu().pin_memory()
+    h_tok = torch.empty(ROWS, dtype=torch.int32).pin_memory()
+    d_logits = torch.empty_like(w.logits)
+    d_hid = torch.empty_like(w.hist_ids)
+    d_hoff = torch.empty_like(w.hist_off)
+    d_u = torch.empty_like(w.uniforms)
+    h2d = h_logits.numel() * 4 + h_hid.numel() * 4 + h_hoff.numel() * 8 + h_u.numel() * 4
+    d2h = ROWS * 4
+
+    def e2e_step():
+        d_logits.copy_(h_logits, non_blocking=True)
+        d_hid.copy_(h_hid, non_blocking=True)
+        d_hoff.copy_(h_hoff, non_blocking=True)
+        d_u.copy_(h_u, non_blocking=True)
+        capi.sample_batch(d_logits, d_u, PARAMS, hist_ids=d_hid, hist_off=d_hoff, hist_max=HIST,
+                          token=tok)
+        h_tok.copy_(tok, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    e2e_rows_s = ROWS * world / (ms_e2e / e2e_steps / 1e3)
+
+    if rank != 0:
+        return
+    value = ROWS * world / (ms_step / 1e3)
+    peak, peak_kind = measured_peak()
+    achieved = ROWS * algo_bytes_per_row() / (ms_step / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,0.5^2) rows, uniform histories, Philox uniforms)",
+        "config": config_block(world),
+        "achieved_hbm_gbs": achieved,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak,
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s",
+                     "traffic": profiled_traffic(),
+                     "algorithmic_bytes_per_launch": ROWS * algo_bytes_per_row(),
+                     "kernel": KERNEL},
+        "e2e": {"value": e2e_rows_s, "unit": "rows/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    import torch
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=dev)
+    try:
+        run_ours(args, rank, world, dev)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,288 @@
+"""ctypes binding of libdiskllm_cuda.so (include/diskllm_cuda.h, include/sampler.h).
+
+This is the Python host side above the C ABI.  It mirrors DiskLLM's sampler interface
+(include/sampler.h:7-34: sampler_create / sampler_free / sampler_apply_*_penalty /
+sampler_sample / greedy_sample) and adds the batched device entry point.  The library is
+required: loading it on a machine without the built .so raises, and nothing here falls back
+to a host implementation.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libdiskllm_cuda.so")
+
+DLLM_OK = 0
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "NCCL", 5: "TIMEOUT",
+                6: "UNSUPPORTED"}
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+MODE_TOPP_SORTED = 0x1
+MODE_PEN_TRUE_DIV = 0x2
+ROW_ERR_HIST_TABLE = 1
+ROW_ERR_NONFINITE = 2
+ROW_ERR_TOPK_LARGE = 4
+ROW_ERR_WALK = 8
+ROW_ERR_TIMEOUT = 16
+
+# every symbol the public headers declare
+EXPORTS = [
+    "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
+    "dllm_cuda_set_debug_counters",
+    "dllm_sampler_get_rng_state", "dllm_sampler_set_rng_state",
+    "sampler_create", "sampler_free", "sampler_apply_repetition_penalty",
+    "sampler_apply_presence_penalty", "sampler_sample", "greedy_sample",
+]
+
+
+class DllmError(RuntimeError):
+    pass
+
+
+class SamplerParams(C.Structure):
+    """dllm_sampler_params"""
+    _fields_ = [
+        ("temperature", C.c_float),
+        ("top_p", C.c_float),
+        ("min_p", C.c_float),
+        ("top_k", C.c_int),
+        ("repetition", C.c_float),
+        ("presence", C.c_float),
+        ("frequency", C.c_float),
+    ]
+
+
+class SamplerConfig(C.Structure):
+    """sampler_config (DiskLLM include/sampler.h:10-16)"""
+    _fields_ = [
+        ("temperature", C.c_float),
+        ("top_k", C.c_int),
+        ("top_p", C.c_float),
+        ("min_p", C.c_float),
+        ("seed", C.c_uint64),
+    ]
+
+
+class BatchDesc(C.Structure):
+    """dllm_batch_desc"""
+    _fields_ = [
+        ("rows", C.c_int),
+        ("vocab", C.c_int),
+        ("row_stride", C.c_int64),
+        ("dtype", C.c_int),
+        ("logits", C.c_void_p),
+        ("mask", C.c_void_p),
+        ("mask_stride", C.c_int64),
+        ("hist_ids", C.c_void_p),
+        ("hist_off", C.c_void_p),
+        ("hist_max", C.c_int),
+        ("uniforms", C.c_void_p),
+        ("params", SamplerParams),
+        ("row_params", C.c_void_p),
+        ("topk_max", C.c_int),
+        ("flags", C.c_uint),
+        ("token", C.c_void_p),
+        ("probs", C.c_void_p),
+        ("probs_stride", C.c_int64),
+        ("pen_logits", C.c_void_p),
+        ("pen_stride", C.c_int64),
+        ("status", C.c_void_p),
+        ("topk_ids", C.c_void_p),
+        ("topk_stride", C.c_int64),
+    ]
+
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> C.CDLL:
+    """Loads libdiskllm_cuda.so; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise DllmError(f"{path} is missing: build it with `python -m diskllm_b200.build`")
+    lib = C.CDLL(path)
+    lib.dllm_cuda_sample_batch.restype = C.c_int
+    lib.dllm_cuda_sample_batch.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
+    lib.dllm_cuda_set_debug_counters.restype = C.c_int
+    lib.dllm_cuda_set_debug_counters.argtypes = [C.c_void_p]
+    lib.dllm_cuda_version.restype = C.c_char_p
+    lib.dllm_cuda_last_error.restype = C.c_char_p
+    lib.dllm_sampler_get_rng_state.restype = C.c_uint64
+    lib.dllm_sampler_get_rng_state.argtypes = [C.c_void_p]
+    lib.dllm_sampler_set_rng_state.restype = None
+    lib.dllm_sampler_set_rng_state.argtypes = [C.c_void_p, C.c_uint64]
+    lib.sampler_create.restype = C.c_void_p
+    lib.sampler_create.argtypes = [C.POINTER(SamplerConfig)]
+    lib.sampler_free.restype = None
+    lib.sampler_free.argtypes = [C.c_void_p]
+    lib.sampler_sample.restype = C.c_int
+    lib.sampler_sample.argtypes = [C.c_void_p, C.c_void_p, C.c_int]
+    lib.greedy_sample.restype = C.c_int
+    lib.greedy_sample.argtypes = [C.c_void_p, C.c_int]
+    for name in ("sampler_apply_repetition_penalty", "sampler_apply_presence_penalty"):
+        f = getattr(lib, name)
+        f.restype = None
+        f.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_float]
+    _lib = lib
+    return lib
+
+
+def set_debug_counters(tensor_or_none):
+    """Points the kernels' diagnostic counters at a zeroed CUDA int64 tensor of >= 32 entries
+    (or switches them off with None)."""
+    ptr = None if tensor_or_none is None else tensor_or_none.data_ptr()
+    rc = load_library().dllm_cuda_set_debug_counters(ptr)
+    if rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_set_debug_counters: {STATUS_NAMES.get(rc, rc)}")
+
+
+def version() -> str:
+    return load_library().dllm_cuda_version().decode()
+
+
+def make_params(temperature=1.0, top_p=1.0, min_p=0.0, top_k=0, repetition=1.0, presence=0.0,
+                frequency=0.0) -> SamplerParams:
+    return SamplerParams(float(temperature), float(top_p), float(min_p), int(top_k),
+                         float(repetition), float(presence), float(frequency))
+
+
+# ---------------------------------------------------------------------------------------------
+# drop-in sampler (host pointers, like DiskLLM's sampler.h)
+
+class Sampler:
+    """DiskLLM's `sampler` object (src/sampler.c:56-95) served by the CUDA library."""
+
+    def __init__(self, temperature=0.7, top_k=40, top_p=0.9, min_p=0.0, seed=0):
+        self._lib = load_library()
+        cfg = SamplerConfig(float(temperature), int(top_k), float(top_p), float(min_p), int(seed))
+        self._h = self._lib.sampler_create(C.byref(cfg))
+        if not self._h:
+            raise DllmError("sampler_create returned NULL")
+
+    def close(self):
+        if self._h:
+            self._lib.sampler_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def rng_state(self) -> int:
+        return int(self._lib.dllm_sampler_get_rng_state(self._h))
+
+    @rng_state.setter
+    def rng_state(self, v: int):
+        self._lib.dllm_sampler_set_rng_state(self._h, int(v))
+
+    def sample(self, logits: np.ndarray) -> int:
+        a = np.ascontiguousarray(logits, dtype=np.float32)
+        return int(self._lib.sampler_sample(self._h, a.ctypes.data, a.shape[0]))
+
+
+def greedy_sample(logits: np.ndarray) -> int:
+    a = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(load_library().greedy_sample(a.ctypes.data, a.shape[0]))
+
+
+def apply_repetition_penalty(logits: np.ndarray, seen, penalty: float) -> None:
+    """In place on a float32 numpy row, like src/sampler.c:21-33."""
+    assert logits.dtype == np.float32 and logits.flags.c_contiguous
+    ids = np.ascontiguousarray(seen, dtype=np.int32)
+    load_library().sampler_apply_repetition_penalty(logits.ctypes.data, logits.shape[0],
+                                                    ids.ctypes.data, ids.shape[0], penalty)
+
+
+def apply_presence_penalty(logits: np.ndarray, seen, presence: float) -> None:
+    """In place on a float32 numpy row, like src/sampler.c:35-52."""
+    assert logits.dtype == np.float32 and logits.flags.c_contiguous
+    ids = np.ascontiguousarray(seen, dtype=np.int32)
+    load_library().sampler_apply_presence_penalty(logits.ctypes.data, logits.shape[0],
+                                                  ids.ctypes.data, ids.shape[0], presence)
+
+
+# ---------------------------------------------------------------------------------------------
+# batched device entry point (torch tensors are only containers for device memory here)
+
+def fill_desc(logits, uniforms, params=None, *, mask=None, hist_ids=None, hist_off=None,
+              hist_max=None, row_params=None, topk_max=0, flags=0, token=None, probs=None,
+              pen_logits=None, status=None, topk_ids=None) -> tuple[BatchDesc, object]:
+    """Builds a dllm_batch_desc from CUDA tensors; returns (desc, token tensor)."""
+    import torch
+
+    assert logits.is_cuda and logits.dim() == 2
+    rows, vocab = logits.shape
+    if logits.dtype == torch.float32:
+        dt = DTYPE_F32
+    elif logits.dtype == torch.bfloat16:
+        dt = DTYPE_BF16
+    else:
+        raise TypeError(f"unsupported logits dtype {logits.dtype}")
+    assert logits.stride(1) == 1
+    if token is None:
+        token = torch.empty(rows, dtype=torch.int32, device=logits.device)
+    if params is None:
+        params = make_params()
+    elif isinstance(params, dict):
+        params = make_params(**params)
+    d = BatchDesc()
+    d.rows, d.vocab, d.row_stride, d.dtype = rows, vocab, logits.stride(0), dt
+    d.logits = logits.data_ptr()
+    if mask is not None:
+        assert mask.dtype in (torch.int32, torch.uint32) and mask.is_cuda
+        d.mask, d.mask_stride = mask.data_ptr(), mask.stride(0)
+    if hist_ids is not None:
+        assert hist_ids.dtype == torch.int32 and hist_off.dtype == torch.int64
+        d.hist_ids, d.hist_off = hist_ids.data_ptr(), hist_off.data_ptr()
+        if hist_max is None:
+            hist_max = int((hist_off[1:] - hist_off[:-1]).max().item()) if rows else 0
+        d.hist_max = int(hist_max)
+    assert uniforms.dtype == torch.float32 and uniforms.is_cuda
+    d.uniforms = uniforms.data_ptr()
+    d.params = params
+    if row_params is not None:
+        d.row_params = row_params.data_ptr()
+        d.topk_max = int(topk_max)
+    d.flags = int(flags)
+    d.token = token.data_ptr()
+    if probs is not None:
+        d.probs, d.probs_stride = probs.data_ptr(), probs.stride(0)
+    if pen_logits is not None:
+        d.pen_logits, d.pen_stride = pen_logits.data_ptr(), pen_logits.stride(0)
+    if status is not None:
+        d.status = status.data_ptr()
+    if topk_ids is not None:
+        d.topk_ids, d.topk_stride = topk_ids.data_ptr(), topk_ids.stride(0)
+    return d, token
+
+
+def sample_batch(logits, uniforms, params=None, *, stream=None, check=True, **kw):
+    """Calls dllm_cuda_sample_batch on CUDA tensors.  Returns the int32 token tensor."""
+    import torch
+
+    d, token = fill_desc(logits, uniforms, params, **kw)
+    if stream is None:
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+    rc = load_library().dllm_cuda_sample_batch(C.byref(d), C.c_void_p(stream))
+    if check and rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_sample_batch: {STATUS_NAMES.get(rc, rc)} "
+                        f"({load_library().dllm_cuda_last_error().decode()})")
+    return token
+
+
+def params_array(rows_params, device):
+    """list of dicts -> device tensor laid out as dllm_sampler_params[rows]"""
+    import torch
+
+    arr = (SamplerParams * len(rows_params))(*[make_params(**p) for p in rows_params])
+    raw = np.frombuffer(bytes(arr), dtype=np.uint8).copy()
+    return torch.from_numpy(raw).to(device)

@@ -1,0 +1,328 @@
+// dllm_capi.cu -- the C ABI of libdiskllm_cuda.so (include/diskllm_cuda.h, include/sampler.h).
+//
+// dllm_cuda_sample_batch validates a descriptor, picks (and caches) a launch configuration
+// for the row length and starts the fused sampler kernel.  The sampler.h drop-ins keep the
+// reference's host-pointer contract: they copy the row to the device, run the same kernels
+// and copy results back.  None of them computes on the host.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+#include <new>
+#include <vector>
+
+#include "dllm_internal.h"
+#include "sampler.h"
+
+using namespace dllm;
+
+static thread_local char g_last_error[256] = "";
+
+static void set_error(const char *what, cudaError_t e) {
+    snprintf(g_last_error, sizeof g_last_error, "%s: %s", what, cudaGetErrorString(e));
+}
+
+extern "C" const char *dllm_cuda_last_error(void) { return g_last_error; }
+
+extern "C" dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters) {
+    return set_debug_counters(device_counters);
+}
+
+extern "C" const char *dllm_cuda_version(void) { return "diskllm_cuda 0.1.0 sm_100a"; }
+
+// ----------------------------------------------------------------------------------------
+// launch configuration cache
+
+namespace {
+struct CfgKey {
+    int dev, vocab, dtype, hist_bound, topk_cap;
+    bool operator==(const CfgKey &o) const {
+        return dev == o.dev && vocab == o.vocab && dtype == o.dtype && hist_bound == o.hist_bound &&
+               topk_cap == o.topk_cap;
+    }
+};
+std::mutex g_cfg_mu;
+std::vector<std::pair<CfgKey, LaunchCfg>> g_cfgs;
+
+int bucket(int x) {
+    if (x <= 0) return 0;
+    int p = 16;
+    while (p < x) p <<= 1;
+    return p;
+}
+}  // namespace
+
+static dllm_status get_config(int vocab, int dtype, int hist_max, int topk_max, LaunchCfg *out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        set_error("cudaGetDevice", e);
+        return DLLM_ERR_CUDA;
+    }
+    CfgKey key{dev, vocab, dtype, bucket(hist_max), topk_max > 0 ? bucket(topk_max) : 0};
+    std::lock_guard<std::mutex> lk(g_cfg_mu);
+    for (auto &kv : g_cfgs)
+        if (kv.first == key) {
+            *out = kv.second;
+            return DLLM_OK;
+        }
+    LaunchCfg c;
+    dllm_status st = choose_config(vocab, dtype, key.hist_bound, key.topk_cap, &c);
+    if (st != DLLM_OK) return st;
+    g_cfgs.push_back({key, c});
+    *out = c;
+    return DLLM_OK;
+}
+
+// ----------------------------------------------------------------------------------------
+// batched entry point
+
+extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *stream) {
+    if (!d) return DLLM_ERR_INVALID_ARG;
+    if (d->rows < 0 || d->vocab <= 0 || !d->logits || !d->uniforms || !d->token) return DLLM_ERR_INVALID_ARG;
+    if (d->row_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
+    if (d->dtype != DLLM_DTYPE_F32 && d->dtype != DLLM_DTYPE_BF16) return DLLM_ERR_INVALID_ARG;
+    if (d->mask && d->mask_stride < (d->vocab + 31) / 32) return DLLM_ERR_INVALID_ARG;
+    if ((d->hist_ids == nullptr) != (d->hist_off == nullptr)) return DLLM_ERR_INVALID_ARG;
+    if (d->hist_ids && d->hist_max < 0) return DLLM_ERR_INVALID_ARG;
+    if (d->probs && d->probs_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
+    if (d->pen_logits && d->pen_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
+    if (d->topk_ids && d->topk_stride < (d->row_params ? d->topk_max : d->params.top_k))
+        return DLLM_ERR_INVALID_ARG;
+    if (d->flags & ~(unsigned)DLLM_MODE_PEN_TRUE_DIV) return DLLM_ERR_UNSUPPORTED;
+    if (d->rows == 0) return DLLM_OK;
+
+    int topk_max = d->row_params ? d->topk_max : d->params.top_k;
+    if (topk_max >= d->vocab) topk_max = 0;
+    if (topk_max < 0) topk_max = 0;
+    if (topk_max > KMAX) return DLLM_ERR_UNSUPPORTED;
+
+    LaunchCfg cfg;
+    dllm_status st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
+    if (st != DLLM_OK) return st;
+
+    KernelArgs a = {};
+    a.logits = d->logits;
+    a.row_stride = d->row_stride;
+    a.dtype = d->dtype;
+    const int vec = d->dtype == DLLM_DTYPE_F32 ? 4 : 8;
+    a.vec_ok = ((uintptr_t)d->logits % 16 == 0) && (d->row_stride % vec == 0);
+    a.mask = d->mask;
+    a.mask_stride = d->mask_stride;
+    a.hist_ids = d->hist_ids;
+    a.hist_off = d->hist_off;
+    a.uniforms = d->uniforms;
+    a.bparams = d->params;
+    a.rparams = d->row_params;
+    a.rows = d->rows;
+    a.vocab = d->vocab;
+    a.vocab_total = d->vocab;
+    a.vocab_offset = 0;
+    a.S = cfg.S;
+    a.L = cfg.L;
+    a.htab = cfg.htab;
+    a.uni_bytes = (int)(cfg.smem - (size_t)cfg.S * 4);
+    a.cluster = cfg.cluster;
+    a.flags = d->flags;
+    a.token = d->token;
+    a.probs = d->probs;
+    a.probs_stride = d->probs_stride;
+    a.pen_out = d->pen_logits;
+    a.pen_stride = d->pen_stride;
+    a.status = d->status;
+    a.topk_ids = d->topk_ids;
+    a.topk_stride = d->topk_stride;
+    st = launch_sample(a, cfg, (cudaStream_t)stream);
+    if (st != DLLM_OK) set_error("sample kernel launch", cudaGetLastError());
+    return st;
+}
+
+// ----------------------------------------------------------------------------------------
+// history penalty kernel for the host-pointer drop-ins (src/sampler.c:21-52): one CTA,
+// thread i owns history entry i; the first occurrence of each id applies the penalty.
+
+__global__ void penalty_kernel(float *logits, int vocab, const int *seen, int n, float value, int mode) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int id = seen[i];
+        if (id < 0 || id >= vocab) continue;
+        bool first = true;
+        int count = 1;
+        for (int j = 0; j < i; j++)
+            if (seen[j] == id) {
+                first = false;
+                break;
+            }
+        if (!first) continue;
+        for (int j = i + 1; j < n; j++) count += seen[j] == id;
+        float v = logits[id];
+        if (mode == 0) {  // repetition, once per occurrence
+            const float inv = __fdiv_rn(1.0f, value);
+            for (int k = 0; k < count; k++) v = v < 0.0f ? __fmul_rn(v, value) : __fmul_rn(v, inv);
+        } else {          // presence, once per id
+            v = __fsub_rn(v, value);
+        }
+        logits[id] = v;
+    }
+}
+
+// ----------------------------------------------------------------------------------------
+// drop-in sampler.h
+
+struct DevBuf {
+    int dev = -1;
+    cudaStream_t stream = nullptr;
+    float *row = nullptr;
+    int cap = 0;
+    int *ids = nullptr;
+    int ids_cap = 0;
+    float *u = nullptr;
+    int32_t *tok = nullptr;
+};
+
+struct sampler {
+    sampler_config cfg;
+    uint64_t rng;
+    DevBuf buf;
+};
+
+[[noreturn]] static void die(const char *what, cudaError_t e) {
+    fprintf(stderr, "libdiskllm_cuda: %s failed: %s\n", what, cudaGetErrorString(e));
+    abort();
+}
+#define DLLM_CHECK(x)                          \
+    do {                                       \
+        cudaError_t _e = (x);                  \
+        if (_e != cudaSuccess) die(#x, _e);    \
+    } while (0)
+
+static void buf_reserve(DevBuf &b, int vocab, int nids) {
+    if (!b.stream) {
+        DLLM_CHECK(cudaGetDevice(&b.dev));
+        DLLM_CHECK(cudaStreamCreateWithFlags(&b.stream, cudaStreamNonBlocking));
+        DLLM_CHECK(cudaMalloc(&b.u, sizeof(float)));
+        DLLM_CHECK(cudaMalloc(&b.tok, sizeof(int32_t)));
+    }
+    if (vocab > b.cap) {
+        if (b.row) DLLM_CHECK(cudaFree(b.row));
+        DLLM_CHECK(cudaMalloc(&b.row, sizeof(float) * (size_t)vocab));
+        b.cap = vocab;
+    }
+    if (nids > b.ids_cap) {
+        if (b.ids) DLLM_CHECK(cudaFree(b.ids));
+        DLLM_CHECK(cudaMalloc(&b.ids, sizeof(int) * (size_t)nids));
+        b.ids_cap = nids;
+    }
+}
+
+static void buf_release(DevBuf &b) {
+    if (b.row) cudaFree(b.row);
+    if (b.ids) cudaFree(b.ids);
+    if (b.u) cudaFree(b.u);
+    if (b.tok) cudaFree(b.tok);
+    if (b.stream) cudaStreamDestroy(b.stream);
+    b = DevBuf();
+}
+
+static thread_local DevBuf t_free_buf;  // for greedy_sample / penalties (no sampler object)
+
+static int run_one_row(DevBuf &b, const float *host_logits, int vocab, const dllm_sampler_params &p, float r) {
+    buf_reserve(b, vocab, 0);
+    DLLM_CHECK(cudaMemcpyAsync(b.row, host_logits, sizeof(float) * (size_t)vocab, cudaMemcpyHostToDevice, b.stream));
+    DLLM_CHECK(cudaMemcpyAsync(b.u, &r, sizeof(float), cudaMemcpyHostToDevice, b.stream));
+    dllm_batch_desc d = {};
+    d.rows = 1;
+    d.vocab = vocab;
+    d.row_stride = vocab;
+    d.dtype = DLLM_DTYPE_F32;
+    d.logits = b.row;
+    d.uniforms = b.u;
+    d.params = p;
+    d.token = b.tok;
+    dllm_status st = dllm_cuda_sample_batch(&d, b.stream);
+    if (st != DLLM_OK) {
+        fprintf(stderr, "libdiskllm_cuda: dllm_cuda_sample_batch failed (%d): %s\n", (int)st, g_last_error);
+        abort();
+    }
+    int32_t tok = 0;
+    DLLM_CHECK(cudaMemcpyAsync(&tok, b.tok, sizeof(int32_t), cudaMemcpyDeviceToHost, b.stream));
+    DLLM_CHECK(cudaStreamSynchronize(b.stream));
+    return tok;
+}
+
+extern "C" sampler *sampler_create(const sampler_config *cfg) {
+    if (!cfg) return nullptr;
+    sampler *s = (sampler *)calloc(1, sizeof(sampler));
+    if (!s) return nullptr;
+    new (&s->buf) DevBuf();
+    s->cfg = *cfg;
+    s->rng = cfg->seed ? cfg->seed : 0xDEADBEEF12345678ULL;
+    return s;
+}
+
+extern "C" void sampler_free(sampler *s) {
+    if (!s) return;
+    buf_release(s->buf);
+    free(s);
+}
+
+extern "C" uint64_t dllm_sampler_get_rng_state(const sampler *s) { return s ? s->rng : 0; }
+extern "C" void dllm_sampler_set_rng_state(sampler *s, uint64_t st) {
+    if (s) s->rng = st;
+}
+
+// xorshift64 and its uniform, src/sampler.c:69-81
+static float next_uniform(uint64_t *state) {
+    uint64_t x = *state;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *state = x;
+    return (float)(x >> 11) * (1.0f / (float)(1ULL << 53));
+}
+
+extern "C" int sampler_sample(sampler *s, float *logits, int vocab_size) {
+    if (!s || !logits || vocab_size <= 0) return 0;
+    dllm_sampler_params p = {};
+    p.temperature = s->cfg.temperature;
+    p.top_k = s->cfg.top_k;
+    p.top_p = s->cfg.top_p;
+    p.min_p = s->cfg.min_p;
+    p.repetition = 1.0f;
+    const float r = p.temperature == 0.0f ? 0.0f : next_uniform(&s->rng);
+    return run_one_row(s->buf, logits, vocab_size, p, r);
+}
+
+extern "C" int greedy_sample(const float *logits, int vocab_size) {
+    if (!logits || vocab_size <= 0) return 0;
+    dllm_sampler_params p = {};
+    p.temperature = 0.0f;
+    p.top_p = 1.0f;
+    p.repetition = 1.0f;
+    return run_one_row(t_free_buf, logits, vocab_size, p, 0.0f);
+}
+
+static void apply_penalty(float *logits, int vocab, const int *seen, int n, float value, int mode) {
+    DevBuf &b = t_free_buf;
+    buf_reserve(b, vocab, n);
+    DLLM_CHECK(cudaMemcpyAsync(b.row, logits, sizeof(float) * (size_t)vocab, cudaMemcpyHostToDevice, b.stream));
+    DLLM_CHECK(cudaMemcpyAsync(b.ids, seen, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, b.stream));
+    penalty_kernel<<<1, 1024, 0, b.stream>>>(b.row, vocab, b.ids, n, value, mode);
+    DLLM_CHECK(cudaGetLastError());
+    DLLM_CHECK(cudaMemcpyAsync(logits, b.row, sizeof(float) * (size_t)vocab, cudaMemcpyDeviceToHost, b.stream));
+    DLLM_CHECK(cudaStreamSynchronize(b.stream));
+}
+
+extern "C" void sampler_apply_repetition_penalty(float *logits, int vocab_size, const int *seen_tokens,
+                                                 int num_seen, float penalty) {
+    if (penalty <= 1.0f || !seen_tokens || num_seen <= 0 || !logits || vocab_size <= 0) return;
+    apply_penalty(logits, vocab_size, seen_tokens, num_seen, penalty, 0);
+}
+
+extern "C" void sampler_apply_presence_penalty(float *logits, int vocab_size, const int *seen_tokens,
+                                               int num_seen, float presence_penalty) {
+    if (presence_penalty == 0.0f || !seen_tokens || num_seen <= 0 || !logits || vocab_size <= 0) return;
+    apply_penalty(logits, vocab_size, seen_tokens, num_seen, presence_penalty, 1);
+}

@@ -1,0 +1,72 @@
+// dllm_internal.h -- launch arguments shared by the sampler kernels and their host launchers.
+// Not part of the public C ABI (that is include/diskllm_cuda.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "diskllm_cuda.h"
+
+namespace dllm {
+
+// Per-row status bits written to dllm_batch_desc::status (0 = OK).
+enum : int32_t {
+    ROW_ERR_HIST_TABLE = 1,   // more distinct in-slice history ids than the table holds
+    ROW_ERR_NONFINITE  = 2,   // +inf / NaN row maximum (unsupported input)
+    ROW_ERR_TOPK_LARGE = 4,   // top_k above the kernel's candidate capacity
+    ROW_ERR_WALK       = 8,   // internal consistency check of the draw walk failed
+    ROW_ERR_TIMEOUT    = 16,  // a bounded wait on a bulk copy expired
+};
+
+// Largest top-k list the fused kernel handles.
+constexpr int KMAX = 1024;
+
+struct KernelArgs {
+    const void     *logits;
+    int64_t         row_stride;     // elements between rows of logits
+    int             dtype;          // DLLM_DTYPE_F32 / DLLM_DTYPE_BF16
+    int             vec_ok;         // 16-byte vector loads legal for every row
+    const uint32_t *mask;
+    int64_t         mask_stride;    // uint32 words between rows of mask
+    const int32_t  *hist_ids;
+    const int64_t  *hist_off;
+    const float    *uniforms;
+    dllm_sampler_params bparams;    // broadcast params
+    const dllm_sampler_params *rparams; // per-row params (device) or null
+    int             rows;
+    int             vocab;          // ids in this logits slice
+    int             vocab_total;    // full vocabulary (history ids are checked against it)
+    int             vocab_offset;   // global id of local index 0
+    int             S;              // slice length per CTA (= NT * L)
+    int             L;              // elements per thread chunk (L % 8 == 4)
+    int             htab;           // history hash-table entries (power of 2)
+    int             uni_bytes;      // bytes of the shared area after the slice
+    int             cluster;        // CTAs per row (cluster size)
+    unsigned        flags;
+    int32_t        *token;
+    float          *probs;          // dense [rows][vocab] final probabilities or null
+    int64_t         probs_stride;
+    float          *pen_out;        // dense [rows][vocab] penalised logits or null
+    int64_t         pen_stride;
+    int32_t        *status;         // [rows] or null
+    int32_t        *topk_ids;       // [rows][topk_stride] or null
+    int64_t         topk_stride;
+    unsigned long long *dbg;        // diagnostic counters or null
+};
+
+// Launch configuration chosen by the host for one (vocab, dtype, history bound, top-k bound).
+struct LaunchCfg {
+    int cluster;     // C
+    int threads;     // NT
+    int L;
+    int S;
+    int htab;
+    size_t smem;     // dynamic shared memory bytes
+    int max_clusters;// co-resident clusters on the device
+};
+
+dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
+dllm_status set_debug_counters(unsigned long long *dev_counters);
+dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream);
+
+}  // namespace dllm

@@ -1,0 +1,1588 @@
+// dllm_kernel.cuh -- fused batched sampler for B200 (sm_100a): device code.
+// Included by dllm_kernel_inst.cu, which is compiled once per chunk length.
+//
+// One thread-block cluster samples one row at a time (persistent over rows).  The row is split
+// into C contiguous slices, one per CTA; each slice is copied from HBM once into shared memory
+// with a bulk (TMA) copy while the next row's slice is prefetched into L2, and every later pass
+// reads shared memory.  Thread t of a CTA owns one contiguous chunk of L elements of the slice
+// (L is a compile-time constant, L % 8 == 4, so 16-byte shared loads of a warp are free of bank
+// conflicts).  Per row:
+//
+//   P1  bulk copy, grammar mask -> -inf, history penalties from an in-shared-memory hash table
+//       (presence / frequency once per id, repetition once per occurrence), slice maximum
+//                                                                         -> cluster max M
+//   greedy (temperature 0): first index holding M                        -> token
+//   top-k (0 < k < V): per-thread maxima give a threshold with >= k elements at or above it;
+//       the survivors are gathered into CTA 0, sorted by (t desc, id asc), the first k kept,
+//       and softmax / min-p / top-p / draw run on that short list (a 4-pass radix select is
+//       the fallback when too many elements survive the threshold)
+//   otherwise (top-k off: the reference's index-order list):
+//   P2  t = (x - M) * (1/T), e = expf(t - max_t) in place, double sum    -> cluster sum
+//   P2b min-p (absolute threshold) kept count / renormalisation sum      -> cluster sums
+//   P3  chunk sums of the list probabilities, exclusive scan over the cluster; the one warp
+//       holding the chunk where (float)cumsum first reaches top_p finds the cut element
+//                                                                          -> cluster
+//   P4  exact emulation of the reference's sequential fp32 draw (src/sampler.c:226-231).
+//       Within one binade [2^e, 2^(e+1)) of the running sum c, fl(c + q) = c + n*ulp(c), where
+//       n depends only on q and on the parity of c/ulp (ties-to-even), so a run of adds is a
+//       function of one parity bit: (n_even, n_odd).  Each thread computes that pair for four
+//       sub-chunks of its chunk (real fp32 chains started at 2^e and 2^e + ulp, e predicted from
+//       the exact double prefix), composes them, and each warp composes its 32 chunks into a
+//       record of the form prefix / one boundary chunk / suffix.  The records are gathered in
+//       CTA 0, where one walker warp composes them in order on the exact running sum, checking
+//       every step's validity, replaying boundary chunks in plain fp32 (cooperatively, a few
+//       elements per lane) and descending into the chunk where the uniform falls.
+//
+// Bit-exactness: the translation unit is built with -fmad=false and -ftz=true (the reference
+// executables run with FTZ|DAZ); every operation that must round like the reference is an
+// explicit __f*_rn intrinsic.
+#pragma once
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "dllm_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace dllm {
+
+typedef void (*KernelFn)(const KernelArgs);
+
+// everything below has internal linkage: this header is compiled into several units
+namespace {
+
+constexpr int MAXW = 16;          // warps per CTA (blockDim <= 512)
+constexpr int CAND_CAP = 2048;    // top-k survivors gathered in CTA 0
+constexpr int STASH_SLOTS = 24;   // boundary chunks whose probabilities are gathered in CTA 0
+constexpr int TMA_PIECE = 32768;  // bytes per bulk copy instruction
+constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
+
+enum : int { REC_IDENT = 0, REC_CLEAN = 1, REC_MIXED = 2, REC_PBS = 3 };
+
+// Diagnostic counters: per-phase cycles of cluster rank 0 and draw-walk statistics.  Each
+// CTA's thread 0 stores KernelArgs::dbg here at kernel start (every CTA stores the same
+// value).  Null in normal operation.
+__device__ unsigned long long *g_dbg = nullptr;
+enum : int {
+    DBG_P1 = 0, DBG_W1 = 1, DBG_P2 = 2, DBG_W2 = 3, DBG_P3 = 4, DBG_W3 = 5, DBG_CUT = 6,
+    DBG_P4 = 7, DBG_W5 = 8, DBG_WALK = 9, DBG_WEND = 10, DBG_TOPK = 11, DBG_LOADWAIT = 12,
+    DBG_ROWS = 16, DBG_REPLAY = 17, DBG_EXPAND = 18, DBG_STEPS = 19, DBG_REPLAY_IT = 20,
+    DBG_PBS = 21, DBG_STASH_MISS = 22, DBG_TOPK_FALLBACK = 23,
+};
+__device__ __forceinline__ void dbg_add(int k, unsigned long long v) {
+    if (g_dbg) atomicAdd(g_dbg + k, v);
+}
+
+// Warp-level record: a prefix run of chunks in binade e_pre, an optional boundary chunk, and a
+// suffix run (from chunk sfrom) in binade e_suf.  REC_CLEAN uses only the prefix fields.
+struct WRec {
+    int type;
+    int e_pre;
+    uint32_t p0, p1;
+    int bchunk;       // boundary chunk (lane) or -1
+    int e_suf;
+    uint32_t s0, s1;
+    int slot;         // stash slot holding the boundary chunk's probabilities, or -1
+    int sfrom;        // first chunk of the suffix
+    int pad[2];
+};
+
+// Values each CTA publishes to its cluster.  Every field is written at most once per row and
+// read only after the cluster barrier that follows the write.
+struct Xch {
+    float m;
+    float mt;
+    double dsum;
+    double s2;
+    double s2all;
+    int nkept;
+    double tot;
+    int first_member;
+    float first_w;
+    int last_member;
+    int cut_idx;
+    double cut_s3;
+    int gidx;
+    int flags;
+    uint32_t theta;
+    int cnt_gt, cnt_eq;
+    int ncand;        // CTA 0: survivors gathered
+    int nstash;       // CTA 0: stash slots used
+    unsigned hist[2][256];
+};
+
+struct Shared {
+    Xch xs;
+    unsigned long long tma_bar;
+    double red_d[MAXW];
+    float red_f[MAXW];
+    int red_i[MAXW];
+    int red_i2[MAXW];
+    int bcast_i[4];
+};
+
+__device__ __forceinline__ uint32_t fbits(float x) { return __float_as_uint(x); }
+__device__ __forceinline__ float bitsf(uint32_t b) { return __uint_as_float(b); }
+
+// ----------------------------------------------------------------------------------------
+// PTX: shared-memory barrier, bulk copies (no multicast), L2 prefetch
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// ----------------------------------------------------------------------------------------
+// block / warp helpers (deterministic: every thread computes identical results)
+
+template <class T, class Op>
+__device__ __forceinline__ T warp_allreduce(T v, Op op) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <class T, class Op>
+__device__ T block_allreduce(T v, T *scratch, Op op) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_allreduce(v, op);
+    __syncthreads();
+    if (lane == 0) scratch[w] = v;
+    __syncthreads();
+    T r = scratch[0];
+    for (int i = 1; i < nw; i++) r = op(r, scratch[i]);
+    return r;
+}
+
+// Exclusive / inclusive scan of doubles in thread order.  excl(t+1) is bit-identical to
+// incl(t), and the returned total is bit-identical to incl(last).
+__device__ void block_scan_d(double v, double *scratch, double &excl, double &incl, double &total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    double x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        double y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x = y + x;
+    }
+    double prev = __shfl_up_sync(0xffffffffu, x, 1);
+    __syncthreads();
+    if (lane == 31) scratch[w] = x;
+    __syncthreads();
+    double off = 0.0;
+    for (int i = 0; i < w; i++) off = off + scratch[i];
+    double tot = off;
+    for (int i = w; i < nw; i++) tot = tot + scratch[i];
+    excl = lane == 0 ? off : off + prev;
+    incl = off + x;
+    total = tot;
+}
+
+__device__ void block_scan_i(int v, int *scratch, int &excl, int &total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+    }
+    __syncthreads();
+    if (lane == 31) scratch[w] = x;
+    __syncthreads();
+    int off = 0, tot = 0;
+    for (int i = 0; i < nw; i++) {
+        if (i < w) off += scratch[i];
+        tot += scratch[i];
+    }
+    excl = off + x - v;
+    total = tot;
+}
+
+// ----------------------------------------------------------------------------------------
+// probability chain of one element (index-order path)
+
+struct Chain {
+    float inv_sum;
+    float min_p;
+    float inv_s2;
+    float inv_s3;
+    int cut_idx;   // last index inside the top-p prefix (INT_MAX when no cut)
+    int minp;      // min-p active
+    int nokept;    // min-p active but no element reached it: all stay (sampler.c:196)
+    int topp;      // top-p renormalisation active
+};
+
+// probability after softmax and min-p (0 for elements min-p removed)
+__device__ __forceinline__ float w_of(const Chain &ch, float e) {
+    float p = __fmul_rn(e, ch.inv_sum);
+    if (ch.minp) p = (ch.nokept || p >= ch.min_p) ? __fmul_rn(p, ch.inv_s2) : 0.0f;
+    return p;
+}
+__device__ __forceinline__ bool member_of(const Chain &ch, float e) {
+    if (!ch.minp || ch.nokept) return true;
+    return __fmul_rn(e, ch.inv_sum) >= ch.min_p;
+}
+// final draw probability
+__device__ __forceinline__ float q_of(const Chain &ch, float e, int gi) {
+    float w = w_of(ch, e);
+    if (ch.topp) w = gi <= ch.cut_idx ? __fmul_rn(w, ch.inv_s3) : 0.0f;
+    return w;
+}
+
+// ----------------------------------------------------------------------------------------
+// exact fp32 running-sum walk
+//
+// REC_CLEAN(e, n0, n1): starting from any c in binade e (exponent field e) whose bit pattern
+// has parity s, the run ends at bits(c) + n_s, provided the result stays below 2^(e+1).
+// REC_IDENT adds only zeros.  REC_MIXED must be expanded.
+
+// Composition scan over lanes: (a0, a1) of lane l becomes the composition of lanes <= l.
+__device__ __forceinline__ void compose_scan(uint32_t &a0, uint32_t &a1) {
+    const int lane = threadIdx.x & 31;
+    if (__ballot_sync(0xffffffffu, a0 != a1) == 0u) {
+        // no run depends on the parity: composition is a plain sum
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            uint32_t p = __shfl_up_sync(0xffffffffu, a0, d);
+            if (lane >= d) a0 += p;
+        }
+        a1 = a0;
+        return;
+    }
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+        uint32_t p0 = __shfl_up_sync(0xffffffffu, a0, d);
+        uint32_t p1 = __shfl_up_sync(0xffffffffu, a1, d);
+        if (lane >= d) {
+            uint32_t x0 = a0, x1 = a1;
+            a0 = p0 + ((p0 & 1u) ? x1 : x0);
+            a1 = p1 + (((1u + p1) & 1u) ? x1 : x0);
+        }
+    }
+}
+
+// Applies one CLEAN run (e, n0, n1) to cb when valid; returns false (cb unchanged) when the run
+// cannot be applied to this cb (wrong binade, or the result would leave it).
+__device__ __forceinline__ bool apply_run(uint32_t &cb, int e, uint32_t n0, uint32_t n1) {
+    if (n0 == 0u && n1 == 0u) return true;
+    if (cb == 0u || (cb >> 23) != (uint32_t)e) return false;
+    const uint32_t out = cb + ((cb & 1u) ? n1 : n0);
+    if (out >= ((uint32_t)(e + 1) << 23)) return false;
+    cb = out;
+    return true;
+}
+
+// One step of the walk over up to 32 records held one per lane (lanes >= n invalid), from
+// record `pos`.  Either processes a run of valid CLEAN/IDENT records, or expands one record.
+// Returns the drawn index (>= 0), -1 to continue (pos advanced), -2 on an internal error.
+template <class Expand>
+__device__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t n1, uint32_t &cb,
+                         float r, Expand &&expand) {
+    const int lane = threadIdx.x & 31;
+    if (lane == 0) dbg_add(DBG_STEPS, 1);
+    const unsigned live = __ballot_sync(0xffffffffu, lane >= pos && lane < n && type != REC_IDENT);
+    if (!live) {
+        pos = n;
+        return -1;
+    }
+    const int f = __ffs(live) - 1;
+    const int tf = __shfl_sync(0xffffffffu, type, f);
+    const int ef = __shfl_sync(0xffffffffu, e, f);
+    const bool inbin = cb != 0u && (cb >> 23) == (uint32_t)ef;
+    if (tf != REC_CLEAN || !inbin) {
+        int res = expand(f, cb);
+        pos = f + 1;
+        return res;
+    }
+    const unsigned runm = __ballot_sync(0xffffffffu, lane >= f && lane < n &&
+                                                         (type == REC_IDENT || (type == REC_CLEAN && e == ef)));
+    const unsigned notrun = ~runm & (0xffffffffu << f);
+    int run_end = notrun ? __ffs(notrun) - 1 : 32;
+    if (run_end > n) run_end = n;
+    const bool inrun = lane >= f && lane < run_end;
+    uint32_t a0 = (inrun && type == REC_CLEAN) ? n0 : 0u;
+    uint32_t a1 = (inrun && type == REC_CLEAN) ? n1 : 0u;
+    compose_scan(a0, a1);
+    const uint32_t inc = (cb & 1u) ? a1 : a0;
+    const uint32_t cout = cb + inc;
+    const uint32_t lim = (uint32_t)(ef + 1) << 23;
+    const unsigned bad = __ballot_sync(0xffffffffu, inrun && !(cout < lim));
+    const int good_end = bad ? __ffs(bad) - 1 : run_end;
+    const unsigned hit = __ballot_sync(0xffffffffu, lane >= f && lane < good_end && r < bitsf(cout));
+    const uint32_t prev = __shfl_up_sync(0xffffffffu, cout, 1);
+    if (hit) {
+        const int l = __ffs(hit) - 1;
+        const uint32_t prevl = __shfl_sync(0xffffffffu, prev, l);
+        cb = (l == f) ? cb : prevl;
+        int res = expand(l, cb);
+        pos = n;
+        return res >= 0 ? res : -2;
+    }
+    const uint32_t last = __shfl_sync(0xffffffffu, cout, good_end > f ? good_end - 1 : f);
+    if (good_end > f) cb = last;
+    pos = good_end;
+    if (pos < run_end) {
+        int res = expand(pos, cb);
+        pos = pos + 1;
+        return res;
+    }
+    return -1;
+}
+
+// Replays n (<= 8*32) consecutive draw probabilities on the exact running sum cb.
+// Warp-cooperative: lane l owns a sub-range of ceil(n/32) elements.  `load(j)` returns the
+// probability of element j; `gbase + j` is its index.  Returns the drawn index, -1 (not in
+// this range; cb advanced past it) or -2.
+template <class Load>
+__device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, Load &&load) {
+    const int lane = threadIdx.x & 31;
+    const int s = (n + 31) >> 5;
+    const int j0 = lane * s;
+    const int cnt = max(0, min(s, n - j0));
+    float q[8];
+    bool anyq = false;
+#pragma unroll
+    for (int k = 0; k < 8; k++) {
+        q[k] = 0.0f;
+        if (k < cnt) {
+            q[k] = load(j0 + k);
+            anyq |= q[k] != 0.0f;
+        }
+    }
+    if (lane == 0) dbg_add(DBG_REPLAY, 1);
+    // serial replay of one lane's sub-range on the exact running sum
+    auto serial = [&](int jl, uint32_t &cbx) -> int {
+        int found = -1;
+        uint32_t nb = 0;
+        if (lane == jl) {
+            float c = bitsf(cbx);
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (k < cnt) {
+                    c = __fadd_rn(c, q[k]);
+                    if (found < 0 && r < c) found = gbase + j0 + k;
+                }
+            }
+            nb = fbits(c);
+        }
+        found = __shfl_sync(0xffffffffu, found, jl);
+        cbx = __shfl_sync(0xffffffffu, nb, jl);
+        return found;
+    };
+    int pos = 0;
+    for (int guard = 0; pos < 32 && guard < 96; guard++) {
+        if (lane == 0) dbg_add(DBG_REPLAY_IT, 1);
+        if (cb == 0u) {
+            const unsigned m = __ballot_sync(0xffffffffu, lane >= pos && anyq);
+            if (!m) return -1;
+            const int fl = __ffs(m) - 1;
+            int found = serial(fl, cb);
+            pos = fl + 1;
+            if (found >= 0) return found;
+            continue;
+        }
+        const uint32_t eb = cb >> 23;
+        const uint32_t gb = eb << 23, lim = (eb + 1u) << 23;
+        float g0 = bitsf(gb), g1 = bitsf(gb | 1u);
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            if (k < cnt) {
+                g0 = __fadd_rn(g0, q[k]);
+                g1 = __fadd_rn(g1, q[k]);
+            }
+        }
+        const int type = !anyq ? REC_IDENT : ((fbits(g0) < lim && fbits(g1) < lim) ? REC_CLEAN : REC_MIXED);
+        const uint32_t n0 = fbits(g0) - gb, n1 = fbits(g1) - (gb | 1u);
+        int res = walk_step(32, pos, type, (int)eb, n0, n1, cb, r, serial);
+        if (res != -1) return res;
+    }
+    return pos < 32 ? -2 : -1;
+}
+
+// ----------------------------------------------------------------------------------------
+// short sorted list: softmax, min-p, top-p, draw (src/sampler.c:172-233) by one warp.
+// t[i] sorted best-first with ids id[i]; k entries.  Probabilities are written over t[].
+// The double sums run in a different order than the reference's loops; they agree to ~1e-16
+// relative, so (float)(1.0 / sum) is identical except at measure-zero rounding ties.
+
+__device__ double warp_sum_list(const float *v, int k) {
+    const int lane = threadIdx.x & 31;
+    double s = 0.0;
+    for (int i = lane; i < k; i += 32) s = s + (double)v[i];
+    return warp_allreduce(s, [](double x, double y) { return x + y; });
+}
+
+__device__ int sample_sorted_list(float *t, int *id, int k, const dllm_sampler_params &p, float r,
+                                  float *probs_row) {
+    const int lane = threadIdx.x & 31;
+    const float mv = t[0];
+    for (int i = lane; i < k; i += 32) t[i] = expf(__fsub_rn(t[i], mv));
+    __syncwarp();
+    const double sum = warp_sum_list(t, k);
+    const float inv_sum = __double2float_rn(1.0 / sum);
+    for (int i = lane; i < k; i += 32) t[i] = __fmul_rn(t[i], inv_sum);
+    __syncwarp();
+    int kk = k;
+    if (p.min_p > 0.0f) {
+        // stable compaction of the entries with p >= min_p
+        int nk = 0;
+        for (int base = 0; base < kk; base += 32) {
+            const int i = base + lane;
+            const float v = i < kk ? t[i] : 0.0f;
+            const int vid = i < kk ? id[i] : 0;
+            const bool keep = i < kk && v >= p.min_p;
+            const unsigned m = __ballot_sync(0xffffffffu, keep);
+            __syncwarp();
+            if (keep) {
+                const int o = nk + __popc(m & ((1u << lane) - 1u));
+                t[o] = v;
+                id[o] = vid;
+            }
+            nk += __popc(m);
+            __syncwarp();
+        }
+        if (nk > 0) kk = nk;
+        const double s2 = warp_sum_list(t, kk);
+        const float inv2 = __double2float_rn(1.0 / s2);
+        for (int i = lane; i < kk; i += 32) t[i] = __fmul_rn(t[i], inv2);
+        __syncwarp();
+    }
+    if (p.top_p < 1.0f) {
+        int nk = kk;
+        double carry = 0.0, s3 = 0.0;
+        bool found = false;
+        for (int base = 0; base < kk && !found; base += 32) {
+            const int i = base + lane;
+            double x = i < kk ? (double)t[i] : 0.0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                double y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x = y + x;
+            }
+            const double cum = carry + x;
+            const unsigned hit = __ballot_sync(0xffffffffu, i < kk && __double2float_rn(cum) >= p.top_p);
+            if (hit) {
+                const int l = __ffs(hit) - 1;
+                nk = base + l + 1;
+                s3 = __shfl_sync(0xffffffffu, cum, l);
+                found = true;
+            } else {
+                carry = __shfl_sync(0xffffffffu, cum, 31);
+            }
+        }
+        if (!found) s3 = carry;
+        kk = nk;
+        const float inv3 = __double2float_rn(1.0 / s3);
+        for (int i = lane; i < kk; i += 32) t[i] = __fmul_rn(t[i], inv3);
+        __syncwarp();
+    }
+    int tok = 0;
+    if (lane == 0) {
+        float c = 0.0f;
+        tok = id[kk - 1];
+        for (int i = 0; i < kk; i++) {
+            c = __fadd_rn(c, t[i]);
+            if (r < c) {
+                tok = id[i];
+                break;
+            }
+        }
+    }
+    if (probs_row)
+        for (int i = lane; i < kk; i += 32) probs_row[id[i]] = t[i];
+    return __shfl_sync(0xffffffffu, tok, 0);
+}
+
+// ----------------------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t okey(float t) {
+    const uint32_t u = fbits(t);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float okey_inv(uint32_t k) {
+    return bitsf((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+__device__ __forceinline__ uint32_t hash_id(uint32_t x) {
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    return x;
+}
+
+__device__ __forceinline__ void bf16x8_to_f32(const uint4 raw, float *d) {
+    const uint32_t wv[4] = {raw.x, raw.y, raw.z, raw.w};
+    float4 *d4 = reinterpret_cast<float4 *>(d);
+    d4[0] = make_float4(bitsf(wv[0] << 16), bitsf(wv[0] & 0xffff0000u), bitsf(wv[1] << 16),
+                        bitsf(wv[1] & 0xffff0000u));
+    d4[1] = make_float4(bitsf(wv[2] << 16), bitsf(wv[2] & 0xffff0000u), bitsf(wv[3] << 16),
+                        bitsf(wv[3] & 0xffff0000u));
+}
+
+// bf16 slices: 16-byte streaming loads (four in flight per thread), upcast exactly
+__device__ void load_slice_bf16(const KernelArgs &a, int row, int slice0, int slen, float *vals) {
+    const int NT = blockDim.x, tid = threadIdx.x;
+    const __nv_bfloat16 *src = (const __nv_bfloat16 *)a.logits + (int64_t)row * a.row_stride + slice0;
+    int done = 0;
+    if (a.vec_ok) {
+        const int n8 = slen >> 3;
+        const uint4 *s8 = (const uint4 *)src;
+        int i = tid;
+        for (; i + 3 * NT < n8; i += 4 * NT) {
+            uint4 raw[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) raw[u] = __ldcs(s8 + i + u * NT);
+#pragma unroll
+            for (int u = 0; u < 4; u++) bf16x8_to_f32(raw[u], vals + 8 * (i + u * NT));
+        }
+        for (; i < n8; i += NT) bf16x8_to_f32(__ldcs(s8 + i), vals + 8 * i);
+        done = n8 * 8;
+    }
+    const unsigned short *s16 = (const unsigned short *)src;
+    for (int i = done + tid; i < slen; i += NT) vals[i] = bitsf((uint32_t)s16[i] << 16);
+}
+
+// ----------------------------------------------------------------------------------------
+
+template <int DT, int LT>
+__global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a) {
+    static_assert(LT % 8 == 4 && LT <= 252, "chunk length");
+    constexpr int NV = LT / 4;      // float4 per chunk
+    constexpr int SUB = LT / 4;     // elements per sub-chunk (four sub-chunks per chunk)
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(16) unsigned char dsm[];
+    __shared__ Shared sh;
+
+    const int NT = blockDim.x, NW = NT >> 5;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int C = a.cluster;
+    const int rank = (int)cluster.block_rank();
+    const int cid = blockIdx.x / C, ncl = gridDim.x / C;
+    const int S = a.S, V = a.vocab;
+    const int slice0 = rank * S;
+    const int slen = max(0, min(S, V - slice0));
+    const int cbase = tid * LT;               // slice-relative start of this thread's chunk
+
+    float *vals = reinterpret_cast<float *>(dsm);
+    unsigned char *uni = dsm + (size_t)S * sizeof(float);
+    // union area: history table | chunk records + walk stash | top-k survivors + list
+    int *hkeys = reinterpret_cast<int *>(uni);
+    int *hcnt = hkeys + a.htab;
+    int *rec_type = reinterpret_cast<int *>(uni);
+    int *rec_e = rec_type + NT;
+    uint32_t *rec_n0 = reinterpret_cast<uint32_t *>(rec_e + NT);
+    uint32_t *rec_n1 = rec_n0 + NT;
+    // CTA 0 only: the cluster's warp records, then stashed boundary-chunk probabilities
+    WRec *wstash = reinterpret_cast<WRec *>(rec_n1 + NT);
+    float *qstash = reinterpret_cast<float *>(wstash + C * NW);
+    unsigned long long *cand = reinterpret_cast<unsigned long long *>(uni);
+
+    auto remote_xs = [&](int r) -> Xch * { return cluster.map_shared_rank(&sh.xs, r); };
+
+    if (tid == 0) {
+        g_dbg = a.dbg;
+        mbar_init(&sh.tma_bar, 1);
+        fence_proxy_async();
+    }
+    __syncthreads();
+
+    const bool timing = a.dbg != nullptr && rank == 0 && tid == 0;
+    long long tmark = clock64();
+    auto mark = [&](int k) {
+        if (timing) {
+            const long long t = clock64();
+            dbg_add(k, (unsigned long long)(t - tmark));
+            tmark = t;
+        }
+    };
+
+    // bulk copy of this CTA's slice of `row` (fp32 rows with 16-byte aligned slices)
+    const bool use_tma = DT == DLLM_DTYPE_F32 && a.vec_ok;
+    const int tma_elems = slen & ~3;
+    auto issue_row_copy = [&](int row) {
+        const unsigned char *src = reinterpret_cast<const unsigned char *>(
+            (const float *)a.logits + (int64_t)row * a.row_stride + slice0);
+        const uint32_t bytes = (uint32_t)tma_elems * 4u;
+        mbar_arrive_expect_tx(&sh.tma_bar, bytes);
+        for (uint32_t off = 0; off < bytes; off += TMA_PIECE) {
+            const uint32_t nb = bytes - off < (uint32_t)TMA_PIECE ? bytes - off : (uint32_t)TMA_PIECE;
+            bulk_g2s(reinterpret_cast<unsigned char *>(vals) + off, src + off, nb, &sh.tma_bar);
+        }
+    };
+    auto prefetch_row = [&](int row) {
+        const unsigned char *src = reinterpret_cast<const unsigned char *>(
+            (const float *)a.logits + (int64_t)row * a.row_stride + slice0);
+        const uint32_t bytes = (uint32_t)tma_elems * 4u;
+        for (uint32_t off = 0; off < bytes; off += TMA_PIECE) {
+            const uint32_t nb = bytes - off < (uint32_t)TMA_PIECE ? bytes - off : (uint32_t)TMA_PIECE;
+            prefetch_l2(src + off, nb);
+        }
+    };
+
+    uint32_t phase = 0;
+    for (int row = cid; row < a.rows; row += ncl, phase ^= 1u) {
+        if (timing) dbg_add(DBG_ROWS, 1);
+        const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
+        const float r = a.uniforms[row];
+        int flags = 0;
+
+        // ---------------- P1: bulk copy in flight while the history table is built ---------------
+        if (use_tma && tid == 0) {
+            issue_row_copy(row);
+            if (row + ncl < a.rows) prefetch_row(row + ncl);
+        }
+        for (int i = tid; i < a.htab; i += NT) {
+            hkeys[i] = -1;
+            hcnt[i] = 0;
+        }
+        __syncthreads();
+        const bool use_hist = a.hist_ids && a.hist_off &&
+                              (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
+        if (use_hist) {
+            const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+            const uint32_t hm = (uint32_t)a.htab - 1u;
+            for (int64_t j = h0 + tid; j < h1; j += NT) {
+                const int id = a.hist_ids[j];
+                if (id < 0 || id >= a.vocab_total) continue;
+                const int li = id - a.vocab_offset - slice0;
+                if (li < 0 || li >= slen) continue;
+                uint32_t h = hash_id((uint32_t)li) & hm;
+                bool placed = false;
+                for (int probe = 0; probe < a.htab; probe++) {
+                    const int old = atomicCAS(&hkeys[h], -1, li);
+                    if (old == -1 || old == li) {
+                        atomicAdd(&hcnt[h], 1);
+                        placed = true;
+                        break;
+                    }
+                    h = (h + 1u) & hm;
+                }
+                if (!placed) flags |= ROW_ERR_HIST_TABLE;
+            }
+        }
+        if (use_tma) {
+            const float *src = (const float *)a.logits + (int64_t)row * a.row_stride + slice0;
+            for (int i = tma_elems + tid; i < slen; i += NT) vals[i] = __ldcs(src + i);
+        } else if (DT == DLLM_DTYPE_F32) {
+            const float *src = (const float *)a.logits + (int64_t)row * a.row_stride + slice0;
+            for (int i = tid; i < slen; i += NT) vals[i] = __ldcs(src + i);
+        } else {
+            load_slice_bf16(a, row, slice0, slen, vals);
+        }
+        for (int i = slen + tid; i < S; i += NT) vals[i] = -INFINITY;
+        if (use_tma) {
+            long long it = 0;
+            while (!mbar_try_wait(&sh.tma_bar, phase)) {
+                if (++it > WAIT_LIMIT) {
+                    flags |= ROW_ERR_TIMEOUT;
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        mark(DBG_LOADWAIT);
+
+        // mask + raw maximum over this thread's chunk
+        float lmax = -INFINITY;
+        {
+            float4 *v4 = reinterpret_cast<float4 *>(vals + cbase);
+            const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
+            if (mrow) {
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const int li = slice0 + cbase + 4 * j;
+                    float4 x = v4[j];
+                    const uint32_t w = li < V ? (mrow[li >> 5] >> (li & 31)) : 0u;
+                    x.x = (w & 1u) ? x.x : -INFINITY;
+                    x.y = (w & 2u) ? x.y : -INFINITY;
+                    x.z = (w & 4u) ? x.z : -INFINITY;
+                    x.w = (w & 8u) ? x.w : -INFINITY;
+                    v4[j] = x;
+                    lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const float4 x = v4[j];
+                    lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+                }
+            }
+        }
+        const float mraw = block_allreduce(lmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+
+        // ---------------- P1: penalties ----------------------------------------------------------
+        float pmax = -INFINITY;
+        int rescan = 0;
+        if (use_hist) {
+            const float inv_rep = __fdiv_rn(1.0f, p.repetition);
+            const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
+            for (int s = tid; s < a.htab; s += NT) {
+                const int li = hkeys[s];
+                if (li < 0) continue;
+                const int c = hcnt[s];
+                float v = vals[li];
+                const float raw = v;
+                if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
+                if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
+                if (p.repetition > 1.0f) {
+                    for (int k = 0; k < c; k++) {
+                        if (v < 0.0f) v = __fmul_rn(v, p.repetition);
+                        else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
+                    }
+                }
+                vals[li] = v;
+                if (raw == mraw) rescan = 1;
+                pmax = fmaxf(pmax, v);
+            }
+        }
+        float lm;
+        {
+            const float pm = block_allreduce(pmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+            const int rf = block_allreduce((rescan ? 0x10000 : 0) | flags, sh.red_i, [](int x, int y) { return x | y; });
+            flags = rf & 0xffff;
+            if (rf & 0x10000) {
+                float m2 = -INFINITY;
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const float4 x = v4[j];
+                    m2 = fmaxf(m2, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+                }
+                lm = block_allreduce(m2, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+            } else {
+                lm = fmaxf(mraw, pm);
+            }
+        }
+        if (a.pen_out) {
+            float *po = a.pen_out + (int64_t)row * a.pen_stride + slice0;
+            for (int i = tid; i < slen; i += NT) po[i] = vals[i];
+        }
+        if (tid == 0) {
+            sh.xs.m = lm;
+            sh.xs.flags = flags;
+        }
+        mark(DBG_P1);
+        cluster.sync();  // ---- #1
+        mark(DBG_W1);
+        float M = -INFINITY;
+        int rowflags = 0;
+        {
+            float mv = -INFINITY;
+            int fv = 0;
+            if (lane < C) {
+                Xch *x = remote_xs(lane);
+                mv = x->m;
+                fv = x->flags;
+            }
+            M = warp_allreduce(mv, [](float x, float y) { return fmaxf(x, y); });
+            rowflags = warp_allreduce(fv, [](int x, int y) { return x | y; });
+        }
+
+        const bool greedy = p.temperature == 0.0f;
+        const bool topk = p.top_k > 0 && p.top_k < a.vocab_total;
+        int token = -1;
+
+        if (greedy) {
+            // ---------------- greedy: first index holding M ----------------------------------
+            int first = INT_MAX;
+            {
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+#pragma unroll
+                for (int j = NV - 1; j >= 0; j--) {
+                    const float4 x = v4[j];
+                    const int li = cbase + 4 * j;
+                    if (x.w == M && li + 3 < slen) first = li + 3;
+                    if (x.z == M && li + 2 < slen) first = li + 2;
+                    if (x.y == M && li + 1 < slen) first = li + 1;
+                    if (x.x == M && li < slen) first = li;
+                }
+                if (first != INT_MAX) first += slice0;
+            }
+            const int bf = block_allreduce(first, sh.red_i, [](int x, int y) { return min(x, y); });
+            if (tid == 0) sh.xs.gidx = bf;
+            cluster.sync();  // ---- greedy
+            int gv = INT_MAX;
+            if (lane < C) gv = remote_xs(lane)->gidx;
+            token = warp_allreduce(gv, [](int x, int y) { return min(x, y); });
+            if (token == INT_MAX) token = 0;
+        } else if (M == -INFINITY) {
+            // fully masked row: every t is NaN, comparisons fail, the reference's list stays in
+            // id order and it returns the last entry
+            token = topk ? p.top_k - 1 : a.vocab_total - 1;
+            if (topk && a.topk_ids && rank == 0)
+                for (int i = tid; i < p.top_k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = i + a.vocab_offset;
+        } else if (!(M < INFINITY) || M != M) {
+            rowflags |= ROW_ERR_NONFINITE;
+            token = 0;
+        } else if (topk) {
+            // ---------------- top-k ----------------------------------------------------------
+            const int k = p.top_k;
+            int kp2 = 1;
+            while (kp2 < k) kp2 <<= 1;
+            const float inv_temp = __fdiv_rn(1.0f, p.temperature);
+            auto key_of = [&](float v) -> uint32_t { return okey(__fmul_rn(__fsub_rn(v, M), inv_temp)); };
+            if (k > KMAX || 8 * kp2 + 8 * k > a.uni_bytes) {
+                rowflags |= ROW_ERR_TOPK_LARGE;
+                token = 0;
+                goto row_done;
+            }
+            {
+            // survivor capacity: a power of two whose sort buffer and the final list both fit
+            int cap = CAND_CAP;
+            while (cap > kp2 && 8 * cap + 8 * k > a.uni_bytes) cap >>= 1;
+            bool use_threshold = k <= NT && cap >= kp2 && 8 * cap + 8 * k <= a.uni_bytes;
+            if (use_threshold) {
+                // threshold: the k-th largest per-thread maximum (>= k elements at or above it)
+                uint32_t tmax = 0u;
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const float4 x = v4[j];
+                    const int li = cbase + 4 * j;
+                    if (li < slen) tmax = max(tmax, key_of(x.x));
+                    if (li + 1 < slen) tmax = max(tmax, key_of(x.y));
+                    if (li + 2 < slen) tmax = max(tmax, key_of(x.z));
+                    if (li + 3 < slen) tmax = max(tmax, key_of(x.w));
+                }
+                uint32_t pref = 0u;
+                for (int bit = 31; bit >= 0; bit--) {
+                    const uint32_t cv = pref | (1u << bit);
+                    if (__syncthreads_count(tmax >= cv) >= k) pref = cv;
+                }
+                if (tid == 0) {
+                    sh.xs.theta = pref;
+                    sh.xs.ncand = 0;
+                }
+                cluster.sync();  // ---- threshold
+                uint32_t tv = 0u;
+                if (lane < C) tv = remote_xs(lane)->theta;
+                const uint32_t theta = warp_allreduce(tv, [](uint32_t x, uint32_t y) { return max(x, y); });
+                // survivors -> CTA 0
+                int *ncand0 = &remote_xs(0)->ncand;
+                unsigned long long *cand0 = cluster.map_shared_rank(cand, 0);
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const float4 x = v4[j];
+                    const float xs4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int li = cbase + 4 * j + c;
+                        const uint32_t key = li < slen ? key_of(xs4[c]) : 0u;
+                        const bool take = li < slen && key >= theta;
+                        const unsigned m = __ballot_sync(0xffffffffu, take);
+                        if (m) {
+                            const int leader = __ffs(m) - 1;
+                            int base = 0;
+                            if (lane == leader) base = atomicAdd(ncand0, __popc(m));
+                            base = __shfl_sync(0xffffffffu, base, leader);
+                            if (take) {
+                                const int o = base + __popc(m & ((1u << lane) - 1u));
+                                const uint32_t gid = (uint32_t)(slice0 + li);
+                                if (o < cap) cand0[o] = ((unsigned long long)key << 32) | (0xffffffffu - gid);
+                            }
+                        }
+                    }
+                }
+                cluster.sync();  // ---- survivors gathered
+                use_threshold = remote_xs(0)->ncand <= cap;
+                if (!use_threshold && timing) dbg_add(DBG_TOPK_FALLBACK, 1);
+            }
+            if (!use_threshold) {
+                // 4-pass cluster radix select of the k-th key, then exact gather
+                uint32_t prefix = 0, pmask = 0;
+                int krem = k;
+                for (int pass = 0; pass < 4; pass++) {
+                    const int shift = 24 - 8 * pass;
+                    unsigned *h = sh.xs.hist[pass & 1];
+                    for (int i = tid; i < 256; i += NT) h[i] = 0;
+                    __syncthreads();
+                    for (int j = 0; j < LT; j++) {
+                        const int li = cbase + j;
+                        int d = -1;
+                        if (li < slen) {
+                            const uint32_t key = key_of(vals[li]);
+                            if ((key & pmask) == prefix) d = (int)((key >> shift) & 255u);
+                        }
+                        const unsigned peers = __match_any_sync(0xffffffffu, d);
+                        if (d >= 0 && lane == __ffs(peers) - 1) atomicAdd(&h[d], (unsigned)__popc(peers));
+                    }
+                    __syncthreads();
+                    cluster.sync();  // ---- radix pass
+                    if (wid == 0) {
+                        unsigned cntb[8];
+#pragma unroll
+                        for (int b = 0; b < 8; b++) cntb[b] = 0;
+                        for (int rr = 0; rr < C; rr++) {
+                            const unsigned *hr = remote_xs(rr)->hist[pass & 1];
+#pragma unroll
+                            for (int b = 0; b < 8; b++) cntb[b] += hr[lane * 8 + b];
+                        }
+                        unsigned mysum = 0;
+#pragma unroll
+                        for (int b = 0; b < 8; b++) mysum += cntb[b];
+                        unsigned x = mysum;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            unsigned y = __shfl_down_sync(0xffffffffu, x, o);
+                            if (lane + o < 32) x += y;
+                        }
+                        const unsigned above = x - mysum;
+                        int sel = -1;
+                        unsigned gt = 0, acc = above;
+                        if (above < (unsigned)krem && x >= (unsigned)krem) {
+#pragma unroll
+                            for (int b = 7; b >= 0; b--) {
+                                if (sel < 0) {
+                                    if (acc + cntb[b] >= (unsigned)krem) {
+                                        sel = lane * 8 + b;
+                                        gt = acc;
+                                    } else {
+                                        acc += cntb[b];
+                                    }
+                                }
+                            }
+                        }
+                        const unsigned own = __ballot_sync(0xffffffffu, sel >= 0);
+                        const int src = own ? __ffs(own) - 1 : 0;
+                        sel = __shfl_sync(0xffffffffu, sel, src);
+                        gt = __shfl_sync(0xffffffffu, gt, src);
+                        if (lane == 0) {
+                            sh.bcast_i[0] = sel;
+                            sh.bcast_i[1] = (int)gt;
+                        }
+                    }
+                    __syncthreads();
+                    const int sel = sh.bcast_i[0];
+                    krem -= sh.bcast_i[1];
+                    prefix |= (uint32_t)max(sel, 0) << shift;
+                    pmask |= 255u << shift;
+                }
+                const uint32_t kstar = prefix;
+                const int ngt = k - krem;
+                int cgt = 0, ceq = 0;
+                for (int j = 0; j < LT; j++) {
+                    const int li = cbase + j;
+                    if (li < slen) {
+                        const uint32_t key = key_of(vals[li]);
+                        cgt += key > kstar;
+                        ceq += key == kstar;
+                    }
+                }
+                int egt, tgt, eeq, teq;
+                block_scan_i(cgt, sh.red_i, egt, tgt);
+                block_scan_i(ceq, sh.red_i2, eeq, teq);
+                if (tid == 0) {
+                    sh.xs.cnt_gt = tgt;
+                    sh.xs.cnt_eq = teq;
+                }
+                cluster.sync();  // ---- counts
+                int ogt = 0, oeq = 0;
+                for (int rr = 0; rr < rank; rr++) {
+                    Xch *x = remote_xs(rr);
+                    ogt += x->cnt_gt;
+                    oeq += x->cnt_eq;
+                }
+                unsigned long long *cand0 = cluster.map_shared_rank(cand, 0);
+                int pg = ogt + egt, pe = oeq + eeq;
+                for (int j = 0; j < LT; j++) {
+                    const int li = cbase + j;
+                    if (li < slen) {
+                        const uint32_t key = key_of(vals[li]);
+                        const uint32_t gid = (uint32_t)(slice0 + li);
+                        const unsigned long long comp = ((unsigned long long)key << 32) | (0xffffffffu - gid);
+                        if (key > kstar) {
+                            cand0[pg++] = comp;
+                        } else if (key == kstar) {
+                            if (pe < krem) cand0[ngt + pe] = comp;
+                            pe++;
+                        }
+                    }
+                }
+                if (tid == 0 && rank == 0) sh.xs.ncand = k;
+                cluster.sync();  // ---- candidates in CTA 0
+            }
+            if (a.probs) {
+                float *pr = a.probs + (int64_t)row * a.probs_stride + slice0;
+                for (int i = tid; i < slen; i += NT) pr[i] = 0.0f;
+            }
+            if (rank == 0) {
+                const int n = sh.xs.ncand;
+                int P = 1;
+                while (P < n) P <<= 1;
+                for (int i = n + tid; i < P; i += NT) cand[i] = 0ull;
+                __syncthreads();
+                // bitonic sort, descending on (key, ~id)
+                for (int size = 2; size <= P; size <<= 1) {
+                    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                        for (int i = tid; i < P; i += NT) {
+                            const int j = i ^ stride;
+                            if (j > i) {
+                                const bool desc = (i & size) == 0;
+                                const unsigned long long x = cand[i], y = cand[j];
+                                if (desc ? (x < y) : (x > y)) {
+                                    cand[i] = y;
+                                    cand[j] = x;
+                                }
+                            }
+                        }
+                        __syncthreads();
+                    }
+                }
+                float *tl = reinterpret_cast<float *>(cand + P);
+                int *il = reinterpret_cast<int *>(tl + k);
+                for (int i = tid; i < k; i += NT) {
+                    const unsigned long long c = cand[i];
+                    tl[i] = okey_inv((uint32_t)(c >> 32));
+                    il[i] = (int)(0xffffffffu - (uint32_t)(c & 0xffffffffu));
+                    if (a.topk_ids) a.topk_ids[(int64_t)row * a.topk_stride + i] = il[i] + a.vocab_offset;
+                }
+                __syncthreads();
+                if (wid == 0) {
+                    float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride : nullptr;
+                    token = sample_sorted_list(tl, il, k, p, r, pr);
+                }
+            }
+            }
+        } else {
+            // ---------------- index-order path -------------------------------------------------
+            const float inv_temp = __fdiv_rn(1.0f, p.temperature);
+            float mv;
+            if (inv_temp > 0.0f && inv_temp < INFINITY) {
+                mv = __fmul_rn(__fsub_rn(M, M), inv_temp);
+            } else {
+                float tm = -INFINITY;
+                for (int i = tid; i < slen; i += NT) tm = fmaxf(tm, __fmul_rn(__fsub_rn(vals[i], M), inv_temp));
+                tm = block_allreduce(tm, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+                if (tid == 0) sh.xs.mt = tm;
+                cluster.sync();  // ---- odd temperature
+                float tv = -INFINITY;
+                if (lane < C) tv = remote_xs(lane)->mt;
+                mv = warp_allreduce(tv, [](float x, float y) { return fmaxf(x, y); });
+            }
+            // P2: exponentials (in place), double sum with four accumulators
+            double ds;
+            {
+                float4 *v4 = reinterpret_cast<float4 *>(vals + cbase);
+                double acc[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    float4 x = v4[j];
+                    x.x = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
+                    x.y = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
+                    x.z = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
+                    x.w = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
+                    v4[j] = x;
+                    acc[j & 3] = acc[j & 3] + (((double)x.x + (double)x.y) + ((double)x.z + (double)x.w));
+                }
+                ds = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+            }
+            ds = block_allreduce(ds, sh.red_d, [](double x, double y) { return x + y; });
+            if (tid == 0) sh.xs.dsum = ds;
+            mark(DBG_P2);
+            cluster.sync();  // ---- #2
+            mark(DBG_W2);
+            double sum = 0.0;
+            if (lane == 0)
+                for (int rr = 0; rr < C; rr++) sum = sum + remote_xs(rr)->dsum;
+            sum = __shfl_sync(0xffffffffu, sum, 0);
+
+            Chain ch;
+            ch.inv_sum = __double2float_rn(1.0 / sum);
+            ch.min_p = p.min_p;
+            ch.minp = p.min_p > 0.0f;
+            ch.nokept = 0;
+            ch.inv_s2 = 1.0f;
+            ch.topp = p.top_p < 1.0f;
+            ch.inv_s3 = 1.0f;
+            ch.cut_idx = INT_MAX;
+
+            if (ch.minp) {
+                double s2 = 0.0, sall = 0.0;
+                int nk = 0;
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const float4 x = v4[j];
+                    const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const float pp = __fmul_rn(e4[c], ch.inv_sum);
+                        sall = sall + (double)pp;
+                        if (pp >= ch.min_p) {
+                            s2 = s2 + (double)pp;
+                            nk++;
+                        }
+                    }
+                }
+                s2 = block_allreduce(s2, sh.red_d, [](double x, double y) { return x + y; });
+                sall = block_allreduce(sall, sh.red_d, [](double x, double y) { return x + y; });
+                nk = block_allreduce(nk, sh.red_i, [](int x, int y) { return x + y; });
+                if (tid == 0) {
+                    sh.xs.s2 = s2;
+                    sh.xs.s2all = sall;
+                    sh.xs.nkept = nk;
+                }
+                cluster.sync();  // ---- min-p
+                double S2 = 0.0, SA = 0.0;
+                int NK = 0;
+                if (lane == 0) {
+                    for (int rr = 0; rr < C; rr++) {
+                        Xch *x = remote_xs(rr);
+                        S2 = S2 + x->s2;
+                        SA = SA + x->s2all;
+                        NK += x->nkept;
+                    }
+                }
+                S2 = __shfl_sync(0xffffffffu, S2, 0);
+                SA = __shfl_sync(0xffffffffu, SA, 0);
+                NK = __shfl_sync(0xffffffffu, NK, 0);
+                ch.nokept = NK == 0;
+                ch.inv_s2 = __double2float_rn(1.0 / (ch.nokept ? SA : S2));
+            }
+
+            // P3: sub-chunk / chunk sums of the list probabilities, cluster scan
+            double subs[4] = {0.0, 0.0, 0.0, 0.0};
+            int fmem = INT_MAX, lmem = -1;
+            float fw = 0.0f;
+            {
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+                if (ch.minp && !ch.nokept) {
+#pragma unroll
+                    for (int j = 0; j < NV; j++) {
+                        const float4 x = v4[j];
+                        const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const int el = 4 * j + c;
+                            const int li = cbase + el;
+                            const float w = w_of(ch, e4[c]);
+                            subs[el / SUB] = subs[el / SUB] + (double)w;
+                            if (li < slen && member_of(ch, e4[c])) {
+                                if (fmem == INT_MAX) {
+                                    fmem = slice0 + li;
+                                    fw = w;
+                                }
+                                lmem = slice0 + li;
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < NV; j++) {
+                        const float4 x = v4[j];
+                        const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int c = 0; c < 4; c++) {
+                            const int el = 4 * j + c;
+                            subs[el / SUB] = subs[el / SUB] + (double)w_of(ch, e4[c]);
+                        }
+                    }
+                    if (cbase < slen) {
+                        fmem = slice0 + cbase;
+                        fw = w_of(ch, vals[cbase]);
+                        lmem = slice0 + min(cbase + LT, slen) - 1;
+                    }
+                }
+            }
+            const double cs = (subs[0] + subs[1]) + (subs[2] + subs[3]);
+            double excl, incl, ctot;
+            block_scan_d(cs, sh.red_d, excl, incl, ctot);
+            const int bfm = block_allreduce(fmem, sh.red_i, [](int x, int y) { return min(x, y); });
+            const int blm = block_allreduce(lmem, sh.red_i2, [](int x, int y) { return max(x, y); });
+            if (fmem == bfm && fmem != INT_MAX) sh.xs.first_w = fw;
+            if (tid == 0) {
+                sh.xs.tot = ctot;
+                sh.xs.first_member = bfm;
+                sh.xs.last_member = blm;
+                sh.xs.cut_idx = -1;
+                sh.xs.nstash = 0;
+            }
+            mark(DBG_P3);
+            cluster.sync();  // ---- #3
+            mark(DBG_W3);
+            double off = 0.0, grand = 0.0;
+            int gfm = INT_MAX, glm = -1;
+            float gfw = 0.0f;
+            if (lane == 0) {
+                for (int rr = 0; rr < C; rr++) {
+                    Xch *x = remote_xs(rr);
+                    if (rr == rank) off = grand;
+                    grand = grand + x->tot;
+                    if (x->first_member < gfm) {
+                        gfm = x->first_member;
+                        gfw = x->first_w;
+                    }
+                    glm = max(glm, x->last_member);
+                }
+            }
+            off = __shfl_sync(0xffffffffu, off, 0);
+            grand = __shfl_sync(0xffffffffu, grand, 0);
+            gfm = __shfl_sync(0xffffffffu, gfm, 0);
+            gfw = __shfl_sync(0xffffffffu, gfw, 0);
+            glm = __shfl_sync(0xffffffffu, glm, 0);
+            const double P0 = off + excl, P1 = off + incl;
+
+            int last_idx = ch.minp && !ch.nokept ? glm : V - 1;
+            if (ch.topp) {
+                const float tp = p.top_p;
+                int cut = -1;
+                double s3 = grand;
+                if (!(tp > 0.0f)) {
+                    cut = gfm;
+                    s3 = (double)gfw;
+                } else {
+                    // the single chunk where (float)cumsum first reaches top_p; its warp finds the
+                    // cut element cooperatively
+                    const bool crosses = __double2float_rn(P1) >= tp && !(__double2float_rn(P0) >= tp);
+                    const unsigned cm = __ballot_sync(0xffffffffu, crosses);
+                    if (cm) {
+                        const int src = __ffs(cm) - 1;
+                        const double base = __shfl_sync(0xffffffffu, P0, src);
+                        const int cb0 = __shfl_sync(0xffffffffu, cbase, src);
+                        constexpr int SL = (LT + 31) / 32;
+                        const int j0 = lane * SL;
+                        double part = 0.0;
+                        float wv[SL];
+                        bool mem[SL];
+#pragma unroll
+                        for (int k = 0; k < SL; k++) {
+                            const int li = cb0 + j0 + k;
+                            const bool in = j0 + k < LT && li < slen;
+                            const float e = in ? vals[li] : 0.0f;
+                            mem[k] = in && member_of(ch, e);
+                            wv[k] = mem[k] ? w_of(ch, e) : 0.0f;
+                            part = part + (double)wv[k];
+                        }
+                        double x = part;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            double y = __shfl_up_sync(0xffffffffu, x, o);
+                            if (lane >= o) x = y + x;
+                        }
+                        const double ex = __shfl_up_sync(0xffffffffu, x, 1);
+                        double cum = lane == 0 ? base : base + ex;
+                        int hitk = -1, lastm = -1;
+                        double hitc = 0.0;
+#pragma unroll
+                        for (int k = 0; k < SL; k++) {
+                            if (mem[k] && hitk < 0) {
+                                cum = cum + (double)wv[k];
+                                lastm = k;
+                                if (__double2float_rn(cum) >= tp) {
+                                    hitk = k;
+                                    hitc = cum;
+                                }
+                            }
+                        }
+                        const unsigned hm = __ballot_sync(0xffffffffu, hitk >= 0);
+                        int ci;
+                        double cs3;
+                        if (hm) {
+                            const int hl = __ffs(hm) - 1;
+                            ci = __shfl_sync(0xffffffffu, cb0 + j0 + hitk, hl);
+                            cs3 = __shfl_sync(0xffffffffu, hitc, hl);
+                        } else {
+                            // rounding disagreed with the chunk sum: cut at the chunk's last member
+                            const unsigned lm2 = __ballot_sync(0xffffffffu, lastm >= 0);
+                            const int ll = lm2 ? 31 - __clz(lm2) : 0;
+                            ci = __shfl_sync(0xffffffffu, cb0 + j0 + lastm, ll);
+                            cs3 = base + __shfl_sync(0xffffffffu, x, 31);
+                        }
+                        if (lane == 0) {
+                            sh.xs.cut_idx = slice0 + ci;
+                            sh.xs.cut_s3 = cs3;
+                        }
+                    }
+                    cluster.sync();  // ---- #4
+                    if (lane == 0) {
+                        for (int rr = 0; rr < C; rr++) {
+                            Xch *x = remote_xs(rr);
+                            if (x->cut_idx >= 0 && cut < 0) {
+                                cut = x->cut_idx;
+                                s3 = x->cut_s3;
+                            }
+                        }
+                    }
+                    cut = __shfl_sync(0xffffffffu, cut, 0);
+                    s3 = __shfl_sync(0xffffffffu, s3, 0);
+                }
+                if (cut >= 0) {
+                    ch.cut_idx = cut;
+                    last_idx = cut;
+                }
+                ch.inv_s3 = __double2float_rn(1.0 / s3);
+            }
+            mark(DBG_CUT);
+
+            // P4: sub-chunk records (exact fp32 running-sum functions), chunk and warp records
+            {
+                const double inv3 = ch.topp ? (double)ch.inv_s3 : 1.0;
+                uint32_t gb[4];
+                bool pred[4];
+                {
+                    double pre = P0;
+#pragma unroll
+                    for (int s = 0; s < 4; s++) {
+                        const float A0 = __double2float_rn(pre * inv3);
+                        pre = pre + subs[s];
+                        const float A1 = __double2float_rn((s == 3 ? P1 : pre) * inv3);
+                        const uint32_t e0 = fbits(A0) >> 23, e1 = fbits(A1) >> 23;
+                        pred[s] = A0 > 0.0f && e0 == e1 && e0 >= 1u && e0 <= 253u;
+                        gb[s] = (pred[s] ? e0 : 127u) << 23;
+                    }
+                }
+                float g0[4], g1[4];
+                bool anyq[4] = {false, false, false, false};
+#pragma unroll
+                for (int s = 0; s < 4; s++) {
+                    g0[s] = bitsf(gb[s]);
+                    g1[s] = bitsf(gb[s] | 1u);
+                }
+                float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride + slice0 : nullptr;
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+#pragma unroll
+                for (int j = 0; j < NV; j++) {
+                    const float4 x = v4[j];
+                    const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        const int el = 4 * j + c;
+                        const int s = el / SUB;
+                        const int li = cbase + el;
+                        const float q = q_of(ch, e4[c], slice0 + li);
+                        anyq[s] |= q != 0.0f;
+                        g0[s] = __fadd_rn(g0[s], q);
+                        g1[s] = __fadd_rn(g1[s], q);
+                        if (pr && li < slen) pr[li] = q;
+                    }
+                }
+                // compose the four sub-chunks into the chunk record
+                int ctype = REC_IDENT, ce = 0;
+                uint32_t c0 = 0u, c1 = 0u;
+#pragma unroll
+                for (int s = 0; s < 4; s++) {
+                    if (!anyq[s]) continue;
+                    const uint32_t lim = gb[s] + (1u << 23);
+                    const bool ok = pred[s] && fbits(g0[s]) < lim && fbits(g1[s]) < lim;
+                    const int es = (int)(gb[s] >> 23);
+                    if (!ok || ctype == REC_MIXED || (ctype == REC_CLEAN && es != ce)) {
+                        ctype = REC_MIXED;
+                        continue;
+                    }
+                    const uint32_t m0 = fbits(g0[s]) - gb[s], m1 = fbits(g1[s]) - (gb[s] | 1u);
+                    if (ctype == REC_IDENT) {
+                        ctype = REC_CLEAN;
+                        ce = es;
+                        c0 = m0;
+                        c1 = m1;
+                    } else {
+                        const uint32_t x0 = c0, x1 = c1;
+                        c0 = x0 + ((x0 & 1u) ? m1 : m0);
+                        c1 = x1 + (((1u + x1) & 1u) ? m1 : m0);
+                    }
+                }
+                __syncthreads();  // the union area held the history table until now
+                rec_type[tid] = ctype;
+                rec_e[tid] = ce;
+                rec_n0[tid] = c0;
+                rec_n1[tid] = c1;
+                // warp record: prefix run, one boundary chunk, suffix run
+                const unsigned cleanm = __ballot_sync(0xffffffffu, ctype == REC_CLEAN);
+                const int e_first = cleanm ? __shfl_sync(0xffffffffu, ce, __ffs(cleanm) - 1) : 0;
+                const unsigned nonconf =
+                    __ballot_sync(0xffffffffu, ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_first));
+                WRec wr;
+                wr.slot = -1;
+                wr.pad[0] = wr.pad[1] = 0;
+                if (!nonconf) {
+                    uint32_t a0 = ctype == REC_CLEAN ? c0 : 0u, a1 = ctype == REC_CLEAN ? c1 : 0u;
+                    compose_scan(a0, a1);
+                    wr.type = cleanm ? REC_CLEAN : REC_IDENT;
+                    wr.e_pre = e_first;
+                    wr.p0 = __shfl_sync(0xffffffffu, a0, 31);
+                    wr.p1 = __shfl_sync(0xffffffffu, a1, 31);
+                    wr.bchunk = -1;
+                    wr.e_suf = 0;
+                    wr.s0 = wr.s1 = 0u;
+                    wr.sfrom = 32;
+                } else {
+                    const int j = __ffs(nonconf) - 1;
+                    uint32_t a0 = (lane < j && ctype == REC_CLEAN) ? c0 : 0u;
+                    uint32_t a1 = (lane < j && ctype == REC_CLEAN) ? c1 : 0u;
+                    compose_scan(a0, a1);
+                    const uint32_t p0 = __shfl_sync(0xffffffffu, a0, 31), p1 = __shfl_sync(0xffffffffu, a1, 31);
+                    const int tj = __shfl_sync(0xffffffffu, ctype, j);
+                    // the suffix starts after a MIXED boundary chunk, or at a CLEAN chunk j that
+                    // already lies in the next binade
+                    const int sfrom = tj == REC_MIXED ? j + 1 : j;
+                    const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom && ctype == REC_CLEAN);
+                    const int e_s = sclean ? __shfl_sync(0xffffffffu, ce, __ffs(sclean) - 1) : 0;
+                    const unsigned sbad = __ballot_sync(
+                        0xffffffffu, lane >= sfrom && (ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_s)));
+                    uint32_t b0 = (lane >= sfrom && ctype == REC_CLEAN) ? c0 : 0u;
+                    uint32_t b1 = (lane >= sfrom && ctype == REC_CLEAN) ? c1 : 0u;
+                    compose_scan(b0, b1);
+                    wr.type = sbad ? REC_MIXED : REC_PBS;
+                    wr.e_pre = e_first;
+                    wr.p0 = p0;
+                    wr.p1 = p1;
+                    wr.bchunk = tj == REC_MIXED ? j : -1;
+                    wr.e_suf = e_s;
+                    wr.s0 = __shfl_sync(0xffffffffu, b0, 31);
+                    wr.s1 = __shfl_sync(0xffffffffu, b1, 31);
+                    wr.sfrom = sfrom;
+                }
+                // boundary chunk probabilities -> a stash slot in CTA 0 (when one is free)
+                if (wr.type == REC_PBS && wr.bchunk >= 0) {
+                    int slot = -1;
+                    if (lane == 0) {
+                        slot = atomicAdd(&remote_xs(0)->nstash, 1);
+                        if (slot >= STASH_SLOTS) slot = -1;
+                    }
+                    slot = __shfl_sync(0xffffffffu, slot, 0);
+                    wr.slot = slot;
+                    if (slot >= 0) {
+                        float *qs = cluster.map_shared_rank(qstash, 0) + slot * LT;
+                        const int cb0 = (wid * 32 + wr.bchunk) * LT;
+                        for (int k = lane; k < LT; k += 32) qs[k] = q_of(ch, vals[cb0 + k], slice0 + cb0 + k);
+                    } else if (timing) {
+                        dbg_add(DBG_STASH_MISS, 1);
+                    }
+                }
+                if (lane == 0) {
+                    if (wr.type == REC_PBS && timing) dbg_add(DBG_PBS, 1);
+                    WRec *dst = cluster.map_shared_rank(wstash, 0) + rank * NW + wid;
+                    *dst = wr;
+                }
+            }
+            mark(DBG_P4);
+            cluster.sync();  // ---- #5 records visible to the walker
+            mark(DBG_W5);
+
+            if (rank == 0 && wid == 0) {
+                uint32_t cb = 0u;  // running sum, starts at +0.0f
+                int res = -1;
+                const int total_w = C * NW;
+                // chunk-level walk of warp record gw (chunk records read from their CTA), from
+                // chunk `from` on
+                auto walk_chunks = [&](int gw, int from, uint32_t &cbv) -> int {
+                    if (lane == 0) dbg_add(DBG_EXPAND, 1);
+                    const int rr = gw / NW, w = gw % NW;
+                    const int *rt = cluster.map_shared_rank(rec_type, rr);
+                    const int *re = cluster.map_shared_rank(rec_e, rr);
+                    const uint32_t *r0 = cluster.map_shared_rank(rec_n0, rr);
+                    const uint32_t *r1 = cluster.map_shared_rank(rec_n1, rr);
+                    const float *rv = cluster.map_shared_rank(vals, rr);
+                    const int t2 = rt[w * 32 + lane], e2 = re[w * 32 + lane];
+                    const uint32_t a2 = r0[w * 32 + lane], b2 = r1[w * 32 + lane];
+                    auto expandB = [&](int jj, uint32_t &cbx) -> int {
+                        const int lb = (w * 32 + jj) * LT;
+                        return replay_elems(LT, rr * S + lb, cbx, r,
+                                            [&](int k) { return q_of(ch, rv[lb + k], rr * S + lb + k); });
+                    };
+                    int pos2 = from, rs2 = -1;
+                    while (pos2 < 32 && rs2 == -1) rs2 = walk_step(32, pos2, t2, e2, a2, b2, cbv, r, expandB);
+                    return rs2;
+                };
+                for (int gw0 = 0; gw0 < total_w && res == -1; gw0 += 32) {
+                    const int n = min(32, total_w - gw0);
+                    WRec wl = {};
+                    wl.type = REC_IDENT;
+                    if (lane < n) wl = wstash[gw0 + lane];
+                    // a PBS record is applied in three pieces; whatever does not apply is walked
+                    // chunk by chunk
+                    auto expandA = [&](int j, uint32_t &cbv) -> int {
+                        const int gw = gw0 + j;
+                        const int ty = __shfl_sync(0xffffffffu, wl.type, j);
+                        if (ty == REC_PBS) {
+                            const int ep = __shfl_sync(0xffffffffu, wl.e_pre, j);
+                            const uint32_t p0 = __shfl_sync(0xffffffffu, wl.p0, j);
+                            const uint32_t p1 = __shfl_sync(0xffffffffu, wl.p1, j);
+                            const int bc = __shfl_sync(0xffffffffu, wl.bchunk, j);
+                            const int es = __shfl_sync(0xffffffffu, wl.e_suf, j);
+                            const uint32_t s0 = __shfl_sync(0xffffffffu, wl.s0, j);
+                            const uint32_t s1 = __shfl_sync(0xffffffffu, wl.s1, j);
+                            const int slot = __shfl_sync(0xffffffffu, wl.slot, j);
+                            const int sfrom = __shfl_sync(0xffffffffu, wl.sfrom, j);
+                            uint32_t c = cbv;
+                            if (apply_run(c, ep, p0, p1) && !(r < bitsf(c))) {
+                                if (bc >= 0) {
+                                    const int rr = gw / NW, w = gw % NW;
+                                    const int lb = (w * 32 + bc) * LT;
+                                    int found;
+                                    if (slot >= 0) {
+                                        const float *qs = qstash + slot * LT;
+                                        found = replay_elems(LT, rr * S + lb, c, r, [&](int k) { return qs[k]; });
+                                    } else {
+                                        const float *rv = cluster.map_shared_rank(vals, rr);
+                                        found = replay_elems(LT, rr * S + lb, c, r,
+                                                             [&](int k) { return q_of(ch, rv[lb + k], rr * S + lb + k); });
+                                    }
+                                    if (found != -1) return found;
+                                }
+                                uint32_t c2 = c;
+                                if (apply_run(c2, es, s0, s1) && !(r < bitsf(c2))) {
+                                    cbv = c2;
+                                    return -1;
+                                }
+                                cbv = c;
+                                return walk_chunks(gw, sfrom, cbv);
+                            }
+                        }
+                        return walk_chunks(gw, 0, cbv);
+                    };
+                    const int ty = wl.type == REC_PBS ? REC_MIXED : wl.type;
+                    int pos = 0;
+                    while (pos < n && res == -1) res = walk_step(n, pos, ty, wl.e_pre, wl.p0, wl.p1, cb, r, expandA);
+                }
+                if (res == -2) rowflags |= ROW_ERR_WALK;
+                token = res >= 0 ? res : last_idx;
+            }
+            mark(DBG_WALK);
+        }
+
+    row_done:
+        if (rank == 0 && tid == 0) {
+            if (token < 0) token = 0;
+            a.token[row] = token + a.vocab_offset;
+            if (a.status) a.status[row] = rowflags;
+        }
+        mark(DBG_TOPK);
+        fence_proxy_async();  // order this row's generic accesses of the slice before the next bulk copy
+        cluster.sync();       // ---- end of row: peers may reuse their shared memory
+        mark(DBG_WEND);
+    }
+}
+
+}  // namespace
+}  // namespace dllm

@@ -1,0 +1,141 @@
+/*
+ * diskllm_cuda.h -- C ABI of libdiskllm_cuda.so, the B200 (sm_100a) sampler for DiskLLM.
+ *
+ * Two layers:
+ *   1. Drop-in replacements for DiskLLM's sampler.h (include/sampler.h:7-34 in DiskLLM),
+ *      declared in this repo's include/sampler.h with identical names and signatures.
+ *      Linking libdiskllm_cuda.so instead of compiling src/sampler.c keeps
+ *      src/core/sampler_api.c and every caller unchanged.
+ *   2. A batched, device-resident entry point (dllm_cuda_sample_batch) that runs the whole
+ *      per-row chain of src/core/sampler_api.c:48-63 -- grammar mask, presence,
+ *      frequency, repetition, sampler_sample -- for many rows in one launch.
+ *
+ * Every pointer in dllm_batch_desc is a device pointer unless stated otherwise.  The
+ * caller owns all buffers.  Streams are passed as void* (a cudaStream_t).
+ */
+#ifndef DISKLLM_CUDA_H
+#define DISKLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifndef DLLM_API
+#if defined(__GNUC__)
+#define DLLM_API __attribute__((visibility("default")))
+#else
+#define DLLM_API
+#endif
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    DLLM_OK = 0,
+    DLLM_ERR_INVALID_ARG = 1,
+    DLLM_ERR_OOM = 2,
+    DLLM_ERR_CUDA = 3,
+    DLLM_ERR_NCCL = 4,
+    DLLM_ERR_TIMEOUT = 5,
+    DLLM_ERR_UNSUPPORTED = 6,
+} dllm_status;
+
+enum {
+    DLLM_DTYPE_F32 = 0,
+    DLLM_DTYPE_BF16 = 1,
+};
+
+/* mode flags */
+#define DLLM_MODE_TOPP_SORTED   0x1u  /* reserved: sorted-nucleus top-p when top-k is off
+                                         (not yet implemented; rejected) */
+#define DLLM_MODE_PEN_TRUE_DIV  0x2u  /* positive logits divided by the repetition penalty
+                                         (IEEE) instead of multiplied by 1/penalty, which is
+                                         what the reference's -ffast-math build computes */
+
+/* Sampling parameters of one row.  Fields mirror DiskLLM's sampler_config
+ * (include/sampler.h:10-16) plus the penalties of diskllm_sampler_params
+ * (include/diskllm.h:48-56) and the frequency extension. */
+typedef struct {
+    float temperature;   /* 0 -> greedy (src/sampler.c:140-142) */
+    float top_p;         /* >= 1 -> off */
+    float min_p;         /* <= 0 -> off; absolute threshold as in src/sampler.c:188-202 */
+    int   top_k;         /* <= 0 or >= vocab -> off */
+    float repetition;    /* <= 1 -> off (src/sampler.c:21-33, src/core/sampler_api.c:59) */
+    float presence;      /* 0 -> off (src/sampler.c:35-52, src/core/sampler_api.c:55) */
+    float frequency;     /* 0 -> off; not in the reference: x -= (float)count * frequency,
+                            applied after presence, before repetition */
+} dllm_sampler_params;
+
+typedef struct {
+    int rows;                 /* batch rows */
+    int vocab;                /* columns of logits (= vocabulary) */
+    int64_t row_stride;       /* elements between consecutive rows (>= vocab) */
+    int dtype;                /* DLLM_DTYPE_F32 or DLLM_DTYPE_BF16 (upcast exactly) */
+    const void *logits;       /* [rows][row_stride] */
+
+    const uint32_t *mask;     /* grammar allow-mask or NULL: bit (i & 31) of word (i >> 5)
+                                 set = token i allowed; cleared -> -INFINITY, the effect of
+                                 diskllm_grammar_apply_mask (src/core/grammar.c:275-308) */
+    int64_t mask_stride;      /* words between rows (>= (vocab + 31) / 32) */
+
+    const int32_t *hist_ids;  /* token history, CSR; NULL = none */
+    const int64_t *hist_off;  /* [rows + 1] offsets into hist_ids */
+    int hist_max;             /* upper bound on any row's history length (host value) */
+
+    const float *uniforms;    /* [rows] draws in [0, 1), one per row */
+
+    dllm_sampler_params params;            /* host value, used for every row ... */
+    const dllm_sampler_params *row_params; /* ... unless this device array is given */
+    int topk_max;             /* upper bound on top_k over rows when row_params is given */
+
+    unsigned flags;           /* DLLM_MODE_* */
+
+    int32_t *token;           /* [rows] out: sampled token id */
+    float *probs;             /* optional [rows][probs_stride] out: final draw probability
+                                 of every token (0 outside the draw list) */
+    int64_t probs_stride;
+    float *pen_logits;        /* optional [rows][pen_stride] out: logits after mask and
+                                 penalties (what the reference leaves in its logits array) */
+    int64_t pen_stride;
+    int32_t *status;          /* optional [rows] out: 0 or DLLM_ROW_ERR_* bits */
+    int32_t *topk_ids;        /* optional [rows][topk_stride] out: the top-k ids, best first
+                                 (rows where top-k is active) */
+    int64_t topk_stride;
+} dllm_batch_desc;
+
+/* per-row status bits */
+#define DLLM_ROW_ERR_HIST_TABLE 1   /* more distinct history ids than the table holds */
+#define DLLM_ROW_ERR_NONFINITE  2   /* +inf / NaN row maximum (unsupported input) */
+#define DLLM_ROW_ERR_TOPK_LARGE 4   /* top_k above the kernel's candidate capacity */
+#define DLLM_ROW_ERR_WALK       8   /* internal consistency check of the draw failed */
+#define DLLM_ROW_ERR_TIMEOUT   16   /* a bounded wait on a bulk copy expired */
+
+/* Samples every row of the batch on `stream` (stream-ordered; returns after the launch).
+ * Replaces, per row, the sequence of src/core/sampler_api.c:48-63:
+ *   diskllm_grammar_apply_mask -> sampler_apply_presence_penalty ->
+ *   sampler_apply_repetition_penalty -> sampler_sample.
+ * Row i draws with uniforms[i] where the reference draws rand_f32 (src/sampler.c:225). */
+DLLM_API dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *desc, void *stream);
+
+/* Diagnostics: when given a device array of 32 zeroed unsigned 64-bit counters, the sampler
+ * kernels accumulate per-phase cycle counts of each cluster's first CTA and draw-walk
+ * statistics into it; NULL switches it off.  No effect on results. */
+DLLM_API dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters);
+
+/* Version and build information ("diskllm_cuda <ver> sm_100a"). */
+DLLM_API const char *dllm_cuda_version(void);
+
+/* Last CUDA error string recorded by the library on this thread (or ""). */
+DLLM_API const char *dllm_cuda_last_error(void);
+
+/* Draw state of a drop-in sampler (the xorshift64 state of src/sampler.c:63), so that a
+ * resumed stream reproduces its ids. */
+struct sampler;
+DLLM_API uint64_t dllm_sampler_get_rng_state(const struct sampler *s);
+DLLM_API void     dllm_sampler_set_rng_state(struct sampler *s, uint64_t state);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DISKLLM_CUDA_H */

@@ -1,0 +1,257 @@
+"""Parity of the CUDA sampler (through the C ABI) with the restated oracle, which is itself
+pinned bit-for-bit to DiskLLM's compiled sampler.c (test_oracle_vs_reference.py).
+
+Bars:
+  * penalised / masked logits: bit-exact
+  * top-k id lists: bit-exact
+  * probabilities: within 1e-6 absolute
+  * sampled ids: identical, except where the uniform lies within 1e-6 of a CDF boundary
+"""
+import zlib
+
+import numpy as np
+import pytest
+
+import oracle as O
+from util import TOL_PROB, csr, dense_probs, ids_match, pack_mask, u24
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def gpu_run(lg, params, u, mask=None, hist=None, flags=0, dtype="f32"):
+    from diskllm_b200 import capi
+
+    dev = "cuda"
+    rows, V = lg.shape
+    x = torch.from_numpy(lg).to(dev)
+    if dtype == "bf16":
+        x = x.to(torch.bfloat16)
+    ut = torch.from_numpy(np.ascontiguousarray(u, np.float32)).to(dev)
+    kw = {}
+    if mask is not None:
+        kw["mask"] = torch.from_numpy(mask.view(np.int32)).to(dev)
+    if hist is not None:
+        ids, off = csr(hist)
+        kw["hist_ids"] = torch.from_numpy(ids).to(dev)
+        kw["hist_off"] = torch.from_numpy(off).to(dev)
+    probs = torch.full((rows, V), -1.0, device=dev)
+    pen = torch.empty((rows, V), device=dev)
+    status = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+    tk = None
+    k = params.get("top_k", 0)
+    if 0 < k < V:
+        tk = torch.full((rows, k), -1, dtype=torch.int32, device=dev)
+    tok = capi.sample_batch(x, ut, params, flags=flags, probs=probs, pen_logits=pen,
+                            status=status, topk_ids=tk, **kw)
+    torch.cuda.synchronize()
+    return (tok.cpu().numpy(), probs.cpu().numpy(), pen.cpu().numpy(), status.cpu().numpy(),
+            None if tk is None else tk.cpu().numpy())
+
+
+def _any_allowed(mrow, V):
+    bits = np.unpackbits(mrow.view(np.uint8), bitorder="little")[:V]
+    return bits.any()
+
+
+def check(lg, params, u, mask=None, hist=None, flags=0, dtype="f32", check_probs=True):
+    rows, V = lg.shape
+    ref_lg = lg
+    if dtype == "bf16":
+        ref_lg = torch.from_numpy(lg).to(torch.bfloat16).float().numpy()
+    tok, probs, pen, status, tk = gpu_run(lg, params, u, mask, hist, flags, dtype)
+    k = params.get("top_k", 0)
+    ora = O.sample_restated(ref_lg, params, u, mask=mask, hist=hist, flags=flags, want_pen=True,
+                            kept_cap=V, topk_cap=k if 0 < k < V else 1)
+    assert np.all(status == 0), status
+    assert np.array_equal(pen.view(np.uint32), ora.pen_logits.view(np.uint32))
+    bad = [i for i in range(rows) if not ids_match(int(tok[i]), ora, u, i)]
+    assert not bad, f"id mismatch rows {bad[:8]}: gpu {tok[bad[:8]]} oracle {ora.token[bad[:8]]}"
+    if params.get("temperature", 1.0) == 0.0:
+        return tok, ora
+    if tk is not None:
+        for i in range(rows):
+            assert np.array_equal(tk[i], ora.topk_idx[i, :k]), i
+    if check_probs:
+        for i in range(rows):
+            if ref_lg[i].max() == -np.inf or (mask is not None and not _any_allowed(mask[i], V)):
+                continue
+            g, o = probs[i].astype(np.float64), dense_probs(ora, i, V).astype(np.float64)
+            assert np.array_equal(np.isnan(g), np.isnan(o)), i
+            d = np.abs(np.nan_to_num(g) - np.nan_to_num(o))
+            assert d.max() <= TOL_PROB, (i, d.max(), int(d.argmax()))
+    return tok, ora
+
+
+PARAM_SETS = {
+    "cfg1": dict(temperature=0.8, top_k=40, top_p=0.95, repetition=1.1),
+    "cfg2": dict(temperature=0.7, top_k=50, top_p=0.9, repetition=1.1, frequency=0.3, presence=0.2),
+    "cfg3": dict(temperature=1.0, top_k=0, top_p=0.95),
+    "cfg4": dict(temperature=1.0, top_k=0, top_p=0.99, repetition=1.05),
+    "cfg5": dict(temperature=0.9, top_k=64, top_p=0.9, repetition=1.1),
+    "greedy": dict(temperature=0.0, repetition=1.3, presence=-0.5),
+    "server": dict(temperature=0.7, top_k=40, top_p=0.9, min_p=0.05, repetition=1.1),
+    "minp_only": dict(temperature=1.3, top_k=0, top_p=1.0, min_p=1e-5),
+    "minp_topp": dict(temperature=0.8, top_k=0, top_p=0.7, min_p=2e-5),
+    "plain": dict(temperature=1.0, top_k=0, top_p=1.0),
+    "topp_tiny": dict(temperature=1.0, top_k=0, top_p=0.02),
+    "topp_zero": dict(temperature=1.0, top_k=0, top_p=0.0),
+    "k3": dict(temperature=0.5, top_k=3, top_p=1.0),
+    "k_big": dict(temperature=1.1, top_k=700, top_p=0.97),
+    "k_ge_V": dict(temperature=2.0, top_k=10 ** 7, top_p=0.5),
+    "hot": dict(temperature=3.0, top_k=0, top_p=0.999, presence=0.4, frequency=0.1),
+}
+
+
+@pytest.mark.parametrize("V", [1000, 4099, 32000])
+@pytest.mark.parametrize("name", list(PARAM_SETS))
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_parity_random_rows(V, name, with_mask):
+    p = PARAM_SETS[name]
+    if p.get("top_k", 0) > V and name != "k_ge_V":
+        pytest.skip("k > V")
+    rng = np.random.default_rng(zlib.crc32(f"{V}-{name}-{with_mask}".encode()))
+    rows = 12
+    sigma = {1000: 2.5, 4099: 0.5, 32000: 3.0}[V]
+    lg = (rng.standard_normal((rows, V)) * sigma).astype(np.float32)
+    hist = [np.concatenate([rng.integers(0, V, 64), rng.integers(0, 20, 40), [-3, V + 7]])
+            for _ in range(rows)]
+    mask = None
+    if with_mask:
+        allow = rng.random((rows, V)) < 0.3
+        allow[0, :] = False                # fully masked row
+        allow[1, :] = False
+        allow[1, V // 3] = True            # exactly one allowed id
+        mask = pack_mask(allow)
+    u = u24(rng, rows)
+    tok, ora = check(lg, p, u, mask=mask, hist=hist)
+    # a single allowed token is returned, except when top_p <= 0 cuts the index-order list
+    # at its first entry (token 0), which is what the reference does too
+    if with_mask and p.get("temperature", 1.0) != 0.0 and p.get("top_p", 1.0) > 0.0:
+        assert tok[1] == V // 3
+
+
+@pytest.mark.parametrize("name", ["cfg3", "cfg4", "plain", "server", "cfg1"])
+def test_parity_degenerate_rows(name):
+    V = 5003
+    rng = np.random.default_rng(5)
+    rows = [np.zeros(V, np.float32)]                                       # all ties (linear drift)
+    r = np.full(V, -5.0, np.float32); r[300] = 40.0; rows.append(r)        # p ~ 1 spike
+    rows.append(np.linspace(-3, 3, V).astype(np.float32))                  # ramp
+    r = rng.standard_normal(V).astype(np.float32); r[1::2] = r[:-1:2]; rows.append(r)  # ties
+    rows.append((rng.standard_normal(V) * 30).astype(np.float32))          # very peaked
+    rows.append(np.full(V, 1e-30, np.float32))                              # tiny values
+    lg = np.stack(rows)
+    for seed in range(4):
+        u = u24(np.random.default_rng(seed), len(rows))
+        check(lg, PARAM_SETS[name], u)
+
+
+def test_parity_uniform_extremes():
+    V = 2048
+    rng = np.random.default_rng(9)
+    lg = (rng.standard_normal((6, V)) * 0.5).astype(np.float32)
+    u = np.array([0.0, 2.0 ** -24, 0.5, 1.0 - 2.0 ** -24, 0.999999, 0.25], np.float32)
+    for name in ("cfg4", "plain", "cfg1", "minp_topp"):
+        check(lg, PARAM_SETS[name], u)
+
+
+@pytest.mark.parametrize("name", ["cfg5", "cfg3", "greedy"])
+def test_parity_bf16(name):
+    V = 32768
+    rng = np.random.default_rng(21)
+    lg = (rng.standard_normal((8, V)) * 2).astype(np.float32)
+    hist = [rng.integers(0, V, 128) for _ in range(8)]
+    allow = rng.random((8, V)) < 0.1
+    u = u24(rng, 8)
+    check(lg, PARAM_SETS[name], u, mask=pack_mask(allow), hist=hist, dtype="bf16")
+
+
+def test_true_division_mode():
+    from diskllm_b200 import capi
+
+    V = 4000
+    rng = np.random.default_rng(4)
+    lg = (rng.standard_normal((6, V)) * 4).astype(np.float32)
+    hist = [rng.integers(0, V, 300) for _ in range(6)]
+    u = u24(rng, 6)
+    p = dict(temperature=0.9, top_k=20, top_p=0.9, repetition=1.1, presence=0.3)
+    tok, probs, pen, status, tk = gpu_run(lg, p, u, hist=hist, flags=capi.MODE_PEN_TRUE_DIV)
+    ora = O.sample_restated(lg, p, u, hist=hist, want_pen=True, flags=O.PEN_TRUE_DIV)
+    assert np.array_equal(pen.view(np.uint32), ora.pen_logits.view(np.uint32))
+
+
+@pytest.mark.parametrize("cfg", [2, 3, 4])
+def test_config_shaped_rows(cfg):
+    """full vocabulary of the benchmark configurations on a few rows"""
+    from diskllm_b200 import workloads as W
+
+    w = W.CONFIGS[cfg](device="cuda", rows=8)
+    lg = w.logits.float().cpu().numpy()
+    mask = None if w.mask is None else w.mask.cpu().numpy().view(np.uint32)
+    u = w.uniforms.cpu().numpy()
+    check(lg, w.params, u, mask=mask, hist=W.hist_lists(w))
+
+
+def test_full_config4_batch_properties():
+    """config 4 at full size: deterministic, statuses clean, and a sample of rows against the
+    oracle."""
+    from diskllm_b200 import capi
+    from diskllm_b200 import workloads as W
+
+    w = W.config4(device="cuda")
+    st = torch.full((w.rows,), -1, dtype=torch.int32, device="cuda")
+    t1 = capi.sample_batch(w.logits, w.uniforms, w.params, hist_ids=w.hist_ids,
+                           hist_off=w.hist_off, hist_max=w.hist_max, status=st)
+    t2 = capi.sample_batch(w.logits, w.uniforms, w.params, hist_ids=w.hist_ids,
+                           hist_off=w.hist_off, hist_max=w.hist_max)
+    torch.cuda.synchronize()
+    assert torch.equal(t1, t2)
+    assert int(st.abs().sum()) == 0
+    sel = list(range(0, w.rows, 64))
+    lg = w.logits[sel].cpu().numpy()
+    hist = [W.hist_lists(w)[i] for i in sel]
+    u = w.uniforms.cpu().numpy()[sel]
+    ora = O.sample_restated(lg, w.params, u, hist=hist, kept_cap=w.vocab)
+    tok = t1.cpu().numpy()[sel]
+    for i in range(len(sel)):
+        assert ids_match(int(tok[i]), ora, u, i), (sel[i], tok[i], ora.token[i])
+
+
+def test_drop_in_sampler_matches_reference_stream():
+    """sampler_create / sampler_sample through the C ABI against the oracle driven by the same
+    xorshift64 stream (seeded like src/sampler.c:83-89)."""
+    from diskllm_b200 import capi
+
+    rng = np.random.default_rng(12)
+    V = 20000
+    s = capi.Sampler(temperature=0.8, top_k=40, top_p=0.95, seed=1234)
+    us = O.xorshift_uniforms(1234, 20)
+    for i in range(20):
+        row = (rng.standard_normal(V) * 2.5).astype(np.float32)
+        tok = s.sample(row)
+        ora = O.sample_restated(row[None], dict(temperature=0.8, top_k=40, top_p=0.95),
+                                us[i:i + 1], kept_cap=40)
+        assert ids_match(tok, ora, us[i:i + 1], 0)
+    g = capi.Sampler(temperature=0.0, seed=5)      # greedy does not advance the stream
+    st0 = g.rng_state
+    row = rng.standard_normal(V).astype(np.float32)
+    assert g.sample(row) == int(np.argmax(row))
+    assert g.rng_state == st0
+    assert capi.greedy_sample(row) == int(np.argmax(row))
+
+
+def test_drop_in_penalties_in_place():
+    from diskllm_b200 import capi
+
+    rng = np.random.default_rng(13)
+    V = 5000
+    row = (rng.standard_normal(V) * 3).astype(np.float32)
+    seen = np.concatenate([rng.integers(0, V, 200), [-1, V, V + 5], rng.integers(0, 10, 50)])
+    a = row.copy()
+    capi.apply_presence_penalty(a, seen, 0.25)
+    capi.apply_repetition_penalty(a, seen, 1.15)
+    ora = O.sample_restated(row[None], dict(temperature=0.0, presence=0.25, repetition=1.15),
+                            np.zeros(1, np.float32), hist=[seen], want_pen=True)
+    assert np.array_equal(a.view(np.uint32), ora.pen_logits[0].view(np.uint32))

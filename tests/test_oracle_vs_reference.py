@@ -1,0 +1,127 @@
+"""Pins the restated oracle (oracle/dllm_oracle.c) to DiskLLM's own sampler.c, compiled with
+its Makefile:10 flags (oracle/_ref/libref_asbuilt.so), on identical rows and uniforms:
+penalised logits bit-exact, sampled ids identical, and the full fp32 CDF recovered from the
+reference by bisection on the uniform identical bit for bit."""
+import numpy as np
+import pytest
+
+import oracle as O
+from util import u24
+
+PARAM_SETS = [
+    dict(temperature=0.8, top_k=40, top_p=0.95, repetition=1.1),                      # cfg1
+    dict(temperature=0.7, top_k=50, top_p=0.9, repetition=1.1, presence=0.2),         # cfg2 (no freq)
+    dict(temperature=1.0, top_k=0, top_p=0.95),                                       # cfg3
+    dict(temperature=1.0, top_k=0, top_p=0.99, repetition=1.05),                     # cfg4
+    dict(temperature=0.9, top_k=64, top_p=0.9, repetition=1.1),                       # cfg5
+    dict(temperature=0.0, repetition=1.3, presence=-0.5),                             # greedy
+    dict(temperature=0.7, top_k=40, top_p=0.9, min_p=0.05),                           # server default
+    dict(temperature=1.3, top_k=0, top_p=1.0, min_p=1e-4),
+    dict(temperature=0.5, top_k=3, top_p=1.0),
+    dict(temperature=1.0, top_k=0, top_p=0.02),
+    dict(temperature=1.0, top_k=0, top_p=0.0),
+    dict(temperature=2.0, top_k=999999, top_p=0.5),
+]
+
+
+def _case(rng, rows, V, sigma, with_mask, hlen):
+    lg = (rng.standard_normal((rows, V)) * sigma).astype(np.float32)
+    hist = [np.concatenate([rng.integers(0, V, hlen), [-3, V + 7]]) for _ in range(rows)]
+    mask = None
+    if with_mask:
+        mask = rng.integers(0, 2 ** 32, (rows, (V + 31) // 32), dtype=np.uint64).astype(np.uint32)
+    return lg, hist, mask
+
+
+@pytest.mark.parametrize("V,sigma", [(1, 1.0), (5, 2.0), (1000, 2.5), (4099, 0.5), (32000, 3.0)])
+@pytest.mark.parametrize("pi", range(len(PARAM_SETS)))
+@pytest.mark.parametrize("with_mask", [False, True])
+def test_restated_matches_reference(have_reference, V, sigma, pi, with_mask):
+    rng = np.random.default_rng(V * 131 + pi * 7 + with_mask)
+    rows = 24
+    lg, hist, mask = _case(rng, rows, V, sigma, with_mask, 48)
+    u = u24(rng, rows)
+    p = PARAM_SETS[pi]
+    a = O.sample_restated(lg, p, u, mask=mask, hist=hist, want_pen=True)
+    b, _ = O.sample_reference(lg, p, u, mask=mask, hist=hist, want_pen=True)
+    assert np.array_equal(a.pen_logits.view(np.uint32), b.pen_logits.view(np.uint32))
+    assert np.array_equal(a.token, b.token)
+
+
+def test_edge_rows_match_reference(have_reference):
+    rng = np.random.default_rng(7)
+    V = 777
+    rows = [np.zeros(V, np.float32)]                                         # all ties
+    r = np.full(V, -5.0, np.float32); r[300] = 40.0; rows.append(r)          # p ~ 1 spike
+    rows.append(np.linspace(-3, 3, V).astype(np.float32))                    # ramp
+    r = rng.standard_normal(V).astype(np.float32); r[1::2] = r[:-1:2]; rows.append(r)  # ties
+    lg = np.stack(rows)
+    for p in PARAM_SETS:
+        u = u24(rng, len(rows))
+        a = O.sample_restated(lg, p, u)
+        b, _ = O.sample_reference(lg, p, u)
+        assert np.array_equal(a.token, b.token), p
+
+
+@pytest.mark.parametrize("topk", [0, 7])
+def test_fully_masked_and_single_allowed(have_reference, topk):
+    rng = np.random.default_rng(3)
+    V = 300
+    lg = rng.standard_normal((3, V)).astype(np.float32)
+    m = np.zeros((3, (V + 31) // 32), np.uint32)
+    m[1, 5] = 1 << 3          # exactly token 163 allowed
+    m[2, :] = 0xFFFFFFFF
+    for p in (dict(temperature=1.0, top_k=topk, top_p=0.95),
+              dict(temperature=1.0, top_k=topk, top_p=0.95, min_p=0.05),
+              dict(temperature=0.0)):
+        u = u24(rng, 3)
+        a = O.sample_restated(lg, p, u, mask=m)
+        b, _ = O.sample_reference(lg, p, u, mask=m)
+        assert np.array_equal(a.token, b.token), p
+        if p["temperature"] != 0.0:
+            assert a.token[1] == 163
+
+
+def test_strict_build_true_division(have_reference):
+    rng = np.random.default_rng(11)
+    V = 2000
+    lg = (rng.standard_normal((8, V)) * 4).astype(np.float32)
+    hist = [rng.integers(0, V, 300) for _ in range(8)]
+    p = dict(temperature=0.9, top_k=20, top_p=0.9, repetition=1.1, presence=0.3)
+    u = u24(rng, 8)
+    a = O.sample_restated(lg, p, u, hist=hist, want_pen=True, flags=O.PEN_TRUE_DIV, ftz=False)
+    b, _ = O.sample_reference(lg, p, u, hist=hist, want_pen=True, strict=True)
+    assert np.array_equal(a.pen_logits.view(np.uint32), b.pen_logits.view(np.uint32))
+    c = O.sample_restated(lg, p, u, hist=hist, want_pen=True)
+    assert not np.array_equal(a.pen_logits, c.pen_logits)
+
+
+@pytest.mark.parametrize("V,p", [
+    (300, dict(temperature=0.8, top_k=30, top_p=0.95, repetition=1.1)),
+    (150, dict(temperature=1.0, top_k=0, top_p=0.9)),
+    (150, dict(temperature=0.7, top_k=0, top_p=1.0, min_p=0.001)),
+    (9, dict(temperature=1.0, top_k=0, top_p=1.0)),
+])
+def test_cdf_recovered_from_reference_is_bit_identical(have_reference, V, p):
+    rng = np.random.default_rng(V)
+    lg = (rng.standard_normal((1, V)) * 2).astype(np.float32)
+    h = rng.integers(0, V, 20)
+    ids, cdf = O.reference_cdf(lg[0], p, hist_row=h)
+    o = O.sample_restated(lg, p, np.zeros(1, np.float32), hist=[h], kept_cap=V)
+    n = int(o.kept_n[0])
+    oid, ocdf, opr = o.kept_idx[0, :n], o.kept_cdf[0, :n].astype(np.float64), o.kept_prob[0, :n]
+    keep = (opr > 0) & np.concatenate([[True], np.diff(ocdf) > 0])
+    oid, ocdf = oid[keep], ocdf[keep]
+    m = min(len(ids), len(oid))
+    assert m >= 3
+    assert np.array_equal(ids[:m], oid[:m])
+    assert np.array_equal(cdf[:m - 1], ocdf[:m - 1])
+
+
+def test_xorshift_stream_matches_reference(have_reference):
+    """the drop-in sampler's uniforms: seed -> the reference's rand_f32 sequence"""
+    for seed in (0, 1, 42, 0x1234567890ABCDEF):
+        u = O.xorshift_uniforms(seed, 16)
+        for r in u:
+            assert O.reference_seed_for_uniform(float(r)) != 0
+        assert np.all((u >= 0) & (u < 1))
