@@ -3,7 +3,7 @@
     python -m diskllm_b200.build [--force]
 
 The library is self-contained (static CUDA runtime) so plain C callers can link it.  The
-fused kernel is compiled once per chunk length, in parallel.
+kernels are compiled once per sub-chunk length, in parallel.
 """
 from __future__ import annotations
 
@@ -18,9 +18,9 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiskllm_cuda.so")
 
-CHUNK_LENGTHS = [20, 36, 52, 68, 84, 100, 116, 132]
+SUB_LENGTHS = [4, 12, 20, 28, 36, 44, 52, 60]
 UNITS = [("dllm_launch.cu", []), ("dllm_capi.cu", [])] + [
-    ("dllm_kernel_inst.cu", [f"-DDLLM_LT={lt}"]) for lt in CHUNK_LENGTHS
+    ("dllm_kernel_inst.cu", [f"-DDLLM_SUB={s}"]) for s in SUB_LENGTHS
 ]
 SOURCES = sorted({u[0] for u in UNITS})
 HEADERS = ["dllm_internal.h", "dllm_kernel.cuh"]

@@ -32,7 +32,7 @@ ROW_ERR_TIMEOUT = 16
 # every symbol the public headers declare
 EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
-    "dllm_cuda_set_debug_counters",
+    "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes",
     "dllm_sampler_get_rng_state", "dllm_sampler_set_rng_state",
     "sampler_create", "sampler_free", "sampler_apply_repetition_penalty",
     "sampler_apply_presence_penalty", "sampler_sample", "greedy_sample",
@@ -93,6 +93,8 @@ class BatchDesc(C.Structure):
         ("status", C.c_void_p),
         ("topk_ids", C.c_void_p),
         ("topk_stride", C.c_int64),
+        ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
     ]
 
 
@@ -111,6 +113,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_sample_batch.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
     lib.dllm_cuda_set_debug_counters.restype = C.c_int
     lib.dllm_cuda_set_debug_counters.argtypes = [C.c_void_p]
+    lib.dllm_cuda_workspace_bytes.restype = C.c_size_t
+    lib.dllm_cuda_workspace_bytes.argtypes = [C.POINTER(BatchDesc)]
     lib.dllm_cuda_version.restype = C.c_char_p
     lib.dllm_cuda_last_error.restype = C.c_char_p
     lib.dllm_sampler_get_rng_state.restype = C.c_uint64
@@ -215,7 +219,7 @@ def apply_presence_penalty(logits: np.ndarray, seen, presence: float) -> None:
 
 def fill_desc(logits, uniforms, params=None, *, mask=None, hist_ids=None, hist_off=None,
               hist_max=None, row_params=None, topk_max=0, flags=0, token=None, probs=None,
-              pen_logits=None, status=None, topk_ids=None) -> tuple[BatchDesc, object]:
+              pen_logits=None, status=None, topk_ids=None, workspace=None) -> tuple[BatchDesc, object]:
     """Builds a dllm_batch_desc from CUDA tensors; returns (desc, token tensor)."""
     import torch
 
@@ -262,7 +266,15 @@ def fill_desc(logits, uniforms, params=None, *, mask=None, hist_ids=None, hist_o
         d.status = status.data_ptr()
     if topk_ids is not None:
         d.topk_ids, d.topk_stride = topk_ids.data_ptr(), topk_ids.stride(0)
+    if workspace is not None:
+        d.workspace, d.workspace_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     return d, token
+
+
+def workspace_bytes(logits, uniforms, params=None, **kw) -> int:
+    """dllm_cuda_workspace_bytes for the same arguments as sample_batch."""
+    d, _ = fill_desc(logits, uniforms, params, **kw)
+    return int(load_library().dllm_cuda_workspace_bytes(C.byref(d)))
 
 
 def sample_batch(logits, uniforms, params=None, *, stream=None, check=True, **kw):

@@ -78,9 +78,43 @@ static dllm_status get_config(int vocab, int dtype, int hist_max, int topk_max, 
 }
 
 // ----------------------------------------------------------------------------------------
+// library-managed workspace: one grow-only buffer per (device, stream)
+
+namespace {
+struct WsEntry {
+    int dev;
+    void *stream;
+    void *ptr;
+    size_t bytes;
+};
+std::mutex g_ws_mu;
+std::vector<WsEntry> g_ws;
+}  // namespace
+
+static void *internal_workspace(void *stream, size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    for (auto &w : g_ws) {
+        if (w.dev != dev || w.stream != stream) continue;
+        if (w.bytes >= bytes) return w.ptr;
+        cudaFree(w.ptr);  // waits for kernels still using the old buffer
+        w.ptr = nullptr;
+        w.bytes = 0;
+        if (cudaMalloc(&w.ptr, bytes) != cudaSuccess) return nullptr;
+        w.bytes = bytes;
+        return w.ptr;
+    }
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    g_ws.push_back({dev, stream, p, bytes});
+    return p;
+}
+
+// ----------------------------------------------------------------------------------------
 // batched entry point
 
-extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *stream) {
+static dllm_status validate(const dllm_batch_desc *d) {
     if (!d) return DLLM_ERR_INVALID_ARG;
     if (d->rows < 0 || d->vocab <= 0 || !d->logits || !d->uniforms || !d->token) return DLLM_ERR_INVALID_ARG;
     if (d->row_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
@@ -93,16 +127,47 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
     if (d->topk_ids && d->topk_stride < (d->row_params ? d->topk_max : d->params.top_k))
         return DLLM_ERR_INVALID_ARG;
     if (d->flags & ~(unsigned)DLLM_MODE_PEN_TRUE_DIV) return DLLM_ERR_UNSUPPORTED;
-    if (d->rows == 0) return DLLM_OK;
+    if (d->workspace && ((uintptr_t)d->workspace % 256 != 0)) return DLLM_ERR_INVALID_ARG;
+    return DLLM_OK;
+}
 
+static int topk_bound(const dllm_batch_desc *d) {
     int topk_max = d->row_params ? d->topk_max : d->params.top_k;
-    if (topk_max >= d->vocab) topk_max = 0;
-    if (topk_max < 0) topk_max = 0;
+    if (topk_max >= d->vocab || topk_max < 0) topk_max = 0;
+    return topk_max;
+}
+
+extern "C" size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *d) {
+    if (validate(d) != DLLM_OK || d->rows == 0) return 0;
+    const int tk = topk_bound(d);
+    if (tk > KMAX) return 0;
+    LaunchCfg cfg;
+    if (get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, tk, &cfg) != DLLM_OK) return 0;
+    return (size_t)d->rows * row_ws_bytes(nrec_for(cfg));
+}
+
+extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *stream) {
+    dllm_status st = validate(d);
+    if (st != DLLM_OK) return st;
+    if (d->rows == 0) return DLLM_OK;
+    const int topk_max = topk_bound(d);
     if (topk_max > KMAX) return DLLM_ERR_UNSUPPORTED;
 
     LaunchCfg cfg;
-    dllm_status st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
+    st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
     if (st != DLLM_OK) return st;
+    const int nrec = nrec_for(cfg);
+    const size_t ws_need = (size_t)d->rows * row_ws_bytes(nrec);
+    void *ws = d->workspace;
+    if (ws) {
+        if (d->workspace_bytes < ws_need) return DLLM_ERR_INVALID_ARG;
+    } else {
+        ws = internal_workspace(stream, ws_need);
+        if (!ws) {
+            set_error("workspace allocation", cudaErrorMemoryAllocation);
+            return DLLM_ERR_OOM;
+        }
+    }
 
     KernelArgs a = {};
     a.logits = d->logits;
@@ -122,7 +187,9 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
     a.vocab_total = d->vocab;
     a.vocab_offset = 0;
     a.S = cfg.S;
-    a.L = cfg.L;
+    a.SUB = cfg.SUB;
+    a.ws = (unsigned char *)ws;
+    a.nrec = nrec;
     a.htab = cfg.htab;
     a.uni_bytes = (int)(cfg.smem - (size_t)cfg.S * 4);
     a.cluster = cfg.cluster;

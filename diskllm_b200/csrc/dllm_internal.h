@@ -37,8 +37,8 @@ struct KernelArgs {
     int             vocab;          // ids in this logits slice
     int             vocab_total;    // full vocabulary (history ids are checked against it)
     int             vocab_offset;   // global id of local index 0
-    int             S;              // slice length per CTA (= NT * L)
-    int             L;              // elements per thread chunk (L % 8 == 4)
+    int             S;              // slice length per CTA (= 4 * NT * SUB)
+    int             SUB;            // elements per thread sub-chunk (SUB % 8 == 4)
     int             htab;           // history hash-table entries (power of 2)
     int             uni_bytes;      // bytes of the shared area after the slice
     int             cluster;        // CTAs per row (cluster size)
@@ -52,21 +52,33 @@ struct KernelArgs {
     int32_t        *topk_ids;       // [rows][topk_stride] or null
     int64_t         topk_stride;
     unsigned long long *dbg;        // diagnostic counters or null
+    unsigned char  *ws;             // workspace (row headers, warp records, stash)
+    int             nrec;           // warp records per row (4 * warps * cluster)
 };
 
 // Launch configuration chosen by the host for one (vocab, dtype, history bound, top-k bound).
 struct LaunchCfg {
     int cluster;     // C
     int threads;     // NT
-    int L;
+    int SUB;
     int S;
     int htab;
     size_t smem;     // dynamic shared memory bytes
     int max_clusters;// co-resident clusters on the device
 };
 
+// Workspace layout per row: RowHdr, nrec warp records, STASH_SLOTS stash slots.
+constexpr int STASH_SLOTS = 32;
+constexpr int STASH_STRIDE = 64;   // floats per stash slot: [0] = first index (as int), then SUB values
+constexpr int MAX_SUB = 60;
+// RowHdr (128 B) + nrec 24-byte warp records (rounded to 128 B) + the stash
+__host__ __device__ inline size_t row_ws_bytes(int nrec) {
+    return 128 + (((size_t)nrec * 24 + 127) & ~(size_t)127) + (size_t)STASH_SLOTS * STASH_STRIDE * 4;
+}
+
 dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
 dllm_status set_debug_counters(unsigned long long *dev_counters);
 dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream);
+int nrec_for(const LaunchCfg &cfg);
 
 }  // namespace dllm

@@ -1,12 +1,15 @@
 // dllm_kernel.cuh -- fused batched sampler for B200 (sm_100a): device code.
-// Included by dllm_kernel_inst.cu, which is compiled once per chunk length.
+// Included by dllm_kernel_inst.cu, which is compiled once per sub-chunk length.
 //
-// One thread-block cluster samples one row at a time (persistent over rows).  The row is split
-// into C contiguous slices, one per CTA; each slice is copied from HBM once into shared memory
-// with a bulk (TMA) copy while the next row's slice is prefetched into L2, and every later pass
-// reads shared memory.  Thread t of a CTA owns one contiguous chunk of L elements of the slice
-// (L is a compile-time constant, L % 8 == 4, so 16-byte shared loads of a warp are free of bank
-// conflicts).  Per row:
+// Two kernels per batch.
+//
+// Kernel A (sample_rows_kernel): one thread-block cluster samples one row at a time (persistent
+// over rows).  The row is split into C contiguous slices, one per CTA; each slice is copied from
+// HBM once into shared memory with a bulk (TMA) copy while the next row's slice is prefetched
+// into L2, and every later pass reads shared memory.  A slice is 4 * NT sub-chunks of SUB
+// elements (SUB compile-time, SUB % 8 == 4 so 16-byte shared loads of a warp are free of bank
+// conflicts), in index order; thread t owns sub-chunks t, NT + t, 2NT + t, 3NT + t (one per
+// quarter of the slice), which gives each thread four independent dependency chains.  Per row:
 //
 //   P1  bulk copy, grammar mask -> -inf, history penalties from an in-shared-memory hash table
 //       (presence / frequency once per id, repetition once per occurrence), slice maximum
@@ -17,21 +20,26 @@
 //       and softmax / min-p / top-p / draw run on that short list (a 4-pass radix select is
 //       the fallback when too many elements survive the threshold)
 //   otherwise (top-k off: the reference's index-order list):
-//   P2  t = (x - M) * (1/T), e = expf(t - max_t) in place, double sum    -> cluster sum
+//   P2  t = (x - M) * (1/T), e = expf(t - max_t) in place, compensated sum -> cluster sum
 //   P2b min-p (absolute threshold) kept count / renormalisation sum      -> cluster sums
-//   P3  chunk sums of the list probabilities, exclusive scan over the cluster; the one warp
-//       holding the chunk where (float)cumsum first reaches top_p finds the cut element
+//   P3  sub-chunk sums of the list probabilities, exclusive scan over the cluster; the one warp
+//       holding the sub-chunk where (float)cumsum first reaches top_p finds the cut element
 //                                                                          -> cluster
-//   P4  exact emulation of the reference's sequential fp32 draw (src/sampler.c:226-231).
-//       Within one binade [2^e, 2^(e+1)) of the running sum c, fl(c + q) = c + n*ulp(c), where
-//       n depends only on q and on the parity of c/ulp (ties-to-even), so a run of adds is a
-//       function of one parity bit: (n_even, n_odd).  Each thread computes that pair for four
-//       sub-chunks of its chunk (real fp32 chains started at 2^e and 2^e + ulp, e predicted from
-//       the exact double prefix), composes them, and each warp composes its 32 chunks into a
-//       record of the form prefix / one boundary chunk / suffix.  The records are gathered in
-//       CTA 0, where one walker warp composes them in order on the exact running sum, checking
-//       every step's validity, replaying boundary chunks in plain fp32 (cooperatively, a few
-//       elements per lane) and descending into the chunk where the uniform falls.
+//   P4  records for the exact emulation of the reference's sequential fp32 draw
+//       (src/sampler.c:226-231).  Within one binade [2^e, 2^(e+1)) of the running sum c,
+//       fl(c + q) = c + n*ulp(c), where n depends only on q and on the parity of c/ulp
+//       (ties-to-even), so a run of adds is a function of one parity bit: (n_even, n_odd).  Each
+//       thread computes that pair for its four sub-chunks (real fp32 chains started at 2^e and
+//       2^e + ulp, e predicted from the exact double prefix), each warp composes its 32
+//       sub-chunks of a quarter into a record (prefix run / one boundary sub-chunk / suffix run),
+//       and the records, the boundary sub-chunks' probabilities and the row's scalars go to the
+//       workspace.
+//
+// Kernel B (walk_rows_kernel): one warp per row composes the warp records in order on the exact
+// running sum, checking every step's validity, replaying boundary sub-chunks in plain fp32
+// (cooperatively, a few elements per lane), and descending into the region where the uniform
+// falls, whose probabilities it recomputes from the row's inputs with the row's scalars.  The
+// first id with r < c is the sample (or the list's last id when r reaches the total).
 //
 // Bit-exactness: the translation unit is built with -fmad=false and -ftz=true (the reference
 // executables run with FTZ|DAZ); every operation that must round like the reference is an
@@ -51,44 +59,55 @@ namespace dllm {
 
 typedef void (*KernelFn)(const KernelArgs);
 
+// Row scalars kept in the workspace for the walk kernel (128 bytes).
+struct RowHdr {
+    float M, inv_temp, mv, inv_sum, min_p, inv_s2, inv_s3, r;
+    int cut_idx, last_idx, flags, done, minp, nokept, topp, nstash;
+    int pad[16];
+};
+// Warp-level draw record (24 bytes).  meta: type (bits 0-1), boundary sub-chunk (2-7, 63 =
+// none), first suffix sub-chunk (8-13), prefix binade (16-23), suffix binade (24-31).
+struct WRec {
+    uint32_t meta;
+    uint32_t p0, p1, s0, s1;
+    int slot;   // stash slot holding the boundary sub-chunk's probabilities, or -1
+};
+
 // everything below has internal linkage: this header is compiled into several units
 namespace {
 
 constexpr int MAXW = 16;          // warps per CTA (blockDim <= 512)
 constexpr int CAND_CAP = 2048;    // top-k survivors gathered in CTA 0
-constexpr int STASH_SLOTS = 24;   // boundary chunks whose probabilities are gathered in CTA 0
 constexpr int TMA_PIECE = 32768;  // bytes per bulk copy instruction
 constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
+constexpr int WALK_WARPS = 4;     // rows per CTA of the walk kernel
+constexpr int HLIST = 256;        // per-warp history ids kept for a recomputed region
 
 enum : int { REC_IDENT = 0, REC_CLEAN = 1, REC_MIXED = 2, REC_PBS = 3 };
 
-// Diagnostic counters: per-phase cycles of cluster rank 0 and draw-walk statistics.  Each
-// CTA's thread 0 stores KernelArgs::dbg here at kernel start (every CTA stores the same
-// value).  Null in normal operation.
+// Diagnostic counters: per-phase cycles of cluster rank 0 and walk statistics.  Thread 0 of
+// every CTA stores KernelArgs::dbg here at kernel start (all store the same value).
 __device__ unsigned long long *g_dbg = nullptr;
 enum : int {
     DBG_P1 = 0, DBG_W1 = 1, DBG_P2 = 2, DBG_W2 = 3, DBG_P3 = 4, DBG_W3 = 5, DBG_CUT = 6,
-    DBG_P4 = 7, DBG_W5 = 8, DBG_WALK = 9, DBG_WEND = 10, DBG_TOPK = 11, DBG_LOADWAIT = 12,
+    DBG_P4 = 7, DBG_WEND = 10, DBG_TOPK = 11, DBG_LOADWAIT = 12,
     DBG_ROWS = 16, DBG_REPLAY = 17, DBG_EXPAND = 18, DBG_STEPS = 19, DBG_REPLAY_IT = 20,
-    DBG_PBS = 21, DBG_STASH_MISS = 22, DBG_TOPK_FALLBACK = 23,
+    DBG_PBS = 21, DBG_STASH_MISS = 22, DBG_TOPK_FALLBACK = 23, DBG_RECOMP = 24, DBG_WALK_CYC = 25,
 };
 __device__ __forceinline__ void dbg_add(int k, unsigned long long v) {
     if (g_dbg) atomicAdd(g_dbg + k, v);
 }
 
-// Warp-level record: a prefix run of chunks in binade e_pre, an optional boundary chunk, and a
-// suffix run (from chunk sfrom) in binade e_suf.  REC_CLEAN uses only the prefix fields.
-struct WRec {
-    int type;
-    int e_pre;
-    uint32_t p0, p1;
-    int bchunk;       // boundary chunk (lane) or -1
-    int e_suf;
-    uint32_t s0, s1;
-    int slot;         // stash slot holding the boundary chunk's probabilities, or -1
-    int sfrom;        // first chunk of the suffix
-    int pad[2];
-};
+__device__ __forceinline__ RowHdr *row_hdr(const KernelArgs &a, int row) {
+    return reinterpret_cast<RowHdr *>(a.ws + (size_t)row * row_ws_bytes(a.nrec));
+}
+__device__ __forceinline__ WRec *row_recs(const KernelArgs &a, int row) {
+    return reinterpret_cast<WRec *>(reinterpret_cast<unsigned char *>(row_hdr(a, row)) + sizeof(RowHdr));
+}
+__device__ __forceinline__ float *row_stash(const KernelArgs &a, int row) {
+    const size_t recb = ((size_t)a.nrec * sizeof(WRec) + 127) & ~(size_t)127;
+    return reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(row_hdr(a, row)) + sizeof(RowHdr) + recb);
+}
 
 // Values each CTA publishes to its cluster.  Every field is written at most once per row and
 // read only after the cluster barrier that follows the write.
@@ -110,19 +129,31 @@ struct Xch {
     uint32_t theta;
     int cnt_gt, cnt_eq;
     int ncand;        // CTA 0: survivors gathered
-    int nstash;       // CTA 0: stash slots used
     unsigned hist[2][256];
 };
 
 struct Shared {
     Xch xs;
     unsigned long long tma_bar;
-    double red_d[MAXW];
+    double red_d[4 * MAXW];
     float red_f[MAXW];
-    int red_i[MAXW];
+    int red_i[4 * MAXW];
     int red_i2[MAXW];
     int bcast_i[4];
 };
+
+// compensated fp32 sum (TwoSum per add): s + c carries ~48 bits
+struct CSum {
+    float s, c;
+};
+__device__ __forceinline__ void csum_add(CSum &a, float x) {
+    const float t = __fadd_rn(a.s, x);
+    const float z = __fsub_rn(t, a.s);
+    const float e = __fadd_rn(__fsub_rn(a.s, __fsub_rn(t, z)), __fsub_rn(x, z));
+    a.s = t;
+    a.c = __fadd_rn(a.c, e);
+}
+__device__ __forceinline__ double csum_val(const CSum &a) { return (double)a.s + (double)a.c; }
 
 __device__ __forceinline__ uint32_t fbits(float x) { return __float_as_uint(x); }
 __device__ __forceinline__ float bitsf(uint32_t b) { return __uint_as_float(b); }
@@ -572,13 +603,84 @@ __device__ void load_slice_bf16(const KernelArgs &a, int row, int slice0, int sl
     for (int i = done + tid; i < slen; i += NT) vals[i] = bitsf((uint32_t)s16[i] << 16);
 }
 
-// ----------------------------------------------------------------------------------------
 
-template <int DT, int LT>
+// Exclusive / inclusive scan of four doubles per thread (one per quarter), in thread order;
+// same bit-consistency as block_scan_d for each of the four.
+__device__ void block_scan4_d(const double v[4], double *scratch, double excl[4], double incl[4], double tot[4]) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    double x[4], prev[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        x[q] = v[q];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            double y = __shfl_up_sync(0xffffffffu, x[q], o);
+            if (lane >= o) x[q] = y + x[q];
+        }
+        prev[q] = __shfl_up_sync(0xffffffffu, x[q], 1);
+    }
+    __syncthreads();
+    if (lane == 31)
+#pragma unroll
+        for (int q = 0; q < 4; q++) scratch[q * MAXW + w] = x[q];
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        double off = 0.0;
+        for (int i = 0; i < w; i++) off = off + scratch[q * MAXW + i];
+        double t = off;
+        for (int i = w; i < nw; i++) t = t + scratch[q * MAXW + i];
+        excl[q] = lane == 0 ? off : off + prev[q];
+        incl[q] = off + x[q];
+        tot[q] = t;
+    }
+}
+
+// Exclusive scan of four ints per thread in (quarter, thread) order; returns per-quarter
+// offsets already including the totals of earlier quarters.
+__device__ void block_scan4_i(const int v[4], int *scratch, int excl[4], int &total) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int x[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        x[q] = v[q];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int y = __shfl_up_sync(0xffffffffu, x[q], o);
+            if (lane >= o) x[q] += y;
+        }
+    }
+    __syncthreads();
+    if (lane == 31)
+#pragma unroll
+        for (int q = 0; q < 4; q++) scratch[q * MAXW + w] = x[q];
+    __syncthreads();
+    int base = 0;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        int off = 0, t = 0;
+        for (int i = 0; i < nw; i++) {
+            if (i < w) off += scratch[q * MAXW + i];
+            t += scratch[q * MAXW + i];
+        }
+        excl[q] = base + off + x[q] - v[q];
+        base += t;
+    }
+    total = base;
+}
+
+__device__ __forceinline__ uint32_t pack_meta(int type, int bchunk, int sfrom, int e_pre, int e_suf) {
+    return (uint32_t)type | ((uint32_t)(bchunk < 0 ? 63 : bchunk) << 2) | ((uint32_t)sfrom << 8) |
+           ((uint32_t)(e_pre & 255) << 16) | ((uint32_t)(e_suf & 255) << 24);
+}
+
+// ----------------------------------------------------------------------------------------
+// kernel A
+
+template <int DT, int SUBT>
 __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a) {
-    static_assert(LT % 8 == 4 && LT <= 252, "chunk length");
-    constexpr int NV = LT / 4;      // float4 per chunk
-    constexpr int SUB = LT / 4;     // elements per sub-chunk (four sub-chunks per chunk)
+    static_assert(SUBT % 8 == 4 && SUBT <= MAX_SUB, "sub-chunk length");
+    constexpr int NV4 = SUBT / 4;   // float4 per sub-chunk
     cg::cluster_group cluster = cg::this_cluster();
     extern __shared__ __align__(16) unsigned char dsm[];
     __shared__ Shared sh;
@@ -591,20 +693,15 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
     const int S = a.S, V = a.vocab;
     const int slice0 = rank * S;
     const int slen = max(0, min(S, V - slice0));
-    const int cbase = tid * LT;               // slice-relative start of this thread's chunk
+    int kb[4];  // slice-relative start of this thread's four sub-chunks
+#pragma unroll
+    for (int q = 0; q < 4; q++) kb[q] = (q * NT + tid) * SUBT;
 
     float *vals = reinterpret_cast<float *>(dsm);
     unsigned char *uni = dsm + (size_t)S * sizeof(float);
-    // union area: history table | chunk records + walk stash | top-k survivors + list
+    // union area: history table | top-k survivors + list
     int *hkeys = reinterpret_cast<int *>(uni);
     int *hcnt = hkeys + a.htab;
-    int *rec_type = reinterpret_cast<int *>(uni);
-    int *rec_e = rec_type + NT;
-    uint32_t *rec_n0 = reinterpret_cast<uint32_t *>(rec_e + NT);
-    uint32_t *rec_n1 = rec_n0 + NT;
-    // CTA 0 only: the cluster's warp records, then stashed boundary-chunk probabilities
-    WRec *wstash = reinterpret_cast<WRec *>(rec_n1 + NT);
-    float *qstash = reinterpret_cast<float *>(wstash + C * NW);
     unsigned long long *cand = reinterpret_cast<unsigned long long *>(uni);
 
     auto remote_xs = [&](int r) -> Xch * { return cluster.map_shared_rank(&sh.xs, r); };
@@ -654,12 +751,16 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         if (timing) dbg_add(DBG_ROWS, 1);
         const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
         const float r = a.uniforms[row];
+        RowHdr *hdr = row_hdr(a, row);
         int flags = 0;
 
         // ---------------- P1: bulk copy in flight while the history table is built ---------------
-        if (use_tma && tid == 0) {
-            issue_row_copy(row);
-            if (row + ncl < a.rows) prefetch_row(row + ncl);
+        if (tid == 0) {
+            if (use_tma) {
+                issue_row_copy(row);
+                if (row + ncl < a.rows) prefetch_row(row + ncl);
+            }
+            if (rank == 0) hdr->nstash = 0;
         }
         for (int i = tid; i < a.htab; i += NT) {
             hkeys[i] = -1;
@@ -712,28 +813,26 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         __syncthreads();
         mark(DBG_LOADWAIT);
 
-        // mask + raw maximum over this thread's chunk
+        // mask + raw maximum (strided float4 pass over the slice)
         float lmax = -INFINITY;
         {
-            float4 *v4 = reinterpret_cast<float4 *>(vals + cbase);
+            float4 *v4 = reinterpret_cast<float4 *>(vals);
             const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
             if (mrow) {
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const int li = slice0 + cbase + 4 * j;
-                    float4 x = v4[j];
+                for (int i = tid; i < S / 4; i += NT) {
+                    const int li = slice0 + 4 * i;
+                    float4 x = v4[i];
                     const uint32_t w = li < V ? (mrow[li >> 5] >> (li & 31)) : 0u;
                     x.x = (w & 1u) ? x.x : -INFINITY;
                     x.y = (w & 2u) ? x.y : -INFINITY;
                     x.z = (w & 4u) ? x.z : -INFINITY;
                     x.w = (w & 8u) ? x.w : -INFINITY;
-                    v4[j] = x;
+                    v4[i] = x;
                     lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
             } else {
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const float4 x = v4[j];
+                for (int i = tid; i < S / 4; i += NT) {
+                    const float4 x = v4[i];
                     lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
             }
@@ -772,10 +871,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             flags = rf & 0xffff;
             if (rf & 0x10000) {
                 float m2 = -INFINITY;
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const float4 x = v4[j];
+                const float4 *v4 = reinterpret_cast<const float4 *>(vals);
+                for (int i = tid; i < S / 4; i += NT) {
+                    const float4 x = v4[i];
                     m2 = fmaxf(m2, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
                 lm = block_allreduce(m2, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
@@ -811,23 +909,17 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         const bool greedy = p.temperature == 0.0f;
         const bool topk = p.top_k > 0 && p.top_k < a.vocab_total;
         int token = -1;
+        bool done = true;   // token decided here (else the walk kernel draws it)
 
         if (greedy) {
             // ---------------- greedy: first index holding M ----------------------------------
             int first = INT_MAX;
-            {
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
-#pragma unroll
-                for (int j = NV - 1; j >= 0; j--) {
-                    const float4 x = v4[j];
-                    const int li = cbase + 4 * j;
-                    if (x.w == M && li + 3 < slen) first = li + 3;
-                    if (x.z == M && li + 2 < slen) first = li + 2;
-                    if (x.y == M && li + 1 < slen) first = li + 1;
-                    if (x.x == M && li < slen) first = li;
+            for (int i = tid; i < slen; i += NT)
+                if (vals[i] == M) {
+                    first = i;
+                    break;
                 }
-                if (first != INT_MAX) first += slice0;
-            }
+            if (first != INT_MAX) first += slice0;
             const int bf = block_allreduce(first, sh.red_i, [](int x, int y) { return min(x, y); });
             if (tid == 0) sh.xs.gidx = bf;
             cluster.sync();  // ---- greedy
@@ -864,16 +956,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             if (use_threshold) {
                 // threshold: the k-th largest per-thread maximum (>= k elements at or above it)
                 uint32_t tmax = 0u;
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const float4 x = v4[j];
-                    const int li = cbase + 4 * j;
-                    if (li < slen) tmax = max(tmax, key_of(x.x));
-                    if (li + 1 < slen) tmax = max(tmax, key_of(x.y));
-                    if (li + 2 < slen) tmax = max(tmax, key_of(x.z));
-                    if (li + 3 < slen) tmax = max(tmax, key_of(x.w));
-                }
+                for (int i = tid; i < slen; i += NT) tmax = max(tmax, key_of(vals[i]));
                 uint32_t pref = 0u;
                 for (int bit = 31; bit >= 0; bit--) {
                     const uint32_t cv = pref | (1u << bit);
@@ -890,26 +973,20 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 // survivors -> CTA 0
                 int *ncand0 = &remote_xs(0)->ncand;
                 unsigned long long *cand0 = cluster.map_shared_rank(cand, 0);
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const float4 x = v4[j];
-                    const float xs4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const int li = cbase + 4 * j + c;
-                        const uint32_t key = li < slen ? key_of(xs4[c]) : 0u;
-                        const bool take = li < slen && key >= theta;
-                        const unsigned m = __ballot_sync(0xffffffffu, take);
-                        if (m) {
-                            const int leader = __ffs(m) - 1;
-                            int base = 0;
-                            if (lane == leader) base = atomicAdd(ncand0, __popc(m));
-                            base = __shfl_sync(0xffffffffu, base, leader);
-                            if (take) {
-                                const int o = base + __popc(m & ((1u << lane) - 1u));
-                                const uint32_t gid = (uint32_t)(slice0 + li);
-                                if (o < cap) cand0[o] = ((unsigned long long)key << 32) | (0xffffffffu - gid);
-                            }
+                for (int i0 = 0; i0 < S; i0 += NT) {
+                    const int li = i0 + tid;
+                    const uint32_t key = li < slen ? key_of(vals[li]) : 0u;
+                    const bool take = li < slen && key >= theta;
+                    const unsigned m = __ballot_sync(0xffffffffu, take);
+                    if (m) {
+                        const int leader = __ffs(m) - 1;
+                        int base = 0;
+                        if (lane == leader) base = atomicAdd(ncand0, __popc(m));
+                        base = __shfl_sync(0xffffffffu, base, leader);
+                        if (take) {
+                            const int o = base + __popc(m & ((1u << lane) - 1u));
+                            const uint32_t gid = (uint32_t)(slice0 + li);
+                            if (o < cap) cand0[o] = ((unsigned long long)key << 32) | (0xffffffffu - gid);
                         }
                     }
                 }
@@ -918,7 +995,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 if (!use_threshold && timing) dbg_add(DBG_TOPK_FALLBACK, 1);
             }
             if (!use_threshold) {
-                // 4-pass cluster radix select of the k-th key, then exact gather
+                // 4-pass cluster radix select of the k-th key, then exact gather (ties by id)
                 uint32_t prefix = 0, pmask = 0;
                 int krem = k;
                 for (int pass = 0; pass < 4; pass++) {
@@ -926,8 +1003,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     unsigned *h = sh.xs.hist[pass & 1];
                     for (int i = tid; i < 256; i += NT) h[i] = 0;
                     __syncthreads();
-                    for (int j = 0; j < LT; j++) {
-                        const int li = cbase + j;
+                    for (int i0 = 0; i0 < S; i0 += NT) {
+                        const int li = i0 + tid;
                         int d = -1;
                         if (li < slen) {
                             const uint32_t key = key_of(vals[li]);
@@ -989,18 +1066,23 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
                 const uint32_t kstar = prefix;
                 const int ngt = k - krem;
-                int cgt = 0, ceq = 0;
-                for (int j = 0; j < LT; j++) {
-                    const int li = cbase + j;
-                    if (li < slen) {
-                        const uint32_t key = key_of(vals[li]);
-                        cgt += key > kstar;
-                        ceq += key == kstar;
+                // counts per (quarter, thread) sub-chunk: sub-chunks in that order are in id order
+                int cgt[4], ceq[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    cgt[q] = ceq[q] = 0;
+                    for (int j = 0; j < SUBT; j++) {
+                        const int li = kb[q] + j;
+                        if (li < slen) {
+                            const uint32_t key = key_of(vals[li]);
+                            cgt[q] += key > kstar;
+                            ceq[q] += key == kstar;
+                        }
                     }
                 }
-                int egt, tgt, eeq, teq;
-                block_scan_i(cgt, sh.red_i, egt, tgt);
-                block_scan_i(ceq, sh.red_i2, eeq, teq);
+                int egt[4], eeq[4], tgt, teq;
+                block_scan4_i(cgt, sh.red_i, egt, tgt);
+                block_scan4_i(ceq, sh.red_i, eeq, teq);
                 if (tid == 0) {
                     sh.xs.cnt_gt = tgt;
                     sh.xs.cnt_eq = teq;
@@ -1013,18 +1095,21 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     oeq += x->cnt_eq;
                 }
                 unsigned long long *cand0 = cluster.map_shared_rank(cand, 0);
-                int pg = ogt + egt, pe = oeq + eeq;
-                for (int j = 0; j < LT; j++) {
-                    const int li = cbase + j;
-                    if (li < slen) {
-                        const uint32_t key = key_of(vals[li]);
-                        const uint32_t gid = (uint32_t)(slice0 + li);
-                        const unsigned long long comp = ((unsigned long long)key << 32) | (0xffffffffu - gid);
-                        if (key > kstar) {
-                            cand0[pg++] = comp;
-                        } else if (key == kstar) {
-                            if (pe < krem) cand0[ngt + pe] = comp;
-                            pe++;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    int pg = ogt + egt[q], pe = oeq + eeq[q];
+                    for (int j = 0; j < SUBT; j++) {
+                        const int li = kb[q] + j;
+                        if (li < slen) {
+                            const uint32_t key = key_of(vals[li]);
+                            const uint32_t gid = (uint32_t)(slice0 + li);
+                            const unsigned long long comp = ((unsigned long long)key << 32) | (0xffffffffu - gid);
+                            if (key > kstar) {
+                                cand0[pg++] = comp;
+                            } else if (key == kstar) {
+                                if (pe < krem) cand0[ngt + pe] = comp;
+                                pe++;
+                            }
                         }
                     }
                 }
@@ -1075,6 +1160,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             }
         } else {
             // ---------------- index-order path -------------------------------------------------
+            done = false;
             const float inv_temp = __fdiv_rn(1.0f, p.temperature);
             float mv;
             if (inv_temp > 0.0f && inv_temp < INFINITY) {
@@ -1089,22 +1175,25 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 if (lane < C) tv = remote_xs(lane)->mt;
                 mv = warp_allreduce(tv, [](float x, float y) { return fmaxf(x, y); });
             }
-            // P2: exponentials (in place), double sum with four accumulators
+            // P2: exponentials (in place), compensated sum
             double ds;
             {
-                float4 *v4 = reinterpret_cast<float4 *>(vals + cbase);
-                double acc[4] = {0.0, 0.0, 0.0, 0.0};
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    float4 x = v4[j];
+                float4 *v4 = reinterpret_cast<float4 *>(vals);
+                CSum c0 = {0.0f, 0.0f}, c1 = {0.0f, 0.0f};
+#pragma unroll 2
+                for (int i = tid; i < S / 4; i += NT) {
+                    float4 x = v4[i];
                     x.x = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
                     x.y = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
                     x.z = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
                     x.w = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
-                    v4[j] = x;
-                    acc[j & 3] = acc[j & 3] + (((double)x.x + (double)x.y) + ((double)x.z + (double)x.w));
+                    v4[i] = x;
+                    csum_add(c0, x.x);
+                    csum_add(c1, x.y);
+                    csum_add(c0, x.z);
+                    csum_add(c1, x.w);
                 }
-                ds = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+                ds = csum_val(c0) + csum_val(c1);
             }
             ds = block_allreduce(ds, sh.red_d, [](double x, double y) { return x + y; });
             if (tid == 0) sh.xs.dsum = ds;
@@ -1127,25 +1216,18 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             ch.cut_idx = INT_MAX;
 
             if (ch.minp) {
-                double s2 = 0.0, sall = 0.0;
+                CSum s2c = {0.0f, 0.0f}, sac = {0.0f, 0.0f};
                 int nk = 0;
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
-#pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const float4 x = v4[j];
-                    const float e4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const float pp = __fmul_rn(e4[c], ch.inv_sum);
-                        sall = sall + (double)pp;
-                        if (pp >= ch.min_p) {
-                            s2 = s2 + (double)pp;
-                            nk++;
-                        }
+                for (int i = tid; i < S; i += NT) {
+                    const float pp = __fmul_rn(vals[i], ch.inv_sum);
+                    csum_add(sac, pp);
+                    if (pp >= ch.min_p) {
+                        csum_add(s2c, pp);
+                        nk++;
                     }
                 }
-                s2 = block_allreduce(s2, sh.red_d, [](double x, double y) { return x + y; });
-                sall = block_allreduce(sall, sh.red_d, [](double x, double y) { return x + y; });
+                const double s2 = block_allreduce(csum_val(s2c), sh.red_d, [](double x, double y) { return x + y; });
+                const double sall = block_allreduce(csum_val(sac), sh.red_d, [](double x, double y) { return x + y; });
                 nk = block_allreduce(nk, sh.red_i, [](int x, int y) { return x + y; });
                 if (tid == 0) {
                     sh.xs.s2 = s2;
@@ -1170,62 +1252,60 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 ch.inv_s2 = __double2float_rn(1.0 / (ch.nokept ? SA : S2));
             }
 
-            // P3: sub-chunk / chunk sums of the list probabilities, cluster scan
-            double subs[4] = {0.0, 0.0, 0.0, 0.0};
+            // P3: sums of the list probabilities over this thread's four sub-chunks
+            double subd[4];
             int fmem = INT_MAX, lmem = -1;
             float fw = 0.0f;
             {
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
-                if (ch.minp && !ch.nokept) {
+                CSum sub[4];
 #pragma unroll
-                    for (int j = 0; j < NV; j++) {
-                        const float4 x = v4[j];
+                for (int q = 0; q < 4; q++) sub[q].s = sub[q].c = 0.0f;
+                const bool track = ch.minp && !ch.nokept;
+#pragma unroll 2
+                for (int j = 0; j < NV4; j++) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
                         const float e4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
                         for (int c = 0; c < 4; c++) {
-                            const int el = 4 * j + c;
-                            const int li = cbase + el;
                             const float w = w_of(ch, e4[c]);
-                            subs[el / SUB] = subs[el / SUB] + (double)w;
-                            if (li < slen && member_of(ch, e4[c])) {
-                                if (fmem == INT_MAX) {
-                                    fmem = slice0 + li;
-                                    fw = w;
+                            csum_add(sub[q], w);
+                            if (track) {
+                                const int li = kb[q] + 4 * j + c;
+                                if (li < slen && member_of(ch, e4[c])) {
+                                    if (slice0 + li < fmem) {
+                                        fmem = slice0 + li;
+                                        fw = w;
+                                    }
+                                    lmem = max(lmem, slice0 + li);
                                 }
-                                lmem = slice0 + li;
                             }
                         }
                     }
-                } else {
+                }
 #pragma unroll
-                    for (int j = 0; j < NV; j++) {
-                        const float4 x = v4[j];
-                        const float e4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            const int el = 4 * j + c;
-                            subs[el / SUB] = subs[el / SUB] + (double)w_of(ch, e4[c]);
-                        }
-                    }
-                    if (cbase < slen) {
-                        fmem = slice0 + cbase;
-                        fw = w_of(ch, vals[cbase]);
-                        lmem = slice0 + min(cbase + LT, slen) - 1;
-                    }
+                for (int q = 0; q < 4; q++) subd[q] = csum_val(sub[q]);
+                if (!track && tid == 0 && slen > 0) {
+                    fmem = slice0;
+                    fw = w_of(ch, vals[0]);
+                    lmem = slice0 + slen - 1;
                 }
             }
-            const double cs = (subs[0] + subs[1]) + (subs[2] + subs[3]);
-            double excl, incl, ctot;
-            block_scan_d(cs, sh.red_d, excl, incl, ctot);
+            double excl[4], incl[4], qtot[4];
+            block_scan4_d(subd, sh.red_d, excl, incl, qtot);
+            double Q[5];
+            Q[0] = 0.0;
+#pragma unroll
+            for (int q = 0; q < 4; q++) Q[q + 1] = Q[q] + qtot[q];
             const int bfm = block_allreduce(fmem, sh.red_i, [](int x, int y) { return min(x, y); });
             const int blm = block_allreduce(lmem, sh.red_i2, [](int x, int y) { return max(x, y); });
             if (fmem == bfm && fmem != INT_MAX) sh.xs.first_w = fw;
             if (tid == 0) {
-                sh.xs.tot = ctot;
+                sh.xs.tot = Q[4];
                 sh.xs.first_member = bfm;
                 sh.xs.last_member = blm;
                 sh.xs.cut_idx = -1;
-                sh.xs.nstash = 0;
             }
             mark(DBG_P3);
             cluster.sync();  // ---- #3
@@ -1250,7 +1330,12 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             gfm = __shfl_sync(0xffffffffu, gfm, 0);
             gfw = __shfl_sync(0xffffffffu, gfw, 0);
             glm = __shfl_sync(0xffffffffu, glm, 0);
-            const double P0 = off + excl, P1 = off + incl;
+            double P0[4], P1[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                P0[q] = off + (Q[q] + excl[q]);
+                P1[q] = off + (Q[q] + incl[q]);
+            }
 
             int last_idx = ch.minp && !ch.nokept ? glm : V - 1;
             if (ch.topp) {
@@ -1261,66 +1346,69 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     cut = gfm;
                     s3 = (double)gfw;
                 } else {
-                    // the single chunk where (float)cumsum first reaches top_p; its warp finds the
-                    // cut element cooperatively
-                    const bool crosses = __double2float_rn(P1) >= tp && !(__double2float_rn(P0) >= tp);
-                    const unsigned cm = __ballot_sync(0xffffffffu, crosses);
-                    if (cm) {
-                        const int src = __ffs(cm) - 1;
-                        const double base = __shfl_sync(0xffffffffu, P0, src);
-                        const int cb0 = __shfl_sync(0xffffffffu, cbase, src);
-                        constexpr int SL = (LT + 31) / 32;
-                        const int j0 = lane * SL;
-                        double part = 0.0;
-                        float wv[SL];
-                        bool mem[SL];
+                    // the single sub-chunk where (float)cumsum first reaches top_p; its warp finds
+                    // the cut element cooperatively
 #pragma unroll
-                        for (int k = 0; k < SL; k++) {
-                            const int li = cb0 + j0 + k;
-                            const bool in = j0 + k < LT && li < slen;
-                            const float e = in ? vals[li] : 0.0f;
-                            mem[k] = in && member_of(ch, e);
-                            wv[k] = mem[k] ? w_of(ch, e) : 0.0f;
-                            part = part + (double)wv[k];
-                        }
-                        double x = part;
+                    for (int q = 0; q < 4; q++) {
+                        const bool crosses = __double2float_rn(P1[q]) >= tp && !(__double2float_rn(P0[q]) >= tp);
+                        const unsigned cm = __ballot_sync(0xffffffffu, crosses);
+                        if (cm) {
+                            const int src = __ffs(cm) - 1;
+                            const double base = __shfl_sync(0xffffffffu, P0[q], src);
+                            const int cb0 = __shfl_sync(0xffffffffu, kb[q], src);
+                            constexpr int SL = (SUBT + 31) / 32;
+                            const int j0 = lane * SL;
+                            double part = 0.0;
+                            float wv[SL];
+                            bool mem[SL];
 #pragma unroll
-                        for (int o = 1; o < 32; o <<= 1) {
-                            double y = __shfl_up_sync(0xffffffffu, x, o);
-                            if (lane >= o) x = y + x;
-                        }
-                        const double ex = __shfl_up_sync(0xffffffffu, x, 1);
-                        double cum = lane == 0 ? base : base + ex;
-                        int hitk = -1, lastm = -1;
-                        double hitc = 0.0;
+                            for (int k = 0; k < SL; k++) {
+                                const int li = cb0 + j0 + k;
+                                const bool in = j0 + k < SUBT && li < slen;
+                                const float e = in ? vals[li] : 0.0f;
+                                mem[k] = in && member_of(ch, e);
+                                wv[k] = mem[k] ? w_of(ch, e) : 0.0f;
+                                part = part + (double)wv[k];
+                            }
+                            double x = part;
 #pragma unroll
-                        for (int k = 0; k < SL; k++) {
-                            if (mem[k] && hitk < 0) {
-                                cum = cum + (double)wv[k];
-                                lastm = k;
-                                if (__double2float_rn(cum) >= tp) {
-                                    hitk = k;
-                                    hitc = cum;
+                            for (int o = 1; o < 32; o <<= 1) {
+                                double y = __shfl_up_sync(0xffffffffu, x, o);
+                                if (lane >= o) x = y + x;
+                            }
+                            const double ex = __shfl_up_sync(0xffffffffu, x, 1);
+                            double cum = lane == 0 ? base : base + ex;
+                            int hitk = -1, lastm = -1;
+                            double hitc = 0.0;
+#pragma unroll
+                            for (int k = 0; k < SL; k++) {
+                                if (mem[k] && hitk < 0) {
+                                    cum = cum + (double)wv[k];
+                                    lastm = k;
+                                    if (__double2float_rn(cum) >= tp) {
+                                        hitk = k;
+                                        hitc = cum;
+                                    }
                                 }
                             }
-                        }
-                        const unsigned hm = __ballot_sync(0xffffffffu, hitk >= 0);
-                        int ci;
-                        double cs3;
-                        if (hm) {
-                            const int hl = __ffs(hm) - 1;
-                            ci = __shfl_sync(0xffffffffu, cb0 + j0 + hitk, hl);
-                            cs3 = __shfl_sync(0xffffffffu, hitc, hl);
-                        } else {
-                            // rounding disagreed with the chunk sum: cut at the chunk's last member
-                            const unsigned lm2 = __ballot_sync(0xffffffffu, lastm >= 0);
-                            const int ll = lm2 ? 31 - __clz(lm2) : 0;
-                            ci = __shfl_sync(0xffffffffu, cb0 + j0 + lastm, ll);
-                            cs3 = base + __shfl_sync(0xffffffffu, x, 31);
-                        }
-                        if (lane == 0) {
-                            sh.xs.cut_idx = slice0 + ci;
-                            sh.xs.cut_s3 = cs3;
+                            const unsigned hm = __ballot_sync(0xffffffffu, hitk >= 0);
+                            int ci;
+                            double cs3;
+                            if (hm) {
+                                const int hl = __ffs(hm) - 1;
+                                ci = __shfl_sync(0xffffffffu, cb0 + j0 + hitk, hl);
+                                cs3 = __shfl_sync(0xffffffffu, hitc, hl);
+                            } else {
+                                // rounding disagreed with the sub-chunk sum: cut at its last member
+                                const unsigned lm2 = __ballot_sync(0xffffffffu, lastm >= 0);
+                                const int ll = lm2 ? 31 - __clz(lm2) : 0;
+                                ci = __shfl_sync(0xffffffffu, cb0 + j0 + lastm, ll);
+                                cs3 = base + __shfl_sync(0xffffffffu, x, 31);
+                            }
+                            if (lane == 0) {
+                                sh.xs.cut_idx = slice0 + ci;
+                                sh.xs.cut_s3 = cs3;
+                            }
                         }
                     }
                     cluster.sync();  // ---- #4
@@ -1342,245 +1430,317 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
                 ch.inv_s3 = __double2float_rn(1.0 / s3);
             }
+            if (rank == 0 && tid == 0) {
+                hdr->M = M;
+                hdr->inv_temp = inv_temp;
+                hdr->mv = mv;
+                hdr->inv_sum = ch.inv_sum;
+                hdr->min_p = ch.min_p;
+                hdr->inv_s2 = ch.inv_s2;
+                hdr->inv_s3 = ch.inv_s3;
+                hdr->r = r;
+                hdr->cut_idx = ch.cut_idx;
+                hdr->last_idx = last_idx;
+                hdr->flags = rowflags;
+                hdr->minp = ch.minp;
+                hdr->nokept = ch.nokept;
+                hdr->topp = ch.topp;
+                hdr->done = 0;
+            }
             mark(DBG_CUT);
 
-            // P4: sub-chunk records (exact fp32 running-sum functions), chunk and warp records
+            // P4: sub-chunk records (exact fp32 running-sum functions) and warp records
             {
                 const double inv3 = ch.topp ? (double)ch.inv_s3 : 1.0;
                 uint32_t gb[4];
                 bool pred[4];
-                {
-                    double pre = P0;
 #pragma unroll
-                    for (int s = 0; s < 4; s++) {
-                        const float A0 = __double2float_rn(pre * inv3);
-                        pre = pre + subs[s];
-                        const float A1 = __double2float_rn((s == 3 ? P1 : pre) * inv3);
-                        const uint32_t e0 = fbits(A0) >> 23, e1 = fbits(A1) >> 23;
-                        pred[s] = A0 > 0.0f && e0 == e1 && e0 >= 1u && e0 <= 253u;
-                        gb[s] = (pred[s] ? e0 : 127u) << 23;
-                    }
+                for (int q = 0; q < 4; q++) {
+                    const float A0 = __double2float_rn(P0[q] * inv3);
+                    const float A1 = __double2float_rn(P1[q] * inv3);
+                    const uint32_t e0 = fbits(A0) >> 23, e1 = fbits(A1) >> 23;
+                    pred[q] = A0 > 0.0f && e0 == e1 && e0 >= 1u && e0 <= 253u;
+                    gb[q] = (pred[q] ? e0 : 127u) << 23;
                 }
                 float g0[4], g1[4];
-                bool anyq[4] = {false, false, false, false};
+                bool anyq[4];
 #pragma unroll
-                for (int s = 0; s < 4; s++) {
-                    g0[s] = bitsf(gb[s]);
-                    g1[s] = bitsf(gb[s] | 1u);
+                for (int q = 0; q < 4; q++) {
+                    g0[q] = bitsf(gb[q]);
+                    g1[q] = bitsf(gb[q] | 1u);
+                    anyq[q] = false;
                 }
                 float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride + slice0 : nullptr;
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals + cbase);
+#pragma unroll 2
+                for (int j = 0; j < NV4; j++) {
 #pragma unroll
-                for (int j = 0; j < NV; j++) {
-                    const float4 x = v4[j];
-                    const float e4[4] = {x.x, x.y, x.z, x.w};
+                    for (int q = 0; q < 4; q++) {
+                        const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
+                        const float e4[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-                    for (int c = 0; c < 4; c++) {
-                        const int el = 4 * j + c;
-                        const int s = el / SUB;
-                        const int li = cbase + el;
-                        const float q = q_of(ch, e4[c], slice0 + li);
-                        anyq[s] |= q != 0.0f;
-                        g0[s] = __fadd_rn(g0[s], q);
-                        g1[s] = __fadd_rn(g1[s], q);
-                        if (pr && li < slen) pr[li] = q;
+                        for (int c = 0; c < 4; c++) {
+                            const int li = kb[q] + 4 * j + c;
+                            const float qv = q_of(ch, e4[c], slice0 + li);
+                            anyq[q] |= qv != 0.0f;
+                            g0[q] = __fadd_rn(g0[q], qv);
+                            g1[q] = __fadd_rn(g1[q], qv);
+                            if (pr && li < slen) pr[li] = qv;
+                        }
                     }
                 }
-                // compose the four sub-chunks into the chunk record
-                int ctype = REC_IDENT, ce = 0;
-                uint32_t c0 = 0u, c1 = 0u;
-#pragma unroll
-                for (int s = 0; s < 4; s++) {
-                    if (!anyq[s]) continue;
-                    const uint32_t lim = gb[s] + (1u << 23);
-                    const bool ok = pred[s] && fbits(g0[s]) < lim && fbits(g1[s]) < lim;
-                    const int es = (int)(gb[s] >> 23);
-                    if (!ok || ctype == REC_MIXED || (ctype == REC_CLEAN && es != ce)) {
-                        ctype = REC_MIXED;
-                        continue;
-                    }
-                    const uint32_t m0 = fbits(g0[s]) - gb[s], m1 = fbits(g1[s]) - (gb[s] | 1u);
-                    if (ctype == REC_IDENT) {
-                        ctype = REC_CLEAN;
-                        ce = es;
-                        c0 = m0;
-                        c1 = m1;
+                WRec *recs = row_recs(a, row);
+                float *stash = row_stash(a, row);
+#pragma unroll 1
+                for (int q = 0; q < 4; q++) {
+                    const uint32_t lim = gb[q] + (1u << 23);
+                    const int ctype = !anyq[q] ? REC_IDENT
+                                               : ((pred[q] && fbits(g0[q]) < lim && fbits(g1[q]) < lim) ? REC_CLEAN : REC_MIXED);
+                    const int ce = (int)(gb[q] >> 23);
+                    const uint32_t c0 = fbits(g0[q]) - gb[q], c1 = fbits(g1[q]) - (gb[q] | 1u);
+                    // warp record over the 32 sub-chunks (q, 32*wid .. 32*wid+31)
+                    const unsigned cleanm = __ballot_sync(0xffffffffu, ctype == REC_CLEAN);
+                    const int e_first = cleanm ? __shfl_sync(0xffffffffu, ce, __ffs(cleanm) - 1) : 0;
+                    const unsigned nonconf =
+                        __ballot_sync(0xffffffffu, ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_first));
+                    int type, bchunk = -1, sfrom = 32, e_s = 0;
+                    uint32_t p0, p1, s0 = 0u, s1 = 0u;
+                    if (!nonconf) {
+                        uint32_t a0 = ctype == REC_CLEAN ? c0 : 0u, a1 = ctype == REC_CLEAN ? c1 : 0u;
+                        compose_scan(a0, a1);
+                        type = cleanm ? REC_CLEAN : REC_IDENT;
+                        p0 = __shfl_sync(0xffffffffu, a0, 31);
+                        p1 = __shfl_sync(0xffffffffu, a1, 31);
                     } else {
-                        const uint32_t x0 = c0, x1 = c1;
-                        c0 = x0 + ((x0 & 1u) ? m1 : m0);
-                        c1 = x1 + (((1u + x1) & 1u) ? m1 : m0);
+                        const int j = __ffs(nonconf) - 1;
+                        uint32_t a0 = (lane < j && ctype == REC_CLEAN) ? c0 : 0u;
+                        uint32_t a1 = (lane < j && ctype == REC_CLEAN) ? c1 : 0u;
+                        compose_scan(a0, a1);
+                        p0 = __shfl_sync(0xffffffffu, a0, 31);
+                        p1 = __shfl_sync(0xffffffffu, a1, 31);
+                        const int tj = __shfl_sync(0xffffffffu, ctype, j);
+                        // the suffix starts after a MIXED boundary sub-chunk, or at a CLEAN sub-chunk
+                        // j that already lies in the next binade
+                        sfrom = tj == REC_MIXED ? j + 1 : j;
+                        const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom && ctype == REC_CLEAN);
+                        e_s = sclean ? __shfl_sync(0xffffffffu, ce, __ffs(sclean) - 1) : 0;
+                        const unsigned sbad = __ballot_sync(
+                            0xffffffffu, lane >= sfrom && (ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_s)));
+                        uint32_t b0 = (lane >= sfrom && ctype == REC_CLEAN) ? c0 : 0u;
+                        uint32_t b1 = (lane >= sfrom && ctype == REC_CLEAN) ? c1 : 0u;
+                        compose_scan(b0, b1);
+                        s0 = __shfl_sync(0xffffffffu, b0, 31);
+                        s1 = __shfl_sync(0xffffffffu, b1, 31);
+                        type = sbad ? REC_MIXED : REC_PBS;
+                        bchunk = tj == REC_MIXED ? j : -1;
                     }
-                }
-                __syncthreads();  // the union area held the history table until now
-                rec_type[tid] = ctype;
-                rec_e[tid] = ce;
-                rec_n0[tid] = c0;
-                rec_n1[tid] = c1;
-                // warp record: prefix run, one boundary chunk, suffix run
-                const unsigned cleanm = __ballot_sync(0xffffffffu, ctype == REC_CLEAN);
-                const int e_first = cleanm ? __shfl_sync(0xffffffffu, ce, __ffs(cleanm) - 1) : 0;
-                const unsigned nonconf =
-                    __ballot_sync(0xffffffffu, ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_first));
-                WRec wr;
-                wr.slot = -1;
-                wr.pad[0] = wr.pad[1] = 0;
-                if (!nonconf) {
-                    uint32_t a0 = ctype == REC_CLEAN ? c0 : 0u, a1 = ctype == REC_CLEAN ? c1 : 0u;
-                    compose_scan(a0, a1);
-                    wr.type = cleanm ? REC_CLEAN : REC_IDENT;
-                    wr.e_pre = e_first;
-                    wr.p0 = __shfl_sync(0xffffffffu, a0, 31);
-                    wr.p1 = __shfl_sync(0xffffffffu, a1, 31);
-                    wr.bchunk = -1;
-                    wr.e_suf = 0;
-                    wr.s0 = wr.s1 = 0u;
-                    wr.sfrom = 32;
-                } else {
-                    const int j = __ffs(nonconf) - 1;
-                    uint32_t a0 = (lane < j && ctype == REC_CLEAN) ? c0 : 0u;
-                    uint32_t a1 = (lane < j && ctype == REC_CLEAN) ? c1 : 0u;
-                    compose_scan(a0, a1);
-                    const uint32_t p0 = __shfl_sync(0xffffffffu, a0, 31), p1 = __shfl_sync(0xffffffffu, a1, 31);
-                    const int tj = __shfl_sync(0xffffffffu, ctype, j);
-                    // the suffix starts after a MIXED boundary chunk, or at a CLEAN chunk j that
-                    // already lies in the next binade
-                    const int sfrom = tj == REC_MIXED ? j + 1 : j;
-                    const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom && ctype == REC_CLEAN);
-                    const int e_s = sclean ? __shfl_sync(0xffffffffu, ce, __ffs(sclean) - 1) : 0;
-                    const unsigned sbad = __ballot_sync(
-                        0xffffffffu, lane >= sfrom && (ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_s)));
-                    uint32_t b0 = (lane >= sfrom && ctype == REC_CLEAN) ? c0 : 0u;
-                    uint32_t b1 = (lane >= sfrom && ctype == REC_CLEAN) ? c1 : 0u;
-                    compose_scan(b0, b1);
-                    wr.type = sbad ? REC_MIXED : REC_PBS;
-                    wr.e_pre = e_first;
-                    wr.p0 = p0;
-                    wr.p1 = p1;
-                    wr.bchunk = tj == REC_MIXED ? j : -1;
-                    wr.e_suf = e_s;
-                    wr.s0 = __shfl_sync(0xffffffffu, b0, 31);
-                    wr.s1 = __shfl_sync(0xffffffffu, b1, 31);
-                    wr.sfrom = sfrom;
-                }
-                // boundary chunk probabilities -> a stash slot in CTA 0 (when one is free)
-                if (wr.type == REC_PBS && wr.bchunk >= 0) {
+                    // boundary sub-chunk probabilities -> a stash slot (when one is free)
                     int slot = -1;
+                    if (type == REC_PBS && bchunk >= 0) {
+                        if (lane == 0) {
+                            slot = atomicAdd(&hdr->nstash, 1);
+                            if (slot >= STASH_SLOTS) slot = -1;
+                        }
+                        slot = __shfl_sync(0xffffffffu, slot, 0);
+                        if (slot >= 0) {
+                            const int sb = (q * NT + 32 * wid + bchunk) * SUBT;
+                            float *qs = stash + slot * STASH_STRIDE;
+                            if (lane == 0) qs[0] = __int_as_float(slice0 + sb);
+                            for (int k = lane; k < SUBT; k += 32) qs[1 + k] = q_of(ch, vals[sb + k], slice0 + sb + k);
+                        } else if (timing) {
+                            dbg_add(DBG_STASH_MISS, 1);
+                        }
+                    }
                     if (lane == 0) {
-                        slot = atomicAdd(&remote_xs(0)->nstash, 1);
-                        if (slot >= STASH_SLOTS) slot = -1;
+                        WRec wr;
+                        wr.meta = pack_meta(type, bchunk, sfrom, e_first, e_s);
+                        wr.p0 = p0;
+                        wr.p1 = p1;
+                        wr.s0 = s0;
+                        wr.s1 = s1;
+                        wr.slot = slot;
+                        recs[rank * 4 * NW + q * NW + wid] = wr;
+                        if (type == REC_PBS && timing) dbg_add(DBG_PBS, 1);
                     }
-                    slot = __shfl_sync(0xffffffffu, slot, 0);
-                    wr.slot = slot;
-                    if (slot >= 0) {
-                        float *qs = cluster.map_shared_rank(qstash, 0) + slot * LT;
-                        const int cb0 = (wid * 32 + wr.bchunk) * LT;
-                        for (int k = lane; k < LT; k += 32) qs[k] = q_of(ch, vals[cb0 + k], slice0 + cb0 + k);
-                    } else if (timing) {
-                        dbg_add(DBG_STASH_MISS, 1);
-                    }
-                }
-                if (lane == 0) {
-                    if (wr.type == REC_PBS && timing) dbg_add(DBG_PBS, 1);
-                    WRec *dst = cluster.map_shared_rank(wstash, 0) + rank * NW + wid;
-                    *dst = wr;
                 }
             }
             mark(DBG_P4);
-            cluster.sync();  // ---- #5 records visible to the walker
-            mark(DBG_W5);
-
-            if (rank == 0 && wid == 0) {
-                uint32_t cb = 0u;  // running sum, starts at +0.0f
-                int res = -1;
-                const int total_w = C * NW;
-                // chunk-level walk of warp record gw (chunk records read from their CTA), from
-                // chunk `from` on
-                auto walk_chunks = [&](int gw, int from, uint32_t &cbv) -> int {
-                    if (lane == 0) dbg_add(DBG_EXPAND, 1);
-                    const int rr = gw / NW, w = gw % NW;
-                    const int *rt = cluster.map_shared_rank(rec_type, rr);
-                    const int *re = cluster.map_shared_rank(rec_e, rr);
-                    const uint32_t *r0 = cluster.map_shared_rank(rec_n0, rr);
-                    const uint32_t *r1 = cluster.map_shared_rank(rec_n1, rr);
-                    const float *rv = cluster.map_shared_rank(vals, rr);
-                    const int t2 = rt[w * 32 + lane], e2 = re[w * 32 + lane];
-                    const uint32_t a2 = r0[w * 32 + lane], b2 = r1[w * 32 + lane];
-                    auto expandB = [&](int jj, uint32_t &cbx) -> int {
-                        const int lb = (w * 32 + jj) * LT;
-                        return replay_elems(LT, rr * S + lb, cbx, r,
-                                            [&](int k) { return q_of(ch, rv[lb + k], rr * S + lb + k); });
-                    };
-                    int pos2 = from, rs2 = -1;
-                    while (pos2 < 32 && rs2 == -1) rs2 = walk_step(32, pos2, t2, e2, a2, b2, cbv, r, expandB);
-                    return rs2;
-                };
-                for (int gw0 = 0; gw0 < total_w && res == -1; gw0 += 32) {
-                    const int n = min(32, total_w - gw0);
-                    WRec wl = {};
-                    wl.type = REC_IDENT;
-                    if (lane < n) wl = wstash[gw0 + lane];
-                    // a PBS record is applied in three pieces; whatever does not apply is walked
-                    // chunk by chunk
-                    auto expandA = [&](int j, uint32_t &cbv) -> int {
-                        const int gw = gw0 + j;
-                        const int ty = __shfl_sync(0xffffffffu, wl.type, j);
-                        if (ty == REC_PBS) {
-                            const int ep = __shfl_sync(0xffffffffu, wl.e_pre, j);
-                            const uint32_t p0 = __shfl_sync(0xffffffffu, wl.p0, j);
-                            const uint32_t p1 = __shfl_sync(0xffffffffu, wl.p1, j);
-                            const int bc = __shfl_sync(0xffffffffu, wl.bchunk, j);
-                            const int es = __shfl_sync(0xffffffffu, wl.e_suf, j);
-                            const uint32_t s0 = __shfl_sync(0xffffffffu, wl.s0, j);
-                            const uint32_t s1 = __shfl_sync(0xffffffffu, wl.s1, j);
-                            const int slot = __shfl_sync(0xffffffffu, wl.slot, j);
-                            const int sfrom = __shfl_sync(0xffffffffu, wl.sfrom, j);
-                            uint32_t c = cbv;
-                            if (apply_run(c, ep, p0, p1) && !(r < bitsf(c))) {
-                                if (bc >= 0) {
-                                    const int rr = gw / NW, w = gw % NW;
-                                    const int lb = (w * 32 + bc) * LT;
-                                    int found;
-                                    if (slot >= 0) {
-                                        const float *qs = qstash + slot * LT;
-                                        found = replay_elems(LT, rr * S + lb, c, r, [&](int k) { return qs[k]; });
-                                    } else {
-                                        const float *rv = cluster.map_shared_rank(vals, rr);
-                                        found = replay_elems(LT, rr * S + lb, c, r,
-                                                             [&](int k) { return q_of(ch, rv[lb + k], rr * S + lb + k); });
-                                    }
-                                    if (found != -1) return found;
-                                }
-                                uint32_t c2 = c;
-                                if (apply_run(c2, es, s0, s1) && !(r < bitsf(c2))) {
-                                    cbv = c2;
-                                    return -1;
-                                }
-                                cbv = c;
-                                return walk_chunks(gw, sfrom, cbv);
-                            }
-                        }
-                        return walk_chunks(gw, 0, cbv);
-                    };
-                    const int ty = wl.type == REC_PBS ? REC_MIXED : wl.type;
-                    int pos = 0;
-                    while (pos < n && res == -1) res = walk_step(n, pos, ty, wl.e_pre, wl.p0, wl.p1, cb, r, expandA);
-                }
-                if (res == -2) rowflags |= ROW_ERR_WALK;
-                token = res >= 0 ? res : last_idx;
-            }
-            mark(DBG_WALK);
         }
 
     row_done:
-        if (rank == 0 && tid == 0) {
+        if (done && rank == 0 && tid == 0) {
             if (token < 0) token = 0;
             a.token[row] = token + a.vocab_offset;
             if (a.status) a.status[row] = rowflags;
+            hdr->done = 1;
         }
         mark(DBG_TOPK);
         fence_proxy_async();  // order this row's generic accesses of the slice before the next bulk copy
         cluster.sync();       // ---- end of row: peers may reuse their shared memory
         mark(DBG_WEND);
+    }
+}
+
+// ----------------------------------------------------------------------------------------
+// kernel B: one warp per row draws with the exact fp32 running sum
+
+template <int DT, int SUBT>
+__global__ void __launch_bounds__(WALK_WARPS * 32) walk_rows_kernel(const KernelArgs a) {
+    __shared__ int hls[WALK_WARPS][HLIST];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int row = blockIdx.x * WALK_WARPS + wid;
+    if (threadIdx.x == 0) g_dbg = a.dbg;
+    __syncthreads();
+    if (row >= a.rows) return;
+    const RowHdr h = *row_hdr(a, row);
+    if (h.done) return;
+    const long long t_start = clock64();
+    const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
+    Chain ch;
+    ch.inv_sum = h.inv_sum;
+    ch.min_p = h.min_p;
+    ch.inv_s2 = h.inv_s2;
+    ch.inv_s3 = h.inv_s3;
+    ch.cut_idx = h.cut_idx;
+    ch.minp = h.minp;
+    ch.nokept = h.nokept;
+    ch.topp = h.topp;
+    const float r = h.r;
+    const int C = a.cluster, NW = a.nrec / (4 * C), NT = NW * 32, S = a.S, V = a.vocab;
+    const bool use_hist = a.hist_ids && a.hist_off &&
+                          (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
+    const float inv_rep = __fdiv_rn(1.0f, p.repetition);
+    const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
+    const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
+    int *hl = hls[wid];
+    int nh = 0;
+    bool hist_overflow = false;
+
+    // history ids that fall in [lo, hi) (local indices) -> this warp's list
+    auto load_region_hist = [&](int lo, int hi) {
+        nh = 0;
+        hist_overflow = false;
+        if (!use_hist) return;
+        const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+        for (int64_t j0 = h0; j0 < h1; j0 += 32) {
+            const int64_t j = j0 + lane;
+            int li = -1;
+            if (j < h1) {
+                const int id = a.hist_ids[j];
+                if (id >= 0 && id < a.vocab_total) li = id - a.vocab_offset;
+            }
+            const bool in = li >= lo && li < hi;
+            const unsigned m = __ballot_sync(0xffffffffu, in);
+            if (in) {
+                const int o = nh + __popc(m & ((1u << lane) - 1u));
+                if (o < HLIST) hl[o] = li;
+            }
+            nh += __popc(m);
+        }
+        __syncwarp();
+        if (nh > HLIST) hist_overflow = true;
+    };
+    // draw probability of element li, recomputed from the row's inputs
+    auto qval = [&](int li) -> float {
+        if (li >= V) return 0.0f;
+        float v;
+        if (DT == DLLM_DTYPE_F32)
+            v = ((const float *)a.logits)[(int64_t)row * a.row_stride + li];
+        else
+            v = bitsf((uint32_t)((const unsigned short *)a.logits)[(int64_t)row * a.row_stride + li] << 16);
+        if (mrow && !((mrow[li >> 5] >> (li & 31)) & 1u)) v = -INFINITY;
+        if (use_hist && nh > 0) {
+            int c = 0;
+            if (!hist_overflow) {
+                for (int i = 0; i < nh; i++) c += hl[i] == li;
+            } else {
+                const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+                for (int64_t j = h0; j < h1; j++) c += a.hist_ids[j] - a.vocab_offset == li && a.hist_ids[j] >= 0 &&
+                                                         a.hist_ids[j] < a.vocab_total;
+            }
+            if (c > 0) {
+                if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
+                if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
+                if (p.repetition > 1.0f)
+                    for (int k = 0; k < c; k++) {
+                        if (v < 0.0f) v = __fmul_rn(v, p.repetition);
+                        else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
+                    }
+            }
+        }
+        const float e = expf(__fsub_rn(__fmul_rn(__fsub_rn(v, h.M), h.inv_temp), h.mv));
+        return q_of(ch, e, li);
+    };
+    // replays elements [start, start + n) on the exact running sum, recomputing them
+    auto replay_region = [&](int start, int n, uint32_t &cbv) -> int {
+        if (lane == 0) dbg_add(DBG_RECOMP, 1);
+        load_region_hist(start, start + n);
+        for (int g = 0; g < n; g += 256) {
+            const int m = min(256, n - g);
+            const int res = replay_elems(m, start + g, cbv, r, [&](int j) { return qval(start + g + j); });
+            if (res != -1) return res;
+        }
+        return -1;
+    };
+
+    const WRec *recs = row_recs(a, row);
+    const float *stash = row_stash(a, row);
+    uint32_t cb = 0u;  // running sum, starts at +0.0f
+    int res = -1;
+    for (int gw0 = 0; gw0 < a.nrec && res == -1; gw0 += 32) {
+        const int n = min(32, a.nrec - gw0);
+        WRec wl;
+        wl.meta = REC_IDENT;
+        wl.p0 = wl.p1 = wl.s0 = wl.s1 = 0u;
+        wl.slot = -1;
+        if (lane < n) wl = recs[gw0 + lane];
+        const int ty = (int)(wl.meta & 3u);
+        const int ep = (int)((wl.meta >> 16) & 255u);
+        auto expandA = [&](int j, uint32_t &cbv) -> int {
+            if (lane == 0) dbg_add(DBG_EXPAND, 1);
+            const int g = gw0 + j;
+            const int rr = g / (4 * NW), kk = g % (4 * NW), q = kk / NW, w = kk % NW;
+            const int start = rr * S + (q * NT + 32 * w) * SUBT;
+            const uint32_t meta = __shfl_sync(0xffffffffu, wl.meta, j);
+            if ((int)(meta & 3u) == REC_PBS) {
+                const int bc = (int)((meta >> 2) & 63u);
+                const int sfrom = (int)((meta >> 8) & 63u);
+                const int epre = (int)((meta >> 16) & 255u), esuf = (int)(meta >> 24);
+                const uint32_t p0 = __shfl_sync(0xffffffffu, wl.p0, j), p1 = __shfl_sync(0xffffffffu, wl.p1, j);
+                const uint32_t s0 = __shfl_sync(0xffffffffu, wl.s0, j), s1 = __shfl_sync(0xffffffffu, wl.s1, j);
+                const int slot = __shfl_sync(0xffffffffu, wl.slot, j);
+                uint32_t c = cbv;
+                if (apply_run(c, epre, p0, p1) && !(r < bitsf(c))) {
+                    if (bc != 63) {
+                        int found;
+                        if (slot >= 0) {
+                            const float *qs = stash + slot * STASH_STRIDE;
+                            found = replay_elems(SUBT, __float_as_int(qs[0]), c, r, [&](int k) { return qs[1 + k]; });
+                        } else {
+                            found = replay_region(start + bc * SUBT, SUBT, c);
+                        }
+                        if (found != -1) return found;
+                    }
+                    uint32_t c2 = c;
+                    if (apply_run(c2, esuf, s0, s1) && !(r < bitsf(c2))) {
+                        cbv = c2;
+                        return -1;
+                    }
+                    cbv = c;
+                    return replay_region(start + sfrom * SUBT, (32 - sfrom) * SUBT, cbv);
+                }
+            }
+            return replay_region(start, 32 * SUBT, cbv);
+        };
+        const int tyw = ty == REC_PBS ? REC_MIXED : ty;
+        int pos = 0;
+        while (pos < n && res == -1) res = walk_step(n, pos, tyw, ep, wl.p0, wl.p1, cb, r, expandA);
+    }
+    if (lane == 0) {
+        int flags = h.flags;
+        if (res == -2) flags |= ROW_ERR_WALK;
+        a.token[row] = (res >= 0 ? res : h.last_idx) + a.vocab_offset;
+        if (a.status) a.status[row] = flags;
+        dbg_add(DBG_WALK_CYC, (unsigned long long)(clock64() - t_start));
     }
 }
 

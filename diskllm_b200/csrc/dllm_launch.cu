@@ -10,31 +10,32 @@ namespace dllm {
 static unsigned long long *g_host_dbg = nullptr;  // device counters for KernelArgs::dbg
 static int g_sm_count = 0;
 
-static const int kLTs[] = {20, 36, 52, 68, 84, 100, 116, 132};
+static const int kSUBs[] = {4, 12, 20, 28, 36, 44, 52, 60};
 
-// one getter per instantiation, defined in dllm_kernel_inst.cu (compiled once per chunk length)
-#define DLLM_DECL(L) KernelFn kernel_f32_##L(); KernelFn kernel_bf16_##L();
-DLLM_DECL(20) DLLM_DECL(36) DLLM_DECL(52) DLLM_DECL(68) DLLM_DECL(84) DLLM_DECL(100) DLLM_DECL(116) DLLM_DECL(132)
+// getters per instantiation, defined in dllm_kernel_inst.cu (compiled once per sub-chunk length)
+#define DLLM_DECL(L) KernelFn kernel_a_f32_##L(); KernelFn kernel_a_bf16_##L(); \
+    KernelFn kernel_b_f32_##L(); KernelFn kernel_b_bf16_##L();
+DLLM_DECL(4) DLLM_DECL(12) DLLM_DECL(20) DLLM_DECL(28) DLLM_DECL(36) DLLM_DECL(44) DLLM_DECL(52) DLLM_DECL(60)
 #undef DLLM_DECL
 
-static KernelFn kernel_for(int dtype, int LT) {
+// which = 0: the cluster kernel, 1: the walk kernel
+static KernelFn kernel_for(int dtype, int SUB, int which = 0) {
     const bool bf = dtype == DLLM_DTYPE_BF16;
-    switch (LT) {
-#define DLLM_CASE(L) case L: return bf ? kernel_bf16_##L() : kernel_f32_##L();
-        DLLM_CASE(20) DLLM_CASE(36) DLLM_CASE(52) DLLM_CASE(68) DLLM_CASE(84) DLLM_CASE(100) DLLM_CASE(116) DLLM_CASE(132)
+    switch (SUB) {
+#define DLLM_CASE(L) case L: return which ? (bf ? kernel_b_bf16_##L() : kernel_b_f32_##L()) \
+                                          : (bf ? kernel_a_bf16_##L() : kernel_a_f32_##L());
+        DLLM_CASE(4) DLLM_CASE(12) DLLM_CASE(20) DLLM_CASE(28) DLLM_CASE(36) DLLM_CASE(44) DLLM_CASE(52) DLLM_CASE(60)
 #undef DLLM_CASE
         default: return nullptr;
     }
 }
 
-static size_t union_bytes(int NT, int C, int LT, int htab, int cand_entries) {
-    size_t u = (size_t)8 * htab;
-    // chunk records + (CTA 0) the cluster's warp records + stash of boundary chunks
-    const size_t recs = (size_t)16 * NT + sizeof(WRec) * (size_t)C * (NT / 32) + (size_t)4 * STASH_SLOTS * LT;
-    u = u > recs ? u : recs;
-    const size_t cb = (size_t)8 * cand_entries;
+static size_t union_bytes(int htab, int cand_entries) {
+    const size_t u = (size_t)8 * htab, cb = (size_t)8 * cand_entries;
     return u > cb ? u : cb;
 }
+
+int nrec_for(const LaunchCfg &cfg) { return 4 * (cfg.threads / 32) * cfg.cluster; }
 
 static cudaError_t set_attrs(KernelFn fn, size_t smem) {
     cudaError_t e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -83,47 +84,47 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
     }
     // top-k: survivor sort buffer plus the final list
     const int cand_entries = topk_bound > 0 ? CAND_CAP + 2 * pow2_at_least(topk_bound) : 0;
-    // DLLM_FORCE_CFG="C,NT[,L]" pins the cluster size / block size / chunk (tuning)
+    // DLLM_FORCE_CFG="C,NT[,SUB]" pins the cluster size / block size / sub-chunk (tuning)
     int force_c = 0, force_nt = 0, force_l = 0;
     if (const char *f = getenv("DLLM_FORCE_CFG")) sscanf(f, "%d,%d,%d", &force_c, &force_nt, &force_l);
-    static const int Cs[] = {1, 2, 4, 8, 12, 16};
-    static const int NTs[] = {128, 192, 256, 384, 512};
+    static const int Cs[] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16};
+    static const int NTs[] = {128, 160, 192, 224, 256, 320, 384, 448, 512};
     double best = 1e300;
     LaunchCfg bc = {};
     for (int C : Cs) {
         for (int NT : NTs) {
             if (force_c && (C != force_c || (force_nt && NT != force_nt))) continue;
-            const int per = (vocab + C * NT - 1) / (C * NT);
+            const int per = (vocab + 4 * C * NT - 1) / (4 * C * NT);  // elements per sub-chunk
             int L = -1;
-            for (int lt : kLTs)
+            for (int lt : kSUBs)
                 if (lt >= per && (!force_l || lt == force_l)) {
                     L = lt;
                     break;
                 }
             if (L < 0) continue;
-            const int S = NT * L;
+            const int S = 4 * NT * L;
             if ((long long)S * (C - 1) >= vocab && C > 1) continue;  // an idle CTA
             int hb = hist_bound < S ? hist_bound : S;
             int htab = pow2_at_least(2 * (hb > 16 ? hb : 16));
             if (htab > 16384) htab = 16384;
-            const size_t smem = (size_t)S * 4 + union_bytes(NT, C, L, htab, cand_entries);
+            const size_t smem = (size_t)S * 4 + union_bytes(htab, cand_entries);
             if (smem > 220 * 1024) continue;
             KernelFn fn = kernel_for(dtype, L);
             const int nact = active_clusters(fn, C, NT, smem);
             if (nact <= 0) continue;
             // cost: padded work x idle-SM factor, a penalty when only one CTA fits per SM (no
-            // overlap of one row's serial phases with another row's streaming), and a term for
-            // short chunks (more records for the draw walk)
+            // overlap of one row's latency-bound phases with another row's streaming), and a
+            // term for short sub-chunks (more warp records for the walk)
             const double pad = (double)S * C / vocab;
             const double used = (double)nact * C;
             const double under = used >= g_sm_count ? 1.0 : (double)g_sm_count / used;
             const double per_sm = used / g_sm_count;
-            const double cost = pad * under * (per_sm >= 2.0 ? 1.0 : 1.3) * (1.0 + 24.0 / L);
+            const double cost = pad * under * (per_sm >= 2.0 ? 1.0 : 1.3) * (1.0 + 4.0 / L);
             if (cost < best) {
                 best = cost;
                 bc.cluster = C;
                 bc.threads = NT;
-                bc.L = L;
+                bc.SUB = L;
                 bc.S = S;
                 bc.htab = htab;
                 bc.smem = smem;
@@ -133,8 +134,8 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
     }
     if (best >= 1e299) return DLLM_ERR_UNSUPPORTED;
     if (getenv("DLLM_VERBOSE"))
-        fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d L %d S %d htab %d smem %zu clusters %d\n",
-                vocab, dtype, bc.cluster, bc.threads, bc.L, bc.S, bc.htab, bc.smem, bc.max_clusters);
+        fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d SUB %d S %d htab %d smem %zu clusters %d\n",
+                vocab, dtype, bc.cluster, bc.threads, bc.SUB, bc.S, bc.htab, bc.smem, bc.max_clusters);
     *cfg = bc;
     return DLLM_OK;
 }
@@ -146,8 +147,9 @@ dllm_status set_debug_counters(unsigned long long *dev_counters) {
 
 dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream) {
     if (a.rows == 0) return DLLM_OK;
-    KernelFn fn = kernel_for(a.dtype, cfg.L);
-    if (!fn) return DLLM_ERR_UNSUPPORTED;
+    KernelFn fn = kernel_for(a.dtype, cfg.SUB);
+    KernelFn fnb = kernel_for(a.dtype, cfg.SUB, 1);
+    if (!fn || !fnb) return DLLM_ERR_UNSUPPORTED;
     cudaError_t e = set_attrs(fn, cfg.smem);
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
     const int ncl = a.rows < cfg.max_clusters ? a.rows : cfg.max_clusters;
@@ -166,6 +168,11 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     KernelArgs args = a;
     args.dbg = g_host_dbg;
     e = cudaLaunchKernelEx(&lc, fn, args);
+    if (e != cudaSuccess) return DLLM_ERR_CUDA;
+    // the walk kernel: one warp per row, after the cluster kernel on the same stream
+    const int wb = (a.rows + WALK_WARPS - 1) / WALK_WARPS;
+    fnb<<<wb, WALK_WARPS * 32, 0, stream>>>(args);
+    e = cudaGetLastError();
     return e == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
 }
 

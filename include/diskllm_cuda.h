@@ -102,6 +102,11 @@ typedef struct {
     int32_t *topk_ids;        /* optional [rows][topk_stride] out: the top-k ids, best first
                                  (rows where top-k is active) */
     int64_t topk_stride;
+
+    void *workspace;          /* optional device scratch of >= dllm_cuda_workspace_bytes()
+                                 bytes (256-byte aligned); NULL: the library keeps one
+                                 buffer per (device, stream) and grows it with cudaMalloc */
+    size_t workspace_bytes;
 } dllm_batch_desc;
 
 /* per-row status bits */
@@ -117,6 +122,10 @@ typedef struct {
  *   sampler_apply_repetition_penalty -> sampler_sample.
  * Row i draws with uniforms[i] where the reference draws rand_f32 (src/sampler.c:225). */
 DLLM_API dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *desc, void *stream);
+
+/* Scratch the sampler needs for this descriptor (per-row headers, warp-level draw
+ * records and stashed probabilities; about 16 KB per row).  0 on invalid descriptors. */
+DLLM_API size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *desc);
 
 /* Diagnostics: when given a device array of 32 zeroed unsigned 64-bit counters, the sampler
  * kernels accumulate per-phase cycle counts of each cluster's first CTA and draw-walk
