@@ -32,7 +32,7 @@ ROW_ERR_TIMEOUT = 16
 # every symbol the public headers declare
 EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
-    "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes",
+    "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
     "dllm_sampler_get_rng_state", "dllm_sampler_set_rng_state",
     "sampler_create", "sampler_free", "sampler_apply_repetition_penalty",
     "sampler_apply_presence_penalty", "sampler_sample", "greedy_sample",
@@ -113,6 +113,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_sample_batch.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
     lib.dllm_cuda_set_debug_counters.restype = C.c_int
     lib.dllm_cuda_set_debug_counters.argtypes = [C.c_void_p]
+    lib.dllm_cuda_sample_batch_static.restype = C.c_int
+    lib.dllm_cuda_sample_batch_static.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
     lib.dllm_cuda_workspace_bytes.restype = C.c_size_t
     lib.dllm_cuda_workspace_bytes.argtypes = [C.POINTER(BatchDesc)]
     lib.dllm_cuda_version.restype = C.c_char_p
@@ -289,6 +291,21 @@ def sample_batch(logits, uniforms, params=None, *, stream=None, check=True, **kw
         raise DllmError(f"dllm_cuda_sample_batch: {STATUS_NAMES.get(rc, rc)} "
                         f"({load_library().dllm_cuda_last_error().decode()})")
     return token
+
+
+def sample_batch_static(logits, uniforms, params=None, *, stream=None, check=True, **kw):
+    """Calls dllm_cuda_sample_batch_static: the same sampling with the library's fixed scratch
+    array instead of any allocation.  Returns (token tensor, status code)."""
+    import torch
+
+    d, token = fill_desc(logits, uniforms, params, **kw)
+    if stream is None:
+        stream = torch.cuda.current_stream(logits.device).cuda_stream
+    rc = load_library().dllm_cuda_sample_batch_static(C.byref(d), C.c_void_p(stream))
+    if check and rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_sample_batch_static: {STATUS_NAMES.get(rc, rc)} "
+                        f"({load_library().dllm_cuda_last_error().decode()})")
+    return token, rc
 
 
 def params_array(rows_params, device):

@@ -27,6 +27,10 @@ static void set_error(const char *what, cudaError_t e) {
 
 extern "C" const char *dllm_cuda_last_error(void) { return g_last_error; }
 
+namespace dllm {
+void set_last_error_message(const char *msg) { snprintf(g_last_error, sizeof g_last_error, "%s", msg); }
+}  // namespace dllm
+
 extern "C" dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters) {
     return set_debug_counters(device_counters);
 }

@@ -127,6 +127,21 @@ DLLM_API dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *desc, void *s
  * records and stashed probabilities; about 16 KB per row).  0 on invalid descriptors. */
 DLLM_API size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *desc);
 
+/* Allocation-free variant of dllm_cuda_sample_batch; it has no counterpart in the reference.
+ * For callers that cannot call cudaMalloc -- an embedder whose device memory is all owned by
+ * its own allocator, or a decode loop that must not stall on the device-wide synchronisation
+ * of cudaMalloc/cudaFree.  Instead of a caller buffer or a library-grown one, it uses a
+ * 16 MiB scratch array compiled into the library (held on every GPU that loads the library
+ * until the process exits); desc->workspace is ignored.  Batches whose
+ * dllm_cuda_workspace_bytes() exceeds 16 MiB (about 1,200 rows of vocab 256000) are rejected
+ * with DLLM_ERR_UNSUPPORTED and a message in dllm_cuda_last_error().  The first call on a
+ * device looks up the array's device address and picks the launch configuration, so make it
+ * before any stream capture.  Every call shares the one array: calls whose work overlaps on the
+ * GPU (other streams, other host threads) race and must be serialised by the caller.  The
+ * kernels write every scratch field before reading it, so leftover contents from an earlier
+ * call need no clearing. */
+DLLM_API dllm_status dllm_cuda_sample_batch_static(const dllm_batch_desc *desc, void *stream);
+
 /* Diagnostics: when given a device array of 32 zeroed unsigned 64-bit counters, the sampler
  * kernels accumulate per-phase cycle counts of each cluster's first CTA and draw-walk
  * statistics into it; NULL switches it off.  No effect on results. */
