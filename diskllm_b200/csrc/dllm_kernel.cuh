@@ -47,6 +47,7 @@
 #pragma once
 #include <cooperative_groups.h>
 #include <cuda_bf16.h>
+#include <cuda/std/type_traits>
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -93,6 +94,7 @@ enum : int {
     DBG_P4 = 7, DBG_WEND = 10, DBG_TOPK = 11, DBG_LOADWAIT = 12,
     DBG_ROWS = 16, DBG_REPLAY = 17, DBG_EXPAND = 18, DBG_STEPS = 19, DBG_REPLAY_IT = 20,
     DBG_PBS = 21, DBG_STASH_MISS = 22, DBG_TOPK_FALLBACK = 23, DBG_RECOMP = 24, DBG_WALK_CYC = 25,
+    DBG_P2L = 13, DBG_P3L = 14, DBG_P3S = 15, DBG_P4L = 26, DBG_MAXP = 27,
 };
 __device__ __forceinline__ void dbg_add(int k, unsigned long long v) {
     if (g_dbg) atomicAdd(g_dbg + k, v);
@@ -142,18 +144,23 @@ struct Shared {
     int bcast_i[4];
 };
 
-// compensated fp32 sum (TwoSum per add): s + c carries ~48 bits
+// Compensated fp32 sum of values in [0, 1]: the running sum starts at CSUM_BASE (2.0), so it is
+// never below the next addend and Fast2Sum (t = s + x; err = x - (t - s)) recovers each
+// rounding error exactly; s + c - CSUM_BASE carries ~48 bits.
+constexpr float CSUM_BASE = 2.0f;
 struct CSum {
     float s, c;
 };
+__device__ __forceinline__ CSum csum_zero() { return CSum{CSUM_BASE, 0.0f}; }
 __device__ __forceinline__ void csum_add(CSum &a, float x) {
     const float t = __fadd_rn(a.s, x);
-    const float z = __fsub_rn(t, a.s);
-    const float e = __fadd_rn(__fsub_rn(a.s, __fsub_rn(t, z)), __fsub_rn(x, z));
+    const float err = __fsub_rn(x, __fsub_rn(t, a.s));
     a.s = t;
-    a.c = __fadd_rn(a.c, e);
+    a.c = __fadd_rn(a.c, err);
 }
-__device__ __forceinline__ double csum_val(const CSum &a) { return (double)a.s + (double)a.c; }
+__device__ __forceinline__ double csum_val(const CSum &a) {
+    return ((double)a.s - (double)CSUM_BASE) + (double)a.c;
+}
 
 __device__ __forceinline__ uint32_t fbits(float x) { return __float_as_uint(x); }
 __device__ __forceinline__ float bitsf(uint32_t b) { return __uint_as_float(b); }
@@ -205,7 +212,7 @@ __device__ __forceinline__ T warp_allreduce(T v, Op op) {
 }
 
 template <class T, class Op>
-__device__ T block_allreduce(T v, T *scratch, Op op) {
+__device__ __forceinline__ T block_allreduce(T v, T *scratch, Op op) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     v = warp_allreduce(v, op);
     __syncthreads();
@@ -218,7 +225,7 @@ __device__ T block_allreduce(T v, T *scratch, Op op) {
 
 // Exclusive / inclusive scan of doubles in thread order.  excl(t+1) is bit-identical to
 // incl(t), and the returned total is bit-identical to incl(last).
-__device__ void block_scan_d(double v, double *scratch, double &excl, double &incl, double &total) {
+__device__ __forceinline__ void block_scan_d(double v, double *scratch, double &excl, double &incl, double &total) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     double x = v;
 #pragma unroll
@@ -239,7 +246,7 @@ __device__ void block_scan_d(double v, double *scratch, double &excl, double &in
     total = tot;
 }
 
-__device__ void block_scan_i(int v, int *scratch, int &excl, int &total) {
+__device__ __forceinline__ void block_scan_i(int v, int *scratch, int &excl, int &total) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int x = v;
 #pragma unroll
@@ -606,7 +613,7 @@ __device__ void load_slice_bf16(const KernelArgs &a, int row, int slice0, int sl
 
 // Exclusive / inclusive scan of four doubles per thread (one per quarter), in thread order;
 // same bit-consistency as block_scan_d for each of the four.
-__device__ void block_scan4_d(const double v[4], double *scratch, double excl[4], double incl[4], double tot[4]) {
+__device__ __forceinline__ void block_scan4_d(const double v[4], double *scratch, double excl[4], double incl[4], double tot[4]) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     double x[4], prev[4];
 #pragma unroll
@@ -638,7 +645,7 @@ __device__ void block_scan4_d(const double v[4], double *scratch, double excl[4]
 
 // Exclusive scan of four ints per thread in (quarter, thread) order; returns per-quarter
 // offsets already including the totals of earlier quarters.
-__device__ void block_scan4_i(const int v[4], int *scratch, int excl[4], int &total) {
+__device__ __forceinline__ void block_scan4_i(const int v[4], int *scratch, int excl[4], int &total) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int x[4];
 #pragma unroll
@@ -672,6 +679,36 @@ __device__ void block_scan4_i(const int v[4], int *scratch, int excl[4], int &to
 __device__ __forceinline__ uint32_t pack_meta(int type, int bchunk, int sfrom, int e_pre, int e_suf) {
     return (uint32_t)type | ((uint32_t)(bchunk < 0 ? 63 : bchunk) << 2) | ((uint32_t)sfrom << 8) |
            ((uint32_t)(e_pre & 255) << 16) | ((uint32_t)(e_suf & 255) << 24);
+}
+
+// P4 element loop: the draw probability of every element of the four sub-chunks, added into
+// two fp32 chains per sub-chunk (started at 2^e and 2^e + ulp); qmax[q] > 0 iff any is nonzero
+template <class T>
+__device__ __forceinline__ T pick4(const T (&v)[4], int q) {
+    return q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
+}
+
+template <bool MINP, int NV4>
+__device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], const int (&lim)[4], const Chain &ch,
+                                        float scale3, float (&g0)[4], float (&g1)[4], float (&qmax)[4]) {
+#pragma unroll 2
+    for (int j = 0; j < NV4; j++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
+            const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float w = __fmul_rn(e4[c], ch.inv_sum);
+                if (MINP) w = (ch.nokept || w >= ch.min_p) ? __fmul_rn(w, ch.inv_s2) : 0.0f;
+                float qv = __fmul_rn(w, scale3);
+                qv = (4 * j + c <= lim[q]) ? qv : 0.0f;
+                qmax[q] = fmaxf(qmax[q], qv);
+                g0[q] = __fadd_rn(g0[q], qv);
+                g1[q] = __fadd_rn(g1[q], qv);
+            }
+        }
+    }
 }
 
 // ----------------------------------------------------------------------------------------
@@ -837,6 +874,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
             }
         }
+        mark(DBG_MAXP);
         const float mraw = block_allreduce(lmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
 
         // ---------------- P1: penalties ----------------------------------------------------------
@@ -1179,7 +1217,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             double ds;
             {
                 float4 *v4 = reinterpret_cast<float4 *>(vals);
-                CSum c0 = {0.0f, 0.0f}, c1 = {0.0f, 0.0f};
+                CSum c0 = csum_zero(), c1 = csum_zero();
 #pragma unroll 2
                 for (int i = tid; i < S / 4; i += NT) {
                     float4 x = v4[i];
@@ -1195,15 +1233,18 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
                 ds = csum_val(c0) + csum_val(c1);
             }
+            mark(DBG_P2L);
             ds = block_allreduce(ds, sh.red_d, [](double x, double y) { return x + y; });
             if (tid == 0) sh.xs.dsum = ds;
             mark(DBG_P2);
             cluster.sync();  // ---- #2
             mark(DBG_W2);
+            // peers' values read in parallel (lane rr reads CTA rr), folded in rank order
             double sum = 0.0;
-            if (lane == 0)
-                for (int rr = 0; rr < C; rr++) sum = sum + remote_xs(rr)->dsum;
-            sum = __shfl_sync(0xffffffffu, sum, 0);
+            {
+                const double x = lane < C ? remote_xs(lane)->dsum : 0.0;
+                for (int rr = 0; rr < C; rr++) sum = sum + __shfl_sync(0xffffffffu, x, rr);
+            }
 
             Chain ch;
             ch.inv_sum = __double2float_rn(1.0 / sum);
@@ -1216,7 +1257,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             ch.cut_idx = INT_MAX;
 
             if (ch.minp) {
-                CSum s2c = {0.0f, 0.0f}, sac = {0.0f, 0.0f};
+                CSum s2c = csum_zero(), sac = csum_zero();
                 int nk = 0;
                 for (int i = tid; i < S; i += NT) {
                     const float pp = __fmul_rn(vals[i], ch.inv_sum);
@@ -1237,17 +1278,16 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 cluster.sync();  // ---- min-p
                 double S2 = 0.0, SA = 0.0;
                 int NK = 0;
-                if (lane == 0) {
+                {
+                    Xch *x = remote_xs(lane < C ? lane : 0);
+                    const double a2 = lane < C ? x->s2 : 0.0, aa = lane < C ? x->s2all : 0.0;
+                    const int an = lane < C ? x->nkept : 0;
                     for (int rr = 0; rr < C; rr++) {
-                        Xch *x = remote_xs(rr);
-                        S2 = S2 + x->s2;
-                        SA = SA + x->s2all;
-                        NK += x->nkept;
+                        S2 = S2 + __shfl_sync(0xffffffffu, a2, rr);
+                        SA = SA + __shfl_sync(0xffffffffu, aa, rr);
+                        NK += __shfl_sync(0xffffffffu, an, rr);
                     }
                 }
-                S2 = __shfl_sync(0xffffffffu, S2, 0);
-                SA = __shfl_sync(0xffffffffu, SA, 0);
-                NK = __shfl_sync(0xffffffffu, NK, 0);
                 ch.nokept = NK == 0;
                 ch.inv_s2 = __double2float_rn(1.0 / (ch.nokept ? SA : S2));
             }
@@ -1259,7 +1299,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             {
                 CSum sub[4];
 #pragma unroll
-                for (int q = 0; q < 4; q++) sub[q].s = sub[q].c = 0.0f;
+                for (int q = 0; q < 4; q++) sub[q] = csum_zero();
                 const bool track = ch.minp && !ch.nokept;
 #pragma unroll 2
                 for (int j = 0; j < NV4; j++) {
@@ -1292,8 +1332,10 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     lmem = slice0 + slen - 1;
                 }
             }
+            mark(DBG_P3L);
             double excl[4], incl[4], qtot[4];
             block_scan4_d(subd, sh.red_d, excl, incl, qtot);
+            mark(DBG_P3S);
             double Q[5];
             Q[0] = 0.0;
 #pragma unroll
@@ -1313,23 +1355,24 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             double off = 0.0, grand = 0.0;
             int gfm = INT_MAX, glm = -1;
             float gfw = 0.0f;
-            if (lane == 0) {
+            {
+                Xch *x = remote_xs(lane < C ? lane : 0);
+                const double xt = lane < C ? x->tot : 0.0;
+                const int xf = lane < C ? x->first_member : INT_MAX;
+                const float xw = lane < C ? x->first_w : 0.0f;
+                const int xl = lane < C ? x->last_member : -1;
                 for (int rr = 0; rr < C; rr++) {
-                    Xch *x = remote_xs(rr);
                     if (rr == rank) off = grand;
-                    grand = grand + x->tot;
-                    if (x->first_member < gfm) {
-                        gfm = x->first_member;
-                        gfw = x->first_w;
+                    grand = grand + __shfl_sync(0xffffffffu, xt, rr);
+                    const int f = __shfl_sync(0xffffffffu, xf, rr);
+                    const float fwv = __shfl_sync(0xffffffffu, xw, rr);
+                    if (f < gfm) {
+                        gfm = f;
+                        gfw = fwv;
                     }
-                    glm = max(glm, x->last_member);
+                    glm = max(glm, __shfl_sync(0xffffffffu, xl, rr));
                 }
             }
-            off = __shfl_sync(0xffffffffu, off, 0);
-            grand = __shfl_sync(0xffffffffu, grand, 0);
-            gfm = __shfl_sync(0xffffffffu, gfm, 0);
-            gfw = __shfl_sync(0xffffffffu, gfw, 0);
-            glm = __shfl_sync(0xffffffffu, glm, 0);
             double P0[4], P1[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
@@ -1412,17 +1455,17 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         }
                     }
                     cluster.sync();  // ---- #4
-                    if (lane == 0) {
-                        for (int rr = 0; rr < C; rr++) {
-                            Xch *x = remote_xs(rr);
-                            if (x->cut_idx >= 0 && cut < 0) {
-                                cut = x->cut_idx;
-                                s3 = x->cut_s3;
-                            }
+                    {
+                        Xch *x = remote_xs(lane < C ? lane : 0);
+                        const int xc = lane < C ? x->cut_idx : -1;
+                        const double xs3 = lane < C ? x->cut_s3 : 0.0;
+                        const unsigned hm = __ballot_sync(0xffffffffu, xc >= 0);
+                        if (hm) {
+                            const int src = __ffs(hm) - 1;
+                            cut = __shfl_sync(0xffffffffu, xc, src);
+                            s3 = __shfl_sync(0xffffffffu, xs3, src);
                         }
                     }
-                    cut = __shfl_sync(0xffffffffu, cut, 0);
-                    s3 = __shfl_sync(0xffffffffu, s3, 0);
                 }
                 if (cut >= 0) {
                     ch.cut_idx = cut;
@@ -1471,32 +1514,40 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     anyq[q] = false;
                 }
                 float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride + slice0 : nullptr;
-#pragma unroll 2
-                for (int j = 0; j < NV4; j++) {
+                // elements of sub-chunk q at offset <= lim[q] lie inside the top-p prefix
+                int lim[4];
+                float qmax[4];
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
-                        const float e4[4] = {x.x, x.y, x.z, x.w};
+                for (int q = 0; q < 4; q++) {
+                    const long long d = (long long)ch.cut_idx - (slice0 + kb[q]);
+                    lim[q] = !ch.topp ? SUBT : (int)(d < 0 ? -1 : (d > SUBT ? SUBT : d));
+                    qmax[q] = 0.0f;
+                }
+                const float scale3 = ch.topp ? ch.inv_s3 : 1.0f;
+                if (ch.minp) p4_scan<true, NV4>(vals, kb, lim, ch, scale3, g0, g1, qmax);
+                else p4_scan<false, NV4>(vals, kb, lim, ch, scale3, g0, g1, qmax);
+                mark(DBG_P4L);
 #pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            const int li = kb[q] + 4 * j + c;
-                            const float qv = q_of(ch, e4[c], slice0 + li);
-                            anyq[q] |= qv != 0.0f;
-                            g0[q] = __fadd_rn(g0[q], qv);
-                            g1[q] = __fadd_rn(g1[q], qv);
-                            if (pr && li < slen) pr[li] = qv;
+                for (int q = 0; q < 4; q++) anyq[q] = qmax[q] > 0.0f;
+                if (pr) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        for (int j = 0; j < SUBT; j++) {
+                            const int li = kb[q] + j;
+                            if (li < slen) pr[li] = q_of(ch, vals[li], slice0 + li);
                         }
-                    }
                 }
                 WRec *recs = row_recs(a, row);
                 float *stash = row_stash(a, row);
 #pragma unroll 1
                 for (int q = 0; q < 4; q++) {
-                    const uint32_t lim = gb[q] + (1u << 23);
-                    const int ctype = !anyq[q] ? REC_IDENT
-                                               : ((pred[q] && fbits(g0[q]) < lim && fbits(g1[q]) < lim) ? REC_CLEAN : REC_MIXED);
-                    const int ce = (int)(gb[q] >> 23);
-                    const uint32_t c0 = fbits(g0[q]) - gb[q], c1 = fbits(g1[q]) - (gb[q] | 1u);
+                    // register selects instead of dynamic indexing, which would put the arrays in local memory
+                    const uint32_t gbq = pick4(gb, q), g0q = fbits(pick4(g0, q)), g1q = fbits(pick4(g1, q));
+                    const bool anyqq = pick4(anyq, q), predq = pick4(pred, q);
+                    const uint32_t lim = gbq + (1u << 23);
+                    const int ctype = !anyqq ? REC_IDENT : ((predq && g0q < lim && g1q < lim) ? REC_CLEAN : REC_MIXED);
+                    const int ce = (int)(gbq >> 23);
+                    const uint32_t c0 = g0q - gbq, c1 = g1q - (gbq | 1u);
                     // warp record over the 32 sub-chunks (q, 32*wid .. 32*wid+31)
                     const unsigned cleanm = __ballot_sync(0xffffffffu, ctype == REC_CLEAN);
                     const int e_first = cleanm ? __shfl_sync(0xffffffffu, ce, __ffs(cleanm) - 1) : 0;
@@ -1584,8 +1635,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 // kernel B: one warp per row draws with the exact fp32 running sum
 
 template <int DT, int SUBT>
-__global__ void __launch_bounds__(WALK_WARPS * 32) walk_rows_kernel(const KernelArgs a) {
+__global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const KernelArgs a) {
     __shared__ int hls[WALK_WARPS][HLIST];
+    __shared__ float rbuf[WALK_WARPS][32 * SUBT];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int row = blockIdx.x * WALK_WARPS + wid;
     if (threadIdx.x == 0) g_dbg = a.dbg;
@@ -1639,23 +1691,29 @@ __global__ void __launch_bounds__(WALK_WARPS * 32) walk_rows_kernel(const Kernel
         __syncwarp();
         if (nh > HLIST) hist_overflow = true;
     };
-    // draw probability of element li, recomputed from the row's inputs
-    auto qval = [&](int li) -> float {
-        if (li >= V) return 0.0f;
+    // raw (masked) logit of element li
+    auto raw_of = [&](int li) -> float {
+        if (li >= V) return -INFINITY;
         float v;
         if (DT == DLLM_DTYPE_F32)
-            v = ((const float *)a.logits)[(int64_t)row * a.row_stride + li];
+            v = __ldcs((const float *)a.logits + (int64_t)row * a.row_stride + li);
         else
-            v = bitsf((uint32_t)((const unsigned short *)a.logits)[(int64_t)row * a.row_stride + li] << 16);
+            v = bitsf((uint32_t)__ldcs((const unsigned short *)a.logits + (int64_t)row * a.row_stride + li) << 16);
         if (mrow && !((mrow[li >> 5] >> (li & 31)) & 1u)) v = -INFINITY;
+        return v;
+    };
+    // draw probability of element li from its raw logit v: penalties, temperature, softmax, cuts
+    auto qval = [&](float v, int li) -> float {
         if (use_hist && nh > 0) {
             int c = 0;
             if (!hist_overflow) {
-                for (int i = 0; i < nh; i++) c += hl[i] == li;
+                for (int i = 0; i < min(nh, HLIST); i++) c += hl[i] == li;
             } else {
                 const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-                for (int64_t j = h0; j < h1; j++) c += a.hist_ids[j] - a.vocab_offset == li && a.hist_ids[j] >= 0 &&
-                                                         a.hist_ids[j] < a.vocab_total;
+                for (int64_t j = h0; j < h1; j++) {
+                    const int id = a.hist_ids[j];
+                    c += id >= 0 && id < a.vocab_total && id - a.vocab_offset == li;
+                }
             }
             if (c > 0) {
                 if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
@@ -1670,16 +1728,22 @@ __global__ void __launch_bounds__(WALK_WARPS * 32) walk_rows_kernel(const Kernel
         const float e = expf(__fsub_rn(__fmul_rn(__fsub_rn(v, h.M), h.inv_temp), h.mv));
         return q_of(ch, e, li);
     };
-    // replays elements [start, start + n) on the exact running sum, recomputing them
+    // replays elements [start, start + n) (n <= 32 * SUBT) on the exact running sum, from the
+    // row's inputs staged in shared memory with coalesced loads
+    float *rv = rbuf[wid];
     auto replay_region = [&](int start, int n, uint32_t &cbv) -> int {
         if (lane == 0) dbg_add(DBG_RECOMP, 1);
         load_region_hist(start, start + n);
-        for (int g = 0; g < n; g += 256) {
+#pragma unroll 4
+        for (int i = lane; i < n; i += 32) rv[i] = raw_of(start + i);
+        __syncwarp();
+        int res = -1;
+        for (int g = 0; g < n && res == -1; g += 256) {
             const int m = min(256, n - g);
-            const int res = replay_elems(m, start + g, cbv, r, [&](int j) { return qval(start + g + j); });
-            if (res != -1) return res;
+            res = replay_elems(m, start + g, cbv, r, [&](int j) { return qval(rv[g + j], start + g + j); });
         }
-        return -1;
+        __syncwarp();
+        return res;
     };
 
     const WRec *recs = row_recs(a, row);
