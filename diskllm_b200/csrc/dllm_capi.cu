@@ -195,7 +195,8 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
     a.ws = (unsigned char *)ws;
     a.nrec = nrec;
     a.htab = cfg.htab;
-    a.uni_bytes = (int)(cfg.smem - (size_t)cfg.S * 4);
+    a.nbuf = cfg.nbuf;
+    a.uni_bytes = (int)(cfg.smem - (size_t)cfg.nbuf * (cfg.S + cfg.SUB) * 4);
     a.cluster = cfg.cluster;
     a.flags = d->flags;
     a.token = d->token;

@@ -40,7 +40,8 @@ struct KernelArgs {
     int             S;              // slice length per CTA (= 4 * NT * SUB)
     int             SUB;            // elements per thread sub-chunk (SUB % 8 == 4)
     int             htab;           // history hash-table entries (power of 2)
-    int             uni_bytes;      // bytes of the shared area after the slice
+    int             uni_bytes;      // bytes of the shared area after the slice buffers
+    int             nbuf;           // slice buffers per CTA: 2 = next row's copy overlaps this row
     int             cluster;        // CTAs per row (cluster size)
     unsigned        flags;
     int32_t        *token;
@@ -65,15 +66,24 @@ struct LaunchCfg {
     int htab;
     size_t smem;     // dynamic shared memory bytes
     int max_clusters;// co-resident clusters on the device
+    int nbuf;        // slice buffers per CTA (1 or 2)
 };
 
 // Workspace layout per row: RowHdr, nrec warp records, STASH_SLOTS stash slots.
 constexpr int STASH_SLOTS = 32;
 constexpr int STASH_STRIDE = 64;   // floats per stash slot: [0] = first index (as int), then SUB values
 constexpr int MAX_SUB = 60;
-// RowHdr (128 B) + nrec 24-byte warp records (rounded to 128 B) + the stash
+constexpr int WIDE_SLOTS = 4;              // warp ranges (32 sub-chunks) kept whole for the walk
+constexpr int WIDE_STRIDE = 32 * MAX_SUB;  // floats per wide slot
+// RowHdr (128 B) + nrec 24-byte warp records (rounded to 128 B) + the stash + the wide slots
 __host__ __device__ inline size_t row_ws_bytes(int nrec) {
-    return 128 + (((size_t)nrec * 24 + 127) & ~(size_t)127) + (size_t)STASH_SLOTS * STASH_STRIDE * 4;
+    return 128 + (((size_t)nrec * 24 + 127) & ~(size_t)127) + (size_t)STASH_SLOTS * STASH_STRIDE * 4 +
+           (size_t)WIDE_SLOTS * WIDE_STRIDE * 4;
+}
+
+// shared memory of one walk-kernel warp: its row's warp records and stash, copied in at the start
+__host__ __device__ inline size_t walk_smem_per_warp(int nrec) {
+    return (((size_t)nrec * 24 + 127) & ~(size_t)127) + (size_t)STASH_SLOTS * STASH_STRIDE * 4;
 }
 
 dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);

@@ -64,14 +64,16 @@ typedef void (*KernelFn)(const KernelArgs);
 struct RowHdr {
     float M, inv_temp, mv, inv_sum, min_p, inv_s2, inv_s3, r;
     int cut_idx, last_idx, flags, done, minp, nokept, topp, nstash;
-    int pad[16];
+    int nwide;  // wide stash slots claimed
+    int pad[15];
 };
 // Warp-level draw record (24 bytes).  meta: type (bits 0-1), boundary sub-chunk (2-7, 63 =
 // none), first suffix sub-chunk (8-13), prefix binade (16-23), suffix binade (24-31).
 struct WRec {
     uint32_t meta;
     uint32_t p0, p1, s0, s1;
-    int slot;   // stash slot holding the boundary sub-chunk's probabilities, or -1
+    int16_t nslot;  // PBS: stash slot holding the boundary sub-chunk's probabilities, or -1
+    int16_t wslot;  // wide slot holding all 32 sub-chunks' probabilities, or -1
 };
 
 // everything below has internal linkage: this header is compiled into several units
@@ -83,6 +85,7 @@ constexpr int TMA_PIECE = 32768;  // bytes per bulk copy instruction
 constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
 constexpr int WALK_WARPS = 4;     // rows per CTA of the walk kernel
 constexpr int HLIST = 256;        // per-warp history ids kept for a recomputed region
+constexpr float DRAW_WINDOW = 1.0f / 16384.0f;  // bound assumed on |fp32 running sum - exact prefix|
 
 enum : int { REC_IDENT = 0, REC_CLEAN = 1, REC_MIXED = 2, REC_PBS = 3 };
 
@@ -95,10 +98,17 @@ enum : int {
     DBG_ROWS = 16, DBG_REPLAY = 17, DBG_EXPAND = 18, DBG_STEPS = 19, DBG_REPLAY_IT = 20,
     DBG_PBS = 21, DBG_STASH_MISS = 22, DBG_TOPK_FALLBACK = 23, DBG_RECOMP = 24, DBG_WALK_CYC = 25,
     DBG_P2L = 13, DBG_P3L = 14, DBG_P3S = 15, DBG_P4L = 26, DBG_MAXP = 27,
+    DBG_B_PRE = 8, DBG_B_EXP = 9, DBG_B_REPL = 28, DBG_B_RECOMP = 29,
 };
 __device__ __forceinline__ void dbg_add(int k, unsigned long long v) {
     if (g_dbg) atomicAdd(g_dbg + k, v);
 }
+
+__device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 __device__ __forceinline__ RowHdr *row_hdr(const KernelArgs &a, int row) {
     return reinterpret_cast<RowHdr *>(a.ws + (size_t)row * row_ws_bytes(a.nrec));
@@ -109,6 +119,10 @@ __device__ __forceinline__ WRec *row_recs(const KernelArgs &a, int row) {
 __device__ __forceinline__ float *row_stash(const KernelArgs &a, int row) {
     const size_t recb = ((size_t)a.nrec * sizeof(WRec) + 127) & ~(size_t)127;
     return reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(row_hdr(a, row)) + sizeof(RowHdr) + recb);
+}
+// wide slots: the draw probabilities of all 32 sub-chunks of a MIXED warp record
+__device__ __forceinline__ float *row_wide(const KernelArgs &a, int row) {
+    return row_stash(a, row) + STASH_SLOTS * STASH_STRIDE;
 }
 
 // Values each CTA publishes to its cluster.  Every field is written at most once per row and
@@ -136,7 +150,7 @@ struct Xch {
 
 struct Shared {
     Xch xs;
-    unsigned long long tma_bar;
+    unsigned long long tma_bar[2];
     double red_d[4 * MAXW];
     float red_f[MAXW];
     int red_i[4 * MAXW];
@@ -397,26 +411,19 @@ __device__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t
     return -1;
 }
 
-// Replays n (<= 8*32) consecutive draw probabilities on the exact running sum cb.
-// Warp-cooperative: lane l owns a sub-range of ceil(n/32) elements.  `load(j)` returns the
-// probability of element j; `gbase + j` is its index.  Returns the drawn index, -1 (not in
-// this range; cb advanced past it) or -2.
-template <class Load>
-__device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, Load &&load) {
+// Replays n consecutive draw probabilities src[0..n) (shared memory) on the exact running sum
+// cb.  Warp-cooperative: lane l owns the sub-range [l*s, l*s + s), s = ceil(n/32), summarised
+// as a run record; runs that stay in one binade are composed in parallel, the others are
+// replayed serially by their lane.  `gbase + j` is the index of element j.  Returns the drawn
+// index, -1 (not in this range; cb advanced past it) or -2.
+__device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float *src) {
     const int lane = threadIdx.x & 31;
     const int s = (n + 31) >> 5;
     const int j0 = lane * s;
     const int cnt = max(0, min(s, n - j0));
-    float q[8];
+    const float *my = src + j0;
     bool anyq = false;
-#pragma unroll
-    for (int k = 0; k < 8; k++) {
-        q[k] = 0.0f;
-        if (k < cnt) {
-            q[k] = load(j0 + k);
-            anyq |= q[k] != 0.0f;
-        }
-    }
+    for (int k = 0; k < cnt; k++) anyq |= my[k] != 0.0f;
     if (lane == 0) dbg_add(DBG_REPLAY, 1);
     // serial replay of one lane's sub-range on the exact running sum
     auto serial = [&](int jl, uint32_t &cbx) -> int {
@@ -424,12 +431,9 @@ __device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, Load &&load
         uint32_t nb = 0;
         if (lane == jl) {
             float c = bitsf(cbx);
-#pragma unroll
-            for (int k = 0; k < 8; k++) {
-                if (k < cnt) {
-                    c = __fadd_rn(c, q[k]);
-                    if (found < 0 && r < c) found = gbase + j0 + k;
-                }
+            for (int k = 0; k < cnt; k++) {
+                c = __fadd_rn(c, my[k]);
+                if (found < 0 && r < c) found = gbase + j0 + k;
             }
             nb = fbits(c);
         }
@@ -452,12 +456,10 @@ __device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, Load &&load
         const uint32_t eb = cb >> 23;
         const uint32_t gb = eb << 23, lim = (eb + 1u) << 23;
         float g0 = bitsf(gb), g1 = bitsf(gb | 1u);
-#pragma unroll
-        for (int k = 0; k < 8; k++) {
-            if (k < cnt) {
-                g0 = __fadd_rn(g0, q[k]);
-                g1 = __fadd_rn(g1, q[k]);
-            }
+        for (int k = 0; k < cnt; k++) {
+            const float x = my[k];
+            g0 = __fadd_rn(g0, x);
+            g1 = __fadd_rn(g1, x);
         }
         const int type = !anyq ? REC_IDENT : ((fbits(g0) < lim && fbits(g1) < lim) ? REC_CLEAN : REC_MIXED);
         const uint32_t n0 = fbits(g0) - gb, n1 = fbits(g1) - (gb | 1u);
@@ -688,6 +690,44 @@ __device__ __forceinline__ T pick4(const T (&v)[4], int q) {
     return q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
 }
 
+// P3 body: compensated sums of the list probabilities over the four sub-chunks; TRACK also
+// records the first and last min-p member of this thread's sub-chunks.
+template <bool TRACK, bool MINP, int NV4>
+__device__ __forceinline__ void p3_scan(const float *vals, const int (&kb)[4], int slen, int slice0, const Chain &ch,
+                                        double (&subd)[4], int &fmem, int &lmem, float &fw) {
+    CSum sub[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) sub[q] = csum_zero();
+#pragma unroll 2
+    for (int j = 0; j < NV4; j++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
+            const float e4[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                // w_of with the min-p branch resolved at compile time (TRACK: min-p filters,
+                // MINP && !TRACK: min-p kept everything and only rescales)
+                float w = __fmul_rn(e4[c], ch.inv_sum);
+                if (MINP) w = (!TRACK || w >= ch.min_p) ? __fmul_rn(w, ch.inv_s2) : 0.0f;
+                csum_add(sub[q], w);
+                if (TRACK) {
+                    const int li = kb[q] + 4 * j + c;
+                    if (li < slen && member_of(ch, e4[c])) {
+                        if (slice0 + li < fmem) {
+                            fmem = slice0 + li;
+                            fw = w;
+                        }
+                        lmem = max(lmem, slice0 + li);
+                    }
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) subd[q] = csum_val(sub[q]);
+}
+
 template <bool MINP, int NV4>
 __device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], const int (&lim)[4], const Chain &ch,
                                         float scale3, float (&g0)[4], float (&g1)[4], float (&qmax)[4]) {
@@ -732,10 +772,22 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
     const int slen = max(0, min(S, V - slice0));
     int kb[4];  // slice-relative start of this thread's four sub-chunks
 #pragma unroll
-    for (int q = 0; q < 4; q++) kb[q] = (q * NT + tid) * SUBT;
+    for (int q = 0; q < 4; q++) {
+        // sub-chunks past the slice (S need not fill 4 * NT sub-chunks) read a shared all-zero
+        // sub-chunk stored right after the slice: they add nothing to sums or records
+        const int sc = q * NT + tid;
+        kb[q] = sc * SUBT < S ? sc * SUBT : S;
+    }
 
-    float *vals = reinterpret_cast<float *>(dsm);
-    unsigned char *uni = dsm + (size_t)S * sizeof(float);
+    // slice buffers: with nbuf == 2 the copy of this CTA's next row lands in the other buffer
+    // while the current row is processed
+    float *const vbuf0 = reinterpret_cast<float *>(dsm);
+    float *const vbuf1 = a.nbuf == 2 ? vbuf0 + S + SUBT : vbuf0;
+    unsigned char *uni = dsm + (size_t)a.nbuf * (S + SUBT) * sizeof(float);
+    for (int i = tid; i < SUBT; i += NT) {
+        vbuf0[S + i] = 0.0f;
+        vbuf1[S + i] = 0.0f;
+    }
     // union area: history table | top-k survivors + list
     int *hkeys = reinterpret_cast<int *>(uni);
     int *hcnt = hkeys + a.htab;
@@ -745,7 +797,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 
     if (tid == 0) {
         g_dbg = a.dbg;
-        mbar_init(&sh.tma_bar, 1);
+        mbar_init(&sh.tma_bar[0], 1);
+        mbar_init(&sh.tma_bar[1], 1);
         fence_proxy_async();
     }
     __syncthreads();
@@ -763,14 +816,15 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
     // bulk copy of this CTA's slice of `row` (fp32 rows with 16-byte aligned slices)
     const bool use_tma = DT == DLLM_DTYPE_F32 && a.vec_ok;
     const int tma_elems = slen & ~3;
-    auto issue_row_copy = [&](int row) {
+    auto issue_row_copy = [&](int row, int b) {
         const unsigned char *src = reinterpret_cast<const unsigned char *>(
             (const float *)a.logits + (int64_t)row * a.row_stride + slice0);
+        unsigned char *dst = reinterpret_cast<unsigned char *>(b ? vbuf1 : vbuf0);
         const uint32_t bytes = (uint32_t)tma_elems * 4u;
-        mbar_arrive_expect_tx(&sh.tma_bar, bytes);
+        mbar_arrive_expect_tx(&sh.tma_bar[b], bytes);
         for (uint32_t off = 0; off < bytes; off += TMA_PIECE) {
             const uint32_t nb = bytes - off < (uint32_t)TMA_PIECE ? bytes - off : (uint32_t)TMA_PIECE;
-            bulk_g2s(reinterpret_cast<unsigned char *>(vals) + off, src + off, nb, &sh.tma_bar);
+            bulk_g2s(dst + off, src + off, nb, &sh.tma_bar[b]);
         }
     };
     auto prefetch_row = [&](int row) {
@@ -783,9 +837,17 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
     };
 
-    uint32_t phase = 0;
-    for (int row = cid; row < a.rows; row += ncl, phase ^= 1u) {
+    const bool dbuf = a.nbuf == 2;
+    if (tid == 0 && use_tma) {
+        if (cid < a.rows) issue_row_copy(cid, 0);
+        if (dbuf && cid + ncl < a.rows) issue_row_copy(cid + ncl, 1);
+    }
+    int it = 0;
+    for (int row = cid; row < a.rows; row += ncl, it++) {
         if (timing) dbg_add(DBG_ROWS, 1);
+        const int buf = dbuf ? (it & 1) : 0;
+        const uint32_t phase = dbuf ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
+        float *const vals = buf ? vbuf1 : vbuf0;
         const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
         const float r = a.uniforms[row];
         RowHdr *hdr = row_hdr(a, row);
@@ -793,11 +855,14 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 
         // ---------------- P1: bulk copy in flight while the history table is built ---------------
         if (tid == 0) {
-            if (use_tma) {
-                issue_row_copy(row);
+            if (use_tma && !dbuf) {
+                if (it > 0) issue_row_copy(row, 0);
                 if (row + ncl < a.rows) prefetch_row(row + ncl);
             }
-            if (rank == 0) hdr->nstash = 0;
+            if (rank == 0) {
+                hdr->nstash = 0;
+                hdr->nwide = 0;
+            }
         }
         for (int i = tid; i < a.htab; i += NT) {
             hkeys[i] = -1;
@@ -840,7 +905,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         for (int i = slen + tid; i < S; i += NT) vals[i] = -INFINITY;
         if (use_tma) {
             long long it = 0;
-            while (!mbar_try_wait(&sh.tma_bar, phase)) {
+            while (!mbar_try_wait(&sh.tma_bar[buf], phase)) {
                 if (++it > WAIT_LIMIT) {
                     flags |= ROW_ERR_TIMEOUT;
                     break;
@@ -1296,41 +1361,13 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             double subd[4];
             int fmem = INT_MAX, lmem = -1;
             float fw = 0.0f;
-            {
-                CSum sub[4];
-#pragma unroll
-                for (int q = 0; q < 4; q++) sub[q] = csum_zero();
-                const bool track = ch.minp && !ch.nokept;
-#pragma unroll 2
-                for (int j = 0; j < NV4; j++) {
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
-                        const float e4[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                        for (int c = 0; c < 4; c++) {
-                            const float w = w_of(ch, e4[c]);
-                            csum_add(sub[q], w);
-                            if (track) {
-                                const int li = kb[q] + 4 * j + c;
-                                if (li < slen && member_of(ch, e4[c])) {
-                                    if (slice0 + li < fmem) {
-                                        fmem = slice0 + li;
-                                        fw = w;
-                                    }
-                                    lmem = max(lmem, slice0 + li);
-                                }
-                            }
-                        }
-                    }
-                }
-#pragma unroll
-                for (int q = 0; q < 4; q++) subd[q] = csum_val(sub[q]);
-                if (!track && tid == 0 && slen > 0) {
-                    fmem = slice0;
-                    fw = w_of(ch, vals[0]);
-                    lmem = slice0 + slen - 1;
-                }
+            if (ch.minp && !ch.nokept) p3_scan<true, true, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
+            else if (ch.minp) p3_scan<false, true, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
+            else p3_scan<false, false, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
+            if (!(ch.minp && !ch.nokept) && tid == 0 && slen > 0) {
+                fmem = slice0;
+                fw = w_of(ch, vals[0]);
+                lmem = slice0 + slen - 1;
             }
             mark(DBG_P3L);
             double excl[4], incl[4], qtot[4];
@@ -1496,7 +1533,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             {
                 const double inv3 = ch.topp ? (double)ch.inv_s3 : 1.0;
                 uint32_t gb[4];
-                bool pred[4];
+                bool pred[4], near[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     const float A0 = __double2float_rn(P0[q] * inv3);
@@ -1504,6 +1541,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     const uint32_t e0 = fbits(A0) >> 23, e1 = fbits(A1) >> 23;
                     pred[q] = A0 > 0.0f && e0 == e1 && e0 >= 1u && e0 <= 253u;
                     gb[q] = (pred[q] ? e0 : 127u) << 23;
+                    // the draw can land here: the running sum stays within DRAW_WINDOW of the
+                    // exact prefix (the fp32 drift), so the walk will replay this warp range
+                    near[q] = A1 > 0.0f && A1 + DRAW_WINDOW > r && A0 - DRAW_WINDOW <= r;
                 }
                 float g0[4], g1[4];
                 bool anyq[4];
@@ -1543,7 +1583,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 for (int q = 0; q < 4; q++) {
                     // register selects instead of dynamic indexing, which would put the arrays in local memory
                     const uint32_t gbq = pick4(gb, q), g0q = fbits(pick4(g0, q)), g1q = fbits(pick4(g1, q));
-                    const bool anyqq = pick4(anyq, q), predq = pick4(pred, q);
+                    const bool anyqq = pick4(anyq, q), predq = pick4(pred, q), nearq = pick4(near, q);
                     const uint32_t lim = gbq + (1u << 23);
                     const int ctype = !anyqq ? REC_IDENT : ((predq && g0q < lim && g1q < lim) ? REC_CLEAN : REC_MIXED);
                     const int ce = (int)(gbq >> 23);
@@ -1585,18 +1625,41 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         bchunk = tj == REC_MIXED ? j : -1;
                     }
                     // boundary sub-chunk probabilities -> a stash slot (when one is free)
-                    int slot = -1;
+                    int nslot = -1, wslot = -1;
                     if (type == REC_PBS && bchunk >= 0) {
                         if (lane == 0) {
-                            slot = atomicAdd(&hdr->nstash, 1);
-                            if (slot >= STASH_SLOTS) slot = -1;
+                            nslot = atomicAdd(&hdr->nstash, 1);
+                            if (nslot >= STASH_SLOTS) nslot = -1;
                         }
-                        slot = __shfl_sync(0xffffffffu, slot, 0);
-                        if (slot >= 0) {
+                        nslot = __shfl_sync(0xffffffffu, nslot, 0);
+                        if (nslot >= 0) {
                             const int sb = (q * NT + 32 * wid + bchunk) * SUBT;
-                            float *qs = stash + slot * STASH_STRIDE;
+                            float *qs = stash + nslot * STASH_STRIDE;
                             if (lane == 0) qs[0] = __int_as_float(slice0 + sb);
                             for (int k = lane; k < SUBT; k += 32) qs[1 + k] = q_of(ch, vals[sb + k], slice0 + sb + k);
+                        } else if (timing) {
+                            dbg_add(DBG_STASH_MISS, 1);
+                        }
+                    }
+                    // several binade changes in this warp's range, or the draw may land in it:
+                    // keep every probability so the walk replays them without recomputing
+                    if (type == REC_MIXED || __any_sync(0xffffffffu, nearq)) {
+                        if (lane == 0) {
+                            wslot = atomicAdd(&hdr->nwide, 1);
+                            if (wslot >= WIDE_SLOTS) wslot = -1;
+                        }
+                        wslot = __shfl_sync(0xffffffffu, wslot, 0);
+                        if (wslot >= 0) {
+                            const int kq = pick4(kb, q);
+                            float *ws = row_wide(a, row) + wslot * WIDE_STRIDE + lane * SUBT;
+                            for (int k = 0; k < SUBT; k += 4) {
+                                float4 o;
+                                o.x = q_of(ch, vals[kq + k], slice0 + kq + k);
+                                o.y = q_of(ch, vals[kq + k + 1], slice0 + kq + k + 1);
+                                o.z = q_of(ch, vals[kq + k + 2], slice0 + kq + k + 2);
+                                o.w = q_of(ch, vals[kq + k + 3], slice0 + kq + k + 3);
+                                *reinterpret_cast<float4 *>(ws + k) = o;
+                            }
                         } else if (timing) {
                             dbg_add(DBG_STASH_MISS, 1);
                         }
@@ -1608,7 +1671,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         wr.p1 = p1;
                         wr.s0 = s0;
                         wr.s1 = s1;
-                        wr.slot = slot;
+                        wr.nslot = (int16_t)nslot;
+                        wr.wslot = (int16_t)wslot;
                         recs[rank * 4 * NW + q * NW + wid] = wr;
                         if (type == REC_PBS && timing) dbg_add(DBG_PBS, 1);
                     }
@@ -1627,6 +1691,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         mark(DBG_TOPK);
         fence_proxy_async();  // order this row's generic accesses of the slice before the next bulk copy
         cluster.sync();       // ---- end of row: peers may reuse their shared memory
+        if (dbuf && tid == 0 && use_tma && row + 2 * ncl < a.rows) issue_row_copy(row + 2 * ncl, buf);
         mark(DBG_WEND);
     }
 }
@@ -1637,7 +1702,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 template <int DT, int SUBT>
 __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const KernelArgs a) {
     __shared__ int hls[WALK_WARPS][HLIST];
-    __shared__ float rbuf[WALK_WARPS][32 * SUBT];
+    __shared__ __align__(16) float rbuf[WALK_WARPS][32 * SUBT];
+    extern __shared__ __align__(16) unsigned char wdyn[];
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int row = blockIdx.x * WALK_WARPS + wid;
     if (threadIdx.x == 0) g_dbg = a.dbg;
@@ -1646,6 +1712,22 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
     const RowHdr h = *row_hdr(a, row);
     if (h.done) return;
     const long long t_start = clock64();
+    // the row's warp records and used stash slots -> shared memory, all copies in flight at once
+    const size_t recb = ((size_t)a.nrec * sizeof(WRec) + 127) & ~(size_t)127;
+    unsigned char *wsm = wdyn + (size_t)wid * walk_smem_per_warp(a.nrec);
+    const WRec *recs = reinterpret_cast<const WRec *>(wsm);
+    const float *stash = reinterpret_cast<const float *>(wsm + recb);
+    {
+        const unsigned char *grec = reinterpret_cast<const unsigned char *>(row_recs(a, row));
+        const int nrec16 = (int)(((size_t)a.nrec * sizeof(WRec) + 15) / 16);
+        for (int i = lane; i < nrec16; i += 32) cp_async16(wsm + 16 * i, grec + 16 * i);
+        const int ns = min(h.nstash, STASH_SLOTS);
+        const unsigned char *gst = reinterpret_cast<const unsigned char *>(row_stash(a, row));
+        for (int i = lane; i < ns * STASH_STRIDE / 4; i += 32) cp_async16(wsm + recb + 16 * i, gst + 16 * i);
+        cp_async_wait_all();
+        __syncwarp();
+    }
+    if (lane == 0) dbg_add(DBG_B_PRE, (unsigned long long)(clock64() - t_start));
     const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
     Chain ch;
     ch.inv_sum = h.inv_sum;
@@ -1732,22 +1814,35 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
     // row's inputs staged in shared memory with coalesced loads
     float *rv = rbuf[wid];
     auto replay_region = [&](int start, int n, uint32_t &cbv) -> int {
+        const long long t0 = clock64();
         if (lane == 0) dbg_add(DBG_RECOMP, 1);
         load_region_hist(start, start + n);
+        // raw logits of the region: 16-byte asynchronous copies where aligned, all in flight
+        const int nv = max(0, min(n, V - start));
+        int nc = 0;
+        if (DT == DLLM_DTYPE_F32 && a.vec_ok) {
+            nc = nv & ~3;
+            const float *src = (const float *)a.logits + (int64_t)row * a.row_stride + start;
+            for (int i = lane; i < nc / 4; i += 32) cp_async16(rv + 4 * i, src + 4 * i);
+        }
 #pragma unroll 4
-        for (int i = lane; i < n; i += 32) rv[i] = raw_of(start + i);
+        for (int i = nc + lane; i < n; i += 32) rv[i] = raw_of(start + i);
+        cp_async_wait_all();
         __syncwarp();
-        int res = -1;
-        for (int g = 0; g < n && res == -1; g += 256) {
-            const int m = min(256, n - g);
-            res = replay_elems(m, start + g, cbv, r, [&](int j) { return qval(rv[g + j], start + g + j); });
+#pragma unroll 4
+        for (int i = lane; i < n; i += 32) {
+            const int li = start + i;
+            float v = rv[i];
+            if (i < nc && mrow && !((mrow[li >> 5] >> (li & 31)) & 1u)) v = -INFINITY;
+            rv[i] = li < V ? qval(v, li) : 0.0f;
         }
         __syncwarp();
+        const int res = replay_elems(n, start, cbv, r, rv);
+        __syncwarp();
+        if (lane == 0) dbg_add(DBG_B_RECOMP, (unsigned long long)(clock64() - t0));
         return res;
     };
 
-    const WRec *recs = row_recs(a, row);
-    const float *stash = row_stash(a, row);
     uint32_t cb = 0u;  // running sum, starts at +0.0f
     int res = -1;
     for (int gw0 = 0; gw0 < a.nrec && res == -1; gw0 += 32) {
@@ -1755,15 +1850,35 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
         WRec wl;
         wl.meta = REC_IDENT;
         wl.p0 = wl.p1 = wl.s0 = wl.s1 = 0u;
-        wl.slot = -1;
+        wl.nslot = wl.wslot = -1;
         if (lane < n) wl = recs[gw0 + lane];
         const int ty = (int)(wl.meta & 3u);
         const int ep = (int)((wl.meta >> 16) & 255u);
-        auto expandA = [&](int j, uint32_t &cbv) -> int {
+        auto expandA0 = [&](int j, uint32_t &cbv) __attribute__((always_inline)) -> int {
             if (lane == 0) dbg_add(DBG_EXPAND, 1);
             const int g = gw0 + j;
             const int rr = g / (4 * NW), kk = g % (4 * NW), q = kk / NW, w = kk % NW;
             const int start = rr * S + (q * NT + 32 * w) * SUBT;
+            const int rend = rr * S + S;  // sub-chunks past the slice end hold nothing
+            const int wslot = __shfl_sync(0xffffffffu, (int)wl.wslot, j);
+            bool wide_in = false;
+            // replays [st, st + n) of this warp range: from its wide slot when the cluster
+            // kernel kept one (copied in once), else recomputed from the row's inputs
+            auto replay_clamped = [&](int st, int n, uint32_t &cbv) -> int {
+                n = min(n, rend - st);
+                if (n <= 0) return -1;
+                if (wslot < 0) return replay_region(st, n, cbv);
+                if (!wide_in) {
+                    const float *wsrc = row_wide(a, row) + wslot * WIDE_STRIDE;
+                    for (int i = lane; i < 8 * SUBT; i += 32) cp_async16(rv + 4 * i, wsrc + 4 * i);
+                    cp_async_wait_all();
+                    __syncwarp();
+                    wide_in = true;
+                }
+                const int res = replay_elems(n, st, cbv, r, rv + (st - start));
+                __syncwarp();
+                return res;
+            };
             const uint32_t meta = __shfl_sync(0xffffffffu, wl.meta, j);
             if ((int)(meta & 3u) == REC_PBS) {
                 const int bc = (int)((meta >> 2) & 63u);
@@ -1771,16 +1886,16 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                 const int epre = (int)((meta >> 16) & 255u), esuf = (int)(meta >> 24);
                 const uint32_t p0 = __shfl_sync(0xffffffffu, wl.p0, j), p1 = __shfl_sync(0xffffffffu, wl.p1, j);
                 const uint32_t s0 = __shfl_sync(0xffffffffu, wl.s0, j), s1 = __shfl_sync(0xffffffffu, wl.s1, j);
-                const int slot = __shfl_sync(0xffffffffu, wl.slot, j);
+                const int slot = __shfl_sync(0xffffffffu, (int)wl.nslot, j);
                 uint32_t c = cbv;
                 if (apply_run(c, epre, p0, p1) && !(r < bitsf(c))) {
                     if (bc != 63) {
                         int found;
                         if (slot >= 0) {
                             const float *qs = stash + slot * STASH_STRIDE;
-                            found = replay_elems(SUBT, __float_as_int(qs[0]), c, r, [&](int k) { return qs[1 + k]; });
+                            found = replay_elems(SUBT, __float_as_int(qs[0]), c, r, qs + 1);
                         } else {
-                            found = replay_region(start + bc * SUBT, SUBT, c);
+                            found = replay_clamped(start + bc * SUBT, SUBT, c);
                         }
                         if (found != -1) return found;
                     }
@@ -1790,14 +1905,14 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                         return -1;
                     }
                     cbv = c;
-                    return replay_region(start + sfrom * SUBT, (32 - sfrom) * SUBT, cbv);
+                    return replay_clamped(start + sfrom * SUBT, (32 - sfrom) * SUBT, cbv);
                 }
             }
-            return replay_region(start, 32 * SUBT, cbv);
+            return replay_clamped(start, 32 * SUBT, cbv);
         };
         const int tyw = ty == REC_PBS ? REC_MIXED : ty;
         int pos = 0;
-        while (pos < n && res == -1) res = walk_step(n, pos, tyw, ep, wl.p0, wl.p1, cb, r, expandA);
+        while (pos < n && res == -1) res = walk_step(n, pos, tyw, ep, wl.p0, wl.p1, cb, r, expandA0);
     }
     if (lane == 0) {
         int flags = h.flags;

@@ -84,9 +84,9 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
     }
     // top-k: survivor sort buffer plus the final list
     const int cand_entries = topk_bound > 0 ? CAND_CAP + 2 * pow2_at_least(topk_bound) : 0;
-    // DLLM_FORCE_CFG="C,NT[,SUB]" pins the cluster size / block size / sub-chunk (tuning)
-    int force_c = 0, force_nt = 0, force_l = 0;
-    if (const char *f = getenv("DLLM_FORCE_CFG")) sscanf(f, "%d,%d,%d", &force_c, &force_nt, &force_l);
+    // DLLM_FORCE_CFG="C,NT[,SUB[,NBUF]]" pins the cluster size / block size / sub-chunk (tuning)
+    int force_c = 0, force_nt = 0, force_l = 0, force_b = 0;
+    if (const char *f = getenv("DLLM_FORCE_CFG")) sscanf(f, "%d,%d,%d,%d", &force_c, &force_nt, &force_l, &force_b);
     static const int Cs[] = {1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11, 12, 13, 14, 15, 16};
     static const int NTs[] = {128, 160, 192, 224, 256, 320, 384, 448, 512};
     double best = 1e300;
@@ -94,7 +94,10 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
     for (int C : Cs) {
         for (int NT : NTs) {
             if (force_c && (C != force_c || (force_nt && NT != force_nt))) continue;
-            const int per = (vocab + 4 * C * NT - 1) / (4 * C * NT);  // elements per sub-chunk
+            // slice: the smallest multiple of the sub-chunk length covering vocab / C; a thread owns
+            // up to four sub-chunks, so the sub-chunk length is the smallest that covers the slice
+            const int need = (vocab + C - 1) / C;
+            const int per = (need + 4 * NT - 1) / (4 * NT);
             int L = -1;
             for (int lt : kSUBs)
                 if (lt >= per && (!force_l || lt == force_l)) {
@@ -102,40 +105,49 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
                     break;
                 }
             if (L < 0) continue;
-            const int S = 4 * NT * L;
+            const int S = (need + L - 1) / L * L;
             if ((long long)S * (C - 1) >= vocab && C > 1) continue;  // an idle CTA
             int hb = hist_bound < S ? hist_bound : S;
             int htab = pow2_at_least(2 * (hb > 16 ? hb : 16));
             if (htab > 16384) htab = 16384;
-            const size_t smem = (size_t)S * 4 + union_bytes(htab, cand_entries);
-            if (smem > 220 * 1024) continue;
-            KernelFn fn = kernel_for(dtype, L);
-            const int nact = active_clusters(fn, C, NT, smem);
-            if (nact <= 0) continue;
-            // cost: padded work x idle-SM factor, a penalty when only one CTA fits per SM (no
-            // overlap of one row's latency-bound phases with another row's streaming), and a
-            // term for short sub-chunks (more warp records for the walk)
-            const double pad = (double)S * C / vocab;
-            const double used = (double)nact * C;
-            const double under = used >= g_sm_count ? 1.0 : (double)g_sm_count / used;
-            const double per_sm = used / g_sm_count;
-            const double cost = pad * under * (per_sm >= 2.0 ? 1.0 : 1.3) * (1.0 + 4.0 / L);
-            if (cost < best) {
-                best = cost;
-                bc.cluster = C;
-                bc.threads = NT;
-                bc.SUB = L;
-                bc.S = S;
-                bc.htab = htab;
-                bc.smem = smem;
-                bc.max_clusters = nact;
+            // one or two slice buffers (with two, the next row's bulk copy overlaps this row)
+            for (int nbuf = 2; nbuf >= 1; nbuf--) {
+                if (force_b && nbuf != force_b) continue;
+                const size_t smem = (size_t)nbuf * (S + L) * 4 + union_bytes(htab, cand_entries);
+                if (smem > 220 * 1024) continue;
+                KernelFn fn = kernel_for(dtype, L);
+                const int nact = active_clusters(fn, C, NT, smem);
+                if (nact <= 0) continue;
+                // cost: padded work x idle-SM factor, a penalty when only one CTA fits per SM (no
+                // overlap of one row's latency-bound phases with another row's streaming), and a
+                // term for short sub-chunks (more warp records for the walk)
+                const double pad = 4.0 * NT * L * C / vocab;  // the busiest thread owns four sub-chunks
+                const double used = (double)nact * C;
+                const double under = used >= g_sm_count ? 1.0 : (double)g_sm_count / used;
+                const double per_sm = used / g_sm_count;
+                const double overlap = nbuf == 2 || per_sm >= 2.0 ? 1.0 : 1.3;
+                const double cost = pad * under * overlap * (1.0 + 4.0 / L);
+                if (getenv("DLLM_LIST_CFGS"))
+                    fprintf(stderr, "dllm candidate: C %d NT %d SUB %d S %d nbuf %d smem %zu clusters %d cost %.3f\n", C, NT, L, S,
+                            nbuf, smem, nact, cost);
+                if (cost < best) {
+                    best = cost;
+                    bc.cluster = C;
+                    bc.threads = NT;
+                    bc.SUB = L;
+                    bc.S = S;
+                    bc.htab = htab;
+                    bc.smem = smem;
+                    bc.max_clusters = nact;
+                    bc.nbuf = nbuf;
+                }
             }
         }
     }
     if (best >= 1e299) return DLLM_ERR_UNSUPPORTED;
     if (getenv("DLLM_VERBOSE"))
-        fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d SUB %d S %d htab %d smem %zu clusters %d\n",
-                vocab, dtype, bc.cluster, bc.threads, bc.SUB, bc.S, bc.htab, bc.smem, bc.max_clusters);
+        fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d SUB %d S %d htab %d smem %zu clusters %d nbuf %d\n",
+                vocab, dtype, bc.cluster, bc.threads, bc.SUB, bc.S, bc.htab, bc.smem, bc.max_clusters, bc.nbuf);
     *cfg = bc;
     return DLLM_OK;
 }
@@ -171,7 +183,10 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
     // the walk kernel: one warp per row, after the cluster kernel on the same stream
     const int wb = (a.rows + WALK_WARPS - 1) / WALK_WARPS;
-    fnb<<<wb, WALK_WARPS * 32, 0, stream>>>(args);
+    const size_t wsmem = (size_t)WALK_WARPS * walk_smem_per_warp(a.nrec);
+    e = cudaFuncSetAttribute((const void *)fnb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    if (e != cudaSuccess) return DLLM_ERR_CUDA;
+    fnb<<<wb, WALK_WARPS * 32, wsmem, stream>>>(args);
     e = cudaGetLastError();
     return e == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
 }
