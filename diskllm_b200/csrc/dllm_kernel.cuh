@@ -137,6 +137,7 @@ struct Xch {
     double tot;
     int first_member;
     float first_w;
+    float first_e;    // exponential of the slice's first element
     int last_member;
     int cut_idx;
     double cut_s3;
@@ -145,6 +146,8 @@ struct Xch {
     uint32_t theta;
     int cnt_gt, cnt_eq;
     int ncand;        // CTA 0: survivors gathered
+    int slots;        // CTA 0: stash slots (low 16 bits) and wide slots (high 16) claimed by
+                      // atomics of every CTA of the cluster; reset at the start of each row
     unsigned hist[2][256];
 };
 
@@ -226,15 +229,18 @@ __device__ __forceinline__ T warp_allreduce(T v, Op op) {
 }
 
 template <class T, class Op>
-__device__ __forceinline__ T block_allreduce(T v, T *scratch, Op op) {
+__device__ __forceinline__ T block_allreduce(T v, T *scratch, Op op, T ident) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
     v = warp_allreduce(v, op);
     __syncthreads();
     if (lane == 0) scratch[w] = v;
     __syncthreads();
-    T r = scratch[0];
-    for (int i = 1; i < nw; i++) r = op(r, scratch[i]);
-    return r;
+    // per-warp values folded by a shuffle tree in every warp; lane 0's result is broadcast so
+    // all threads hold the same bits
+    T x = lane < nw ? scratch[lane] : ident;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x = op(x, __shfl_down_sync(0xffffffffu, x, o));
+    return __shfl_sync(0xffffffffu, x, 0);
 }
 
 // Exclusive / inclusive scan of doubles in thread order.  excl(t+1) is bit-identical to
@@ -339,6 +345,24 @@ __device__ __forceinline__ void compose_scan(uint32_t &a0, uint32_t &a1) {
             uint32_t x0 = a0, x1 = a1;
             a0 = p0 + ((p0 & 1u) ? x1 : x0);
             a1 = p1 + (((1u + p1) & 1u) ? x1 : x0);
+        }
+    }
+}
+
+// Four independent composition scans side by side (general parity form).
+__device__ __forceinline__ void compose_scan4(uint32_t (&a0)[4], uint32_t (&a1)[4]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const uint32_t p0 = __shfl_up_sync(0xffffffffu, a0[q], d);
+            const uint32_t p1 = __shfl_up_sync(0xffffffffu, a1[q], d);
+            if (lane >= d) {
+                const uint32_t x0 = a0[q], x1 = a1[q];
+                a0[q] = p0 + ((p0 & 1u) ? x1 : x0);
+                a1[q] = p1 + (((1u + p1) & 1u) ? x1 : x0);
+            }
         }
     }
 }
@@ -690,6 +714,41 @@ __device__ __forceinline__ T pick4(const T (&v)[4], int q) {
     return q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
 }
 
+// P2 body: exponentials of this thread's four sub-chunks, written back in place, and their
+// compensated sums.  Sub-chunks past the slice (the shared zero sub-chunk) are skipped.
+template <int NV4>
+__device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, float M, float inv_temp, float mv,
+                                        double (&sube)[4]) {
+    CSum sub[4];
+    bool real[4];
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        sub[q] = csum_zero();
+        real[q] = kb[q] < S;
+    }
+#pragma unroll 2
+    for (int j = 0; j < NV4; j++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            if (real[q]) {
+                float4 *p = reinterpret_cast<float4 *>(vals + kb[q] + 4 * j);
+                float4 x = *p;
+                x.x = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
+                x.y = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
+                x.z = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
+                x.w = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
+                *p = x;
+                csum_add(sub[q], x.x);
+                csum_add(sub[q], x.y);
+                csum_add(sub[q], x.z);
+                csum_add(sub[q], x.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) sube[q] = csum_val(sub[q]);
+}
+
 // P3 body: compensated sums of the list probabilities over the four sub-chunks; TRACK also
 // records the first and last min-p member of this thread's sub-chunks.
 template <bool TRACK, bool MINP, int NV4>
@@ -859,10 +918,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 if (it > 0) issue_row_copy(row, 0);
                 if (row + ncl < a.rows) prefetch_row(row + ncl);
             }
-            if (rank == 0) {
-                hdr->nstash = 0;
-                hdr->nwide = 0;
-            }
+            if (rank == 0) sh.xs.slots = 0;
         }
         for (int i = tid; i < a.htab; i += NT) {
             hkeys[i] = -1;
@@ -940,7 +996,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             }
         }
         mark(DBG_MAXP);
-        const float mraw = block_allreduce(lmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+        const float mraw = block_allreduce(lmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
 
         // ---------------- P1: penalties ----------------------------------------------------------
         float pmax = -INFINITY;
@@ -969,8 +1025,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
         float lm;
         {
-            const float pm = block_allreduce(pmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
-            const int rf = block_allreduce((rescan ? 0x10000 : 0) | flags, sh.red_i, [](int x, int y) { return x | y; });
+            const float pm = block_allreduce(pmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
+            const int rf = block_allreduce((rescan ? 0x10000 : 0) | flags, sh.red_i, [](int x, int y) { return x | y; }, 0);
             flags = rf & 0xffff;
             if (rf & 0x10000) {
                 float m2 = -INFINITY;
@@ -979,7 +1035,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     const float4 x = v4[i];
                     m2 = fmaxf(m2, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
-                lm = block_allreduce(m2, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+                lm = block_allreduce(m2, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
             } else {
                 lm = fmaxf(mraw, pm);
             }
@@ -1023,7 +1079,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     break;
                 }
             if (first != INT_MAX) first += slice0;
-            const int bf = block_allreduce(first, sh.red_i, [](int x, int y) { return min(x, y); });
+            const int bf = block_allreduce(first, sh.red_i, [](int x, int y) { return min(x, y); }, INT_MAX);
             if (tid == 0) sh.xs.gidx = bf;
             cluster.sync();  // ---- greedy
             int gv = INT_MAX;
@@ -1271,44 +1327,43 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             } else {
                 float tm = -INFINITY;
                 for (int i = tid; i < slen; i += NT) tm = fmaxf(tm, __fmul_rn(__fsub_rn(vals[i], M), inv_temp));
-                tm = block_allreduce(tm, sh.red_f, [](float x, float y) { return fmaxf(x, y); });
+                tm = block_allreduce(tm, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
                 if (tid == 0) sh.xs.mt = tm;
                 cluster.sync();  // ---- odd temperature
                 float tv = -INFINITY;
                 if (lane < C) tv = remote_xs(lane)->mt;
                 mv = warp_allreduce(tv, [](float x, float y) { return fmaxf(x, y); });
             }
-            // P2: exponentials (in place), compensated sum
-            double ds;
-            {
-                float4 *v4 = reinterpret_cast<float4 *>(vals);
-                CSum c0 = csum_zero(), c1 = csum_zero();
-#pragma unroll 2
-                for (int i = tid; i < S / 4; i += NT) {
-                    float4 x = v4[i];
-                    x.x = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
-                    x.y = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
-                    x.z = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
-                    x.w = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
-                    v4[i] = x;
-                    csum_add(c0, x.x);
-                    csum_add(c1, x.y);
-                    csum_add(c0, x.z);
-                    csum_add(c1, x.w);
-                }
-                ds = csum_val(c0) + csum_val(c1);
-            }
+            // P2: exponentials (in place) and compensated sums per sub-chunk, scanned in
+            // sub-chunk order; the prefix sums of e place the top-p cut
+            double sube[4];
+            p2_scan<NV4>(vals, kb, S, M, inv_temp, mv, sube);
             mark(DBG_P2L);
-            ds = block_allreduce(ds, sh.red_d, [](double x, double y) { return x + y; });
-            if (tid == 0) sh.xs.dsum = ds;
+            double exE[4], inE[4], totE[4];
+            block_scan4_d(sube, sh.red_d, exE, inE, totE);
+            double QE[5];
+            QE[0] = 0.0;
+#pragma unroll
+            for (int q = 0; q < 4; q++) QE[q + 1] = QE[q] + totE[q];
+            if (tid == 0) {
+                sh.xs.dsum = QE[4];
+                sh.xs.first_e = vals[0];
+                sh.xs.cut_idx = -1;
+            }
             mark(DBG_P2);
             cluster.sync();  // ---- #2
             mark(DBG_W2);
             // peers' values read in parallel (lane rr reads CTA rr), folded in rank order
-            double sum = 0.0;
+            double sum = 0.0, offE = 0.0;
+            float e_first;
             {
-                const double x = lane < C ? remote_xs(lane)->dsum : 0.0;
-                for (int rr = 0; rr < C; rr++) sum = sum + __shfl_sync(0xffffffffu, x, rr);
+                Xch *x = remote_xs(lane < C ? lane : 0);
+                const double xd = lane < C ? x->dsum : 0.0;
+                e_first = __shfl_sync(0xffffffffu, x->first_e, 0);
+                for (int rr = 0; rr < C; rr++) {
+                    if (rr == rank) offE = sum;
+                    sum = sum + __shfl_sync(0xffffffffu, xd, rr);
+                }
             }
 
             Chain ch;
@@ -1332,9 +1387,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         nk++;
                     }
                 }
-                const double s2 = block_allreduce(csum_val(s2c), sh.red_d, [](double x, double y) { return x + y; });
-                const double sall = block_allreduce(csum_val(sac), sh.red_d, [](double x, double y) { return x + y; });
-                nk = block_allreduce(nk, sh.red_i, [](int x, int y) { return x + y; });
+                const double s2 = block_allreduce(csum_val(s2c), sh.red_d, [](double x, double y) { return x + y; }, 0.0);
+                const double sall = block_allreduce(csum_val(sac), sh.red_d, [](double x, double y) { return x + y; }, 0.0);
+                nk = block_allreduce(nk, sh.red_i, [](int x, int y) { return x + y; }, 0);
                 if (tid == 0) {
                     sh.xs.s2 = s2;
                     sh.xs.s2all = sall;
@@ -1357,18 +1412,30 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 ch.inv_s2 = __double2float_rn(1.0 / (ch.nokept ? SA : S2));
             }
 
-            // P3: sums of the list probabilities over this thread's four sub-chunks
+            const bool trk = ch.minp && !ch.nokept;
+            double P0[4], P1[4], grand = 0.0;
+            int gfm = INT_MAX, glm = -1;
+            float gfw = 0.0f;
+            if (!trk) {
+                // every element is on the list and w = fl(e * inv_sum) [* inv_s2]: prefix sums of
+                // w from those of e (the per-element roundings add ~1e-10 at most in practice)
+                const double sw = ch.minp ? (double)ch.inv_sum * (double)ch.inv_s2 : (double)ch.inv_sum;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    P0[q] = sw * (offE + (QE[q] + exE[q]));
+                    P1[q] = sw * (offE + (QE[q] + inE[q]));
+                }
+                grand = sw * sum;
+                gfm = 0;
+                gfw = w_of(ch, e_first);
+                glm = V - 1;
+            } else {
+            // P3 (min-p filters the list): sums of the list probabilities over this thread's
+            // four sub-chunks
             double subd[4];
             int fmem = INT_MAX, lmem = -1;
             float fw = 0.0f;
-            if (ch.minp && !ch.nokept) p3_scan<true, true, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
-            else if (ch.minp) p3_scan<false, true, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
-            else p3_scan<false, false, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
-            if (!(ch.minp && !ch.nokept) && tid == 0 && slen > 0) {
-                fmem = slice0;
-                fw = w_of(ch, vals[0]);
-                lmem = slice0 + slen - 1;
-            }
+            p3_scan<true, true, NV4>(vals, kb, slen, slice0, ch, subd, fmem, lmem, fw);
             mark(DBG_P3L);
             double excl[4], incl[4], qtot[4];
             block_scan4_d(subd, sh.red_d, excl, incl, qtot);
@@ -1377,21 +1444,18 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             Q[0] = 0.0;
 #pragma unroll
             for (int q = 0; q < 4; q++) Q[q + 1] = Q[q] + qtot[q];
-            const int bfm = block_allreduce(fmem, sh.red_i, [](int x, int y) { return min(x, y); });
-            const int blm = block_allreduce(lmem, sh.red_i2, [](int x, int y) { return max(x, y); });
+            const int bfm = block_allreduce(fmem, sh.red_i, [](int x, int y) { return min(x, y); }, INT_MAX);
+            const int blm = block_allreduce(lmem, sh.red_i2, [](int x, int y) { return max(x, y); }, INT_MIN);
             if (fmem == bfm && fmem != INT_MAX) sh.xs.first_w = fw;
             if (tid == 0) {
                 sh.xs.tot = Q[4];
                 sh.xs.first_member = bfm;
                 sh.xs.last_member = blm;
-                sh.xs.cut_idx = -1;
             }
             mark(DBG_P3);
             cluster.sync();  // ---- #3
             mark(DBG_W3);
-            double off = 0.0, grand = 0.0;
-            int gfm = INT_MAX, glm = -1;
-            float gfw = 0.0f;
+            double off = 0.0;
             {
                 Xch *x = remote_xs(lane < C ? lane : 0);
                 const double xt = lane < C ? x->tot : 0.0;
@@ -1410,11 +1474,11 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     glm = max(glm, __shfl_sync(0xffffffffu, xl, rr));
                 }
             }
-            double P0[4], P1[4];
 #pragma unroll
             for (int q = 0; q < 4; q++) {
                 P0[q] = off + (Q[q] + excl[q]);
                 P1[q] = off + (Q[q] + incl[q]);
+            }
             }
 
             int last_idx = ch.minp && !ch.nokept ? glm : V - 1;
@@ -1579,61 +1643,78 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
                 WRec *recs = row_recs(a, row);
                 float *stash = row_stash(a, row);
+                // warp records for the four quarters, computed side by side (their shuffle
+                // chains overlap).  Per quarter: the prefix of CLEAN sub-chunks in one binade,
+                // an optional boundary sub-chunk, and the suffix after it (PBS), else MIXED.
+                int ctype[4], ce[4];
+                uint32_t c0[4], c1[4];
+                unsigned cleanm[4], nonconf[4];
+                int e_first[4], jx[4], sfrom[4], e_s[4], type[4], bchunk[4];
+                uint32_t a0[4], a1[4], b0[4], b1[4];
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const uint32_t lim = gb[q] + (1u << 23);
+                    ctype[q] = !anyq[q] ? REC_IDENT
+                                        : ((pred[q] && fbits(g0[q]) < lim && fbits(g1[q]) < lim) ? REC_CLEAN : REC_MIXED);
+                    ce[q] = (int)(gb[q] >> 23);
+                    c0[q] = fbits(g0[q]) - gb[q];
+                    c1[q] = fbits(g1[q]) - (gb[q] | 1u);
+                    cleanm[q] = __ballot_sync(0xffffffffu, ctype[q] == REC_CLEAN);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    e_first[q] = cleanm[q] ? __shfl_sync(0xffffffffu, ce[q], __ffs(cleanm[q]) - 1) : 0;
+                    nonconf[q] = __ballot_sync(0xffffffffu, ctype[q] == REC_MIXED ||
+                                                                (ctype[q] == REC_CLEAN && ce[q] != e_first[q]));
+                    jx[q] = nonconf[q] ? __ffs(nonconf[q]) - 1 : 32;
+                    const bool pin = lane < jx[q] && ctype[q] == REC_CLEAN;
+                    a0[q] = pin ? c0[q] : 0u;
+                    a1[q] = pin ? c1[q] : 0u;
+                }
+                compose_scan4(a0, a1);
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const int tj = __shfl_sync(0xffffffffu, ctype[q], jx[q] & 31);
+                    sfrom[q] = !nonconf[q] ? 32 : (tj == REC_MIXED ? jx[q] + 1 : jx[q]);
+                    bchunk[q] = nonconf[q] && tj == REC_MIXED ? jx[q] : -1;
+                    const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom[q] && ctype[q] == REC_CLEAN);
+                    e_s[q] = sclean ? __shfl_sync(0xffffffffu, ce[q], __ffs(sclean) - 1) : 0;
+                    const unsigned sbad = __ballot_sync(
+                        0xffffffffu, lane >= sfrom[q] && (ctype[q] == REC_MIXED || (ctype[q] == REC_CLEAN && ce[q] != e_s[q])));
+                    type[q] = !nonconf[q] ? (cleanm[q] ? REC_CLEAN : REC_IDENT) : (sbad ? REC_MIXED : REC_PBS);
+                    const bool sin = lane >= sfrom[q] && ctype[q] == REC_CLEAN;
+                    b0[q] = sin ? c0[q] : 0u;
+                    b1[q] = sin ? c1[q] : 0u;
+                }
+                compose_scan4(b0, b1);
+                // stash / wide slots for the four quarters: one claim per warp on CTA 0's counter
+                bool need_st[4], need_wd[4];
+                int n_st = 0, n_wd = 0;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    need_st[q] = type[q] == REC_PBS && bchunk[q] >= 0;
+                    need_wd[q] = type[q] == REC_MIXED || __any_sync(0xffffffffu, near[q]);
+                    n_st += need_st[q];
+                    n_wd += need_wd[q];
+                }
+                int st_next = 0, wd_next = 0;
+                if (n_st + n_wd) {
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&remote_xs(0)->slots, n_st | (n_wd << 16));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    st_next = base & 0xffff;
+                    wd_next = base >> 16;
+                }
 #pragma unroll 1
                 for (int q = 0; q < 4; q++) {
-                    // register selects instead of dynamic indexing, which would put the arrays in local memory
-                    const uint32_t gbq = pick4(gb, q), g0q = fbits(pick4(g0, q)), g1q = fbits(pick4(g1, q));
-                    const bool anyqq = pick4(anyq, q), predq = pick4(pred, q), nearq = pick4(near, q);
-                    const uint32_t lim = gbq + (1u << 23);
-                    const int ctype = !anyqq ? REC_IDENT : ((predq && g0q < lim && g1q < lim) ? REC_CLEAN : REC_MIXED);
-                    const int ce = (int)(gbq >> 23);
-                    const uint32_t c0 = g0q - gbq, c1 = g1q - (gbq | 1u);
-                    // warp record over the 32 sub-chunks (q, 32*wid .. 32*wid+31)
-                    const unsigned cleanm = __ballot_sync(0xffffffffu, ctype == REC_CLEAN);
-                    const int e_first = cleanm ? __shfl_sync(0xffffffffu, ce, __ffs(cleanm) - 1) : 0;
-                    const unsigned nonconf =
-                        __ballot_sync(0xffffffffu, ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_first));
-                    int type, bchunk = -1, sfrom = 32, e_s = 0;
-                    uint32_t p0, p1, s0 = 0u, s1 = 0u;
-                    if (!nonconf) {
-                        uint32_t a0 = ctype == REC_CLEAN ? c0 : 0u, a1 = ctype == REC_CLEAN ? c1 : 0u;
-                        compose_scan(a0, a1);
-                        type = cleanm ? REC_CLEAN : REC_IDENT;
-                        p0 = __shfl_sync(0xffffffffu, a0, 31);
-                        p1 = __shfl_sync(0xffffffffu, a1, 31);
-                    } else {
-                        const int j = __ffs(nonconf) - 1;
-                        uint32_t a0 = (lane < j && ctype == REC_CLEAN) ? c0 : 0u;
-                        uint32_t a1 = (lane < j && ctype == REC_CLEAN) ? c1 : 0u;
-                        compose_scan(a0, a1);
-                        p0 = __shfl_sync(0xffffffffu, a0, 31);
-                        p1 = __shfl_sync(0xffffffffu, a1, 31);
-                        const int tj = __shfl_sync(0xffffffffu, ctype, j);
-                        // the suffix starts after a MIXED boundary sub-chunk, or at a CLEAN sub-chunk
-                        // j that already lies in the next binade
-                        sfrom = tj == REC_MIXED ? j + 1 : j;
-                        const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom && ctype == REC_CLEAN);
-                        e_s = sclean ? __shfl_sync(0xffffffffu, ce, __ffs(sclean) - 1) : 0;
-                        const unsigned sbad = __ballot_sync(
-                            0xffffffffu, lane >= sfrom && (ctype == REC_MIXED || (ctype == REC_CLEAN && ce != e_s)));
-                        uint32_t b0 = (lane >= sfrom && ctype == REC_CLEAN) ? c0 : 0u;
-                        uint32_t b1 = (lane >= sfrom && ctype == REC_CLEAN) ? c1 : 0u;
-                        compose_scan(b0, b1);
-                        s0 = __shfl_sync(0xffffffffu, b0, 31);
-                        s1 = __shfl_sync(0xffffffffu, b1, 31);
-                        type = sbad ? REC_MIXED : REC_PBS;
-                        bchunk = tj == REC_MIXED ? j : -1;
-                    }
+                    const int typeq = pick4(type, q), bchunkq = pick4(bchunk, q);
                     // boundary sub-chunk probabilities -> a stash slot (when one is free)
                     int nslot = -1, wslot = -1;
-                    if (type == REC_PBS && bchunk >= 0) {
-                        if (lane == 0) {
-                            nslot = atomicAdd(&hdr->nstash, 1);
-                            if (nslot >= STASH_SLOTS) nslot = -1;
-                        }
-                        nslot = __shfl_sync(0xffffffffu, nslot, 0);
+                    if (pick4(need_st, q)) {
+                        nslot = st_next < STASH_SLOTS ? st_next : -1;
+                        st_next++;
                         if (nslot >= 0) {
-                            const int sb = (q * NT + 32 * wid + bchunk) * SUBT;
+                            const int sb = (q * NT + 32 * wid + bchunkq) * SUBT;
                             float *qs = stash + nslot * STASH_STRIDE;
                             if (lane == 0) qs[0] = __int_as_float(slice0 + sb);
                             for (int k = lane; k < SUBT; k += 32) qs[1 + k] = q_of(ch, vals[sb + k], slice0 + sb + k);
@@ -1643,12 +1724,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     }
                     // several binade changes in this warp's range, or the draw may land in it:
                     // keep every probability so the walk replays them without recomputing
-                    if (type == REC_MIXED || __any_sync(0xffffffffu, nearq)) {
-                        if (lane == 0) {
-                            wslot = atomicAdd(&hdr->nwide, 1);
-                            if (wslot >= WIDE_SLOTS) wslot = -1;
-                        }
-                        wslot = __shfl_sync(0xffffffffu, wslot, 0);
+                    if (pick4(need_wd, q)) {
+                        wslot = wd_next < WIDE_SLOTS ? wd_next : -1;
+                        wd_next++;
                         if (wslot >= 0) {
                             const int kq = pick4(kb, q);
                             float *ws = row_wide(a, row) + wslot * WIDE_STRIDE + lane * SUBT;
@@ -1664,17 +1742,17 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                             dbg_add(DBG_STASH_MISS, 1);
                         }
                     }
-                    if (lane == 0) {
+                    if (lane == 31) {
                         WRec wr;
-                        wr.meta = pack_meta(type, bchunk, sfrom, e_first, e_s);
-                        wr.p0 = p0;
-                        wr.p1 = p1;
-                        wr.s0 = s0;
-                        wr.s1 = s1;
+                        wr.meta = pack_meta(typeq, bchunkq, pick4(sfrom, q), pick4(e_first, q), pick4(e_s, q));
+                        wr.p0 = pick4(a0, q);
+                        wr.p1 = pick4(a1, q);
+                        wr.s0 = pick4(b0, q);
+                        wr.s1 = pick4(b1, q);
                         wr.nslot = (int16_t)nslot;
                         wr.wslot = (int16_t)wslot;
                         recs[rank * 4 * NW + q * NW + wid] = wr;
-                        if (type == REC_PBS && timing) dbg_add(DBG_PBS, 1);
+                        if (typeq == REC_PBS && timing) dbg_add(DBG_PBS, 1);
                     }
                 }
             }
@@ -1691,6 +1769,10 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         mark(DBG_TOPK);
         fence_proxy_async();  // order this row's generic accesses of the slice before the next bulk copy
         cluster.sync();       // ---- end of row: peers may reuse their shared memory
+        if (!done && rank == 0 && tid == 0) {
+            hdr->nstash = sh.xs.slots & 0xffff;  // slots claimed by every CTA (all claims are done)
+            hdr->nwide = sh.xs.slots >> 16;
+        }
         if (dbuf && tid == 0 && use_tma && row + 2 * ncl < a.rows) issue_row_copy(row + 2 * ncl, buf);
         mark(DBG_WEND);
     }
