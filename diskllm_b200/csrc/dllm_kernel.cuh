@@ -217,6 +217,12 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Cluster barrier without release/acquire semantics: execution ordering only, so it does not wait
+// for this thread's outstanding global stores.  Used where the barrier only separates reads of a
+// peer's shared memory (already consumed before the arrive) from later writes to it.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+}
 
 // ----------------------------------------------------------------------------------------
 // block / warp helpers (deterministic: every thread computes identical results)
@@ -379,11 +385,12 @@ __device__ __forceinline__ bool apply_run(uint32_t &cb, int e, uint32_t n0, uint
 }
 
 // One step of the walk over up to 32 records held one per lane (lanes >= n invalid), from
-// record `pos`.  Either processes a run of valid CLEAN/IDENT records, or expands one record.
-// Returns the drawn index (>= 0), -1 to continue (pos advanced), -2 on an internal error.
-template <class Expand>
-__device__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t n1, uint32_t &cb,
-                         float r, Expand &&expand) {
+// record `pos`.  Either applies a run of valid CLEAN/IDENT records, or asks the caller to expand
+// one record: returns WALK_EXPAND with *xj = that record and cb set to the running sum at its
+// start (*must_hit: the draw lies in it).  Returns -1 to continue (pos advanced).
+constexpr int WALK_EXPAND = -3;
+__device__ __forceinline__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t n1, uint32_t &cb,
+                                         float r, int *xj, bool *must_hit) {
     const int lane = threadIdx.x & 31;
     if (lane == 0) dbg_add(DBG_STEPS, 1);
     const unsigned live = __ballot_sync(0xffffffffu, lane >= pos && lane < n && type != REC_IDENT);
@@ -395,10 +402,10 @@ __device__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t
     const int tf = __shfl_sync(0xffffffffu, type, f);
     const int ef = __shfl_sync(0xffffffffu, e, f);
     const bool inbin = cb != 0u && (cb >> 23) == (uint32_t)ef;
+    *must_hit = false;
     if (tf != REC_CLEAN || !inbin) {
-        int res = expand(f, cb);
-        pos = f + 1;
-        return res;
+        *xj = f;
+        return WALK_EXPAND;
     }
     const unsigned runm = __ballot_sync(0xffffffffu, lane >= f && lane < n &&
                                                          (type == REC_IDENT || (type == REC_CLEAN && e == ef)));
@@ -420,19 +427,41 @@ __device__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t
         const int l = __ffs(hit) - 1;
         const uint32_t prevl = __shfl_sync(0xffffffffu, prev, l);
         cb = (l == f) ? cb : prevl;
-        int res = expand(l, cb);
-        pos = n;
-        return res >= 0 ? res : -2;
+        *xj = l;
+        *must_hit = true;
+        return WALK_EXPAND;
     }
     const uint32_t last = __shfl_sync(0xffffffffu, cout, good_end > f ? good_end - 1 : f);
     if (good_end > f) cb = last;
     pos = good_end;
     if (pos < run_end) {
-        int res = expand(pos, cb);
-        pos = pos + 1;
-        return res;
+        *xj = pos;
+        return WALK_EXPAND;
     }
     return -1;
+}
+
+// Runs walk steps over the 32 lane records until the draw is found (>= 0), the records are
+// exhausted (-1) or an error (-2); `expand(j, cb)` expands record j.
+template <class Expand>
+__device__ __forceinline__ int walk_records(int n, int type, int e, uint32_t n0, uint32_t n1, uint32_t &cb, float r,
+                                            int guard_max, Expand &&expand) {
+    int pos = 0, res = -1;
+    for (int guard = 0; pos < n && res == -1 && guard < guard_max; guard++) {
+        int xj = 0;
+        bool must_hit = false;
+        res = walk_step(n, pos, type, e, n0, n1, cb, r, &xj, &must_hit);
+        if (res == WALK_EXPAND) {
+            res = expand(xj, cb);
+            if (must_hit) {
+                pos = n;
+                if (res < 0) res = -2;
+            } else {
+                pos = xj + 1;
+            }
+        }
+    }
+    return pos < n && res == -1 ? -2 : res;
 }
 
 // Replays n consecutive draw probabilities src[0..n) (shared memory) on the exact running sum
@@ -440,7 +469,7 @@ __device__ int walk_step(int n, int &pos, int type, int e, uint32_t n0, uint32_t
 // as a run record; runs that stay in one binade are composed in parallel, the others are
 // replayed serially by their lane.  `gbase + j` is the index of element j.  Returns the drawn
 // index, -1 (not in this range; cb advanced past it) or -2.
-__device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float *src) {
+__device__ __noinline__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float *src) {
     const int lane = threadIdx.x & 31;
     const int s = (n + 31) >> 5;
     const int j0 = lane * s;
@@ -487,7 +516,14 @@ __device__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float
         }
         const int type = !anyq ? REC_IDENT : ((fbits(g0) < lim && fbits(g1) < lim) ? REC_CLEAN : REC_MIXED);
         const uint32_t n0 = fbits(g0) - gb, n1 = fbits(g1) - (gb | 1u);
-        int res = walk_step(32, pos, type, (int)eb, n0, n1, cb, r, serial);
+        int xj = 0;
+        bool must_hit = false;
+        int res = walk_step(32, pos, type, (int)eb, n0, n1, cb, r, &xj, &must_hit);
+        if (res == WALK_EXPAND) {
+            res = serial(xj, cb);
+            if (must_hit) return res >= 0 ? res : -2;
+            pos = xj + 1;
+        }
         if (res != -1) return res;
     }
     return pos < 32 ? -2 : -1;
@@ -918,7 +954,10 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 if (it > 0) issue_row_copy(row, 0);
                 if (row + ncl < a.rows) prefetch_row(row + ncl);
             }
-            if (rank == 0) sh.xs.slots = 0;
+            if (rank == 0) {
+                sh.xs.slots = 0;
+                hdr->nstash = 0;
+            }
         }
         for (int i = tid; i < a.htab; i += NT) {
             hkeys[i] = -1;
@@ -1492,14 +1531,22 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 } else {
                     // the single sub-chunk where (float)cumsum first reaches top_p; its warp finds
                     // the cut element cooperatively
+                    int qx = -1;
+                    unsigned cmx = 0u;
 #pragma unroll
                     for (int q = 0; q < 4; q++) {
                         const bool crosses = __double2float_rn(P1[q]) >= tp && !(__double2float_rn(P0[q]) >= tp);
                         const unsigned cm = __ballot_sync(0xffffffffu, crosses);
-                        if (cm) {
-                            const int src = __ffs(cm) - 1;
-                            const double base = __shfl_sync(0xffffffffu, P0[q], src);
-                            const int cb0 = __shfl_sync(0xffffffffu, kb[q], src);
+                        if (cm && qx < 0) {
+                            qx = q;
+                            cmx = cm;
+                        }
+                    }
+                    {
+                        if (qx >= 0) {
+                            const int src = __ffs(cmx) - 1;
+                            const double base = __shfl_sync(0xffffffffu, pick4(P0, qx), src);
+                            const int cb0 = __shfl_sync(0xffffffffu, pick4(kb, qx), src);
                             constexpr int SL = (SUBT + 31) / 32;
                             const int j0 = lane * SL;
                             double part = 0.0;
@@ -1634,10 +1681,11 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 #pragma unroll
                 for (int q = 0; q < 4; q++) anyq[q] = qmax[q] > 0.0f;
                 if (pr) {
-#pragma unroll
+#pragma unroll 1
                     for (int q = 0; q < 4; q++)
+#pragma unroll 1
                         for (int j = 0; j < SUBT; j++) {
-                            const int li = kb[q] + j;
+                            const int li = pick4(kb, q) + j;
                             if (li < slen) pr[li] = q_of(ch, vals[li], slice0 + li);
                         }
                 }
@@ -1704,6 +1752,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     base = __shfl_sync(0xffffffffu, base, 0);
                     st_next = base & 0xffff;
                     wd_next = base >> 16;
+                    // stash slots in use for the walk kernel (no value returned: nothing waits)
+                    if (lane == 0 && n_st) atomicMax(&hdr->nstash, min(st_next + n_st, STASH_SLOTS));
                 }
 #pragma unroll 1
                 for (int q = 0; q < 4; q++) {
@@ -1730,6 +1780,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         if (wslot >= 0) {
                             const int kq = pick4(kb, q);
                             float *ws = row_wide(a, row) + wslot * WIDE_STRIDE + lane * SUBT;
+#pragma unroll 1
                             for (int k = 0; k < SUBT; k += 4) {
                                 float4 o;
                                 o.x = q_of(ch, vals[kq + k], slice0 + kq + k);
@@ -1767,12 +1818,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             hdr->done = 1;
         }
         mark(DBG_TOPK);
-        fence_proxy_async();  // order this row's generic accesses of the slice before the next bulk copy
-        cluster.sync();       // ---- end of row: peers may reuse their shared memory
-        if (!done && rank == 0 && tid == 0) {
-            hdr->nstash = sh.xs.slots & 0xffff;  // slots claimed by every CTA (all claims are done)
-            hdr->nwide = sh.xs.slots >> 16;
-        }
+        fence_proxy_async();    // order this row's generic accesses of the slice before the next bulk copy
+        cluster_sync_relaxed();  // ---- end of row: peers may reuse their shared memory
         if (dbuf && tid == 0 && use_tma && row + 2 * ncl < a.rows) issue_row_copy(row + 2 * ncl, buf);
         mark(DBG_WEND);
     }
@@ -1907,11 +1954,11 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
             const float *src = (const float *)a.logits + (int64_t)row * a.row_stride + start;
             for (int i = lane; i < nc / 4; i += 32) cp_async16(rv + 4 * i, src + 4 * i);
         }
-#pragma unroll 4
+#pragma unroll 1
         for (int i = nc + lane; i < n; i += 32) rv[i] = raw_of(start + i);
         cp_async_wait_all();
         __syncwarp();
-#pragma unroll 4
+#pragma unroll 1
         for (int i = lane; i < n; i += 32) {
             const int li = start + i;
             float v = rv[i];
@@ -1936,7 +1983,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
         if (lane < n) wl = recs[gw0 + lane];
         const int ty = (int)(wl.meta & 3u);
         const int ep = (int)((wl.meta >> 16) & 255u);
-        auto expandA0 = [&](int j, uint32_t &cbv) __attribute__((always_inline)) -> int {
+        auto expandA0 = [&](int j, uint32_t &cbv) -> int {
             if (lane == 0) dbg_add(DBG_EXPAND, 1);
             const int g = gw0 + j;
             const int rr = g / (4 * NW), kk = g % (4 * NW), q = kk / NW, w = kk % NW;
@@ -1962,39 +2009,58 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                 return res;
             };
             const uint32_t meta = __shfl_sync(0xffffffffu, wl.meta, j);
+            // at most two replays (a PBS record's boundary sub-chunk, then its suffix) through
+            // one call site: stage 0 whole range, 1 boundary, 2 suffix check, 3 suffix
+            int st = start, nn = 32 * SUBT, stage = 0;
+            uint32_t c = cbv, s0 = 0u, s1 = 0u;
+            int esuf = 0, sfrom = 32;
             if ((int)(meta & 3u) == REC_PBS) {
                 const int bc = (int)((meta >> 2) & 63u);
-                const int sfrom = (int)((meta >> 8) & 63u);
-                const int epre = (int)((meta >> 16) & 255u), esuf = (int)(meta >> 24);
+                const int epre = (int)((meta >> 16) & 255u);
+                sfrom = (int)((meta >> 8) & 63u);
+                esuf = (int)(meta >> 24);
                 const uint32_t p0 = __shfl_sync(0xffffffffu, wl.p0, j), p1 = __shfl_sync(0xffffffffu, wl.p1, j);
-                const uint32_t s0 = __shfl_sync(0xffffffffu, wl.s0, j), s1 = __shfl_sync(0xffffffffu, wl.s1, j);
+                s0 = __shfl_sync(0xffffffffu, wl.s0, j);
+                s1 = __shfl_sync(0xffffffffu, wl.s1, j);
                 const int slot = __shfl_sync(0xffffffffu, (int)wl.nslot, j);
-                uint32_t c = cbv;
                 if (apply_run(c, epre, p0, p1) && !(r < bitsf(c))) {
-                    if (bc != 63) {
-                        int found;
-                        if (slot >= 0) {
-                            const float *qs = stash + slot * STASH_STRIDE;
-                            found = replay_elems(SUBT, __float_as_int(qs[0]), c, r, qs + 1);
-                        } else {
-                            found = replay_clamped(start + bc * SUBT, SUBT, c);
-                        }
+                    stage = 2;
+                    if (bc != 63 && slot >= 0) {
+                        const float *qs = stash + slot * STASH_STRIDE;
+                        const int found = replay_elems(SUBT, __float_as_int(qs[0]), c, r, qs + 1);
                         if (found != -1) return found;
+                    } else if (bc != 63) {
+                        st = start + bc * SUBT;
+                        nn = SUBT;
+                        stage = 1;
                     }
+                } else {
+                    c = cbv;
+                }
+            }
+            for (int it = 0; it < 2; it++) {
+                if (stage == 2) {
                     uint32_t c2 = c;
                     if (apply_run(c2, esuf, s0, s1) && !(r < bitsf(c2))) {
                         cbv = c2;
                         return -1;
                     }
-                    cbv = c;
-                    return replay_clamped(start + sfrom * SUBT, (32 - sfrom) * SUBT, cbv);
+                    st = start + sfrom * SUBT;
+                    nn = (32 - sfrom) * SUBT;
+                    stage = 3;
                 }
+                const int found = replay_clamped(st, nn, c);
+                if (found != -1 || stage != 1) {
+                    cbv = c;
+                    return found;
+                }
+                stage = 2;
             }
-            return replay_clamped(start, 32 * SUBT, cbv);
+            cbv = c;
+            return -2;
         };
         const int tyw = ty == REC_PBS ? REC_MIXED : ty;
-        int pos = 0;
-        while (pos < n && res == -1) res = walk_step(n, pos, tyw, ep, wl.p0, wl.p1, cb, r, expandA0);
+        res = walk_records(n, tyw, ep, wl.p0, wl.p1, cb, r, 1 << 12, expandA0);
     }
     if (lane == 0) {
         int flags = h.flags;
