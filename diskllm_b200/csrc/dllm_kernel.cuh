@@ -63,9 +63,8 @@ typedef void (*KernelFn)(const KernelArgs);
 // Row scalars kept in the workspace for the walk kernel (128 bytes).
 struct RowHdr {
     float M, inv_temp, mv, inv_sum, min_p, inv_s2, inv_s3, r;
-    int cut_idx, last_idx, flags, done, minp, nokept, topp, nstash;
-    int nwide;  // wide stash slots claimed
-    int pad[15];
+    int cut_idx, last_idx, flags, done, minp, nokept, topp;
+    int pad[17];
 };
 // Warp-level draw record (24 bytes).  meta: type (bits 0-1), boundary sub-chunk (2-7, 63 =
 // none), first suffix sub-chunk (8-13), prefix binade (16-23), suffix binade (24-31).
@@ -80,6 +79,7 @@ struct WRec {
 namespace {
 
 constexpr int MAXW = 16;          // warps per CTA (blockDim <= 512)
+constexpr int MAXC = 16;          // CTAs per cluster
 constexpr int CAND_CAP = 2048;    // top-k survivors gathered in CTA 0
 constexpr int TMA_PIECE = 32768;  // bytes per bulk copy instruction
 constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
@@ -146,14 +146,36 @@ struct Xch {
     uint32_t theta;
     int cnt_gt, cnt_eq;
     int ncand;        // CTA 0: survivors gathered
-    int slots;        // CTA 0: stash slots (low 16 bits) and wide slots (high 16) claimed by
-                      // atomics of every CTA of the cluster; reset at the start of each row
     unsigned hist[2][256];
+};
+
+// Values pushed into every CTA of the cluster (st.async with mbarrier completion), one slot per
+// source rank and row parity: #1 the penalised maximum, #2 the exponential sum, #4 the cut.
+// (aligned to their size: st.async .v2 / .v4 destinations must be 8- / 16-byte aligned)
+struct __align__(8) Push1 {
+    float m;
+    int flags;
+};
+struct __align__(16) Push2 {
+    double dsum;
+    float first_e;
+    int pad;
+};
+struct __align__(16) Push4 {
+    int cut_idx;
+    int pad;
+    double cut_s3;
 };
 
 struct Shared {
     Xch xs;
     unsigned long long tma_bar[2];
+    unsigned long long xbar[3][2];  // push exchanges #1, #2, #4 by row parity
+    Push1 in1[2][MAXC];
+    Push2 in2[2][MAXC];
+    Push4 in4[2][MAXC];
+    static_assert(sizeof(Push1) == 8 && sizeof(Push2) == 16 && sizeof(Push4) == 16, "push payload sizes");
+    int slots[2];                   // CTA 0: stash / wide slot claims by row parity
     double red_d[4 * MAXW];
     float red_f[MAXW];
     int red_i[4 * MAXW];
@@ -217,6 +239,38 @@ __device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+// 8- / 16-byte asynchronous store into CTA `rank`'s copy of `slot`, completing on its copy of `bar`
+__device__ __forceinline__ void push8(void *slot, unsigned long long *bar, uint32_t rank, uint32_t x, uint32_t y) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(
+                     mapa_rank(smem_u32(slot), rank)),
+                 "r"(x), "r"(y), "r"(mapa_rank(smem_u32(bar), rank))
+                 : "memory");
+}
+__device__ __forceinline__ void push16(void *slot, unsigned long long *bar, uint32_t rank, uint32_t x, uint32_t y,
+                                       uint32_t z, uint32_t w) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     mapa_rank(smem_u32(slot), rank)),
+                 "r"(x), "r"(y), "r"(z), "r"(w), "r"(mapa_rank(smem_u32(bar), rank))
+                 : "memory");
+}
+// acquire at cluster scope: the completing st.async writes came from other CTAs
+__device__ __forceinline__ bool mbar_try_wait_cluster(unsigned long long *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // Cluster barrier without release/acquire semantics: execution ordering only, so it does not wait
 // for this thread's outstanding global stores.  Used where the barrier only separates reads of a
 // peer's shared memory (already consumed before the arrive) from later writes to it.
@@ -894,9 +948,30 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         g_dbg = a.dbg;
         mbar_init(&sh.tma_bar[0], 1);
         mbar_init(&sh.tma_bar[1], 1);
+        for (int k = 0; k < 3; k++)
+            for (int b = 0; b < 2; b++) mbar_init(&sh.xbar[k][b], 1);
+        sh.slots[0] = sh.slots[1] = 0;
         fence_proxy_async();
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    __syncthreads();
+    // every CTA's exchange barriers exist before any peer pushes into them
+    cluster.sync();
+    uint32_t xph = 0u;  // phase bit per exchange barrier (bit 2k + parity)
+    // Push exchange k of the row with parity par: threads 0..C-1 push this CTA's payload to rank
+    // tid, then every thread waits (bounded) for the C payloads addressed to this CTA.
+    auto xwait = [&](int k, int par) -> bool {
+        const uint32_t bit = 1u << (2 * k + par);
+        long long it2 = 0;
+        bool ok = true;
+        while (!mbar_try_wait_cluster(&sh.xbar[k][par], (xph & bit) ? 1u : 0u)) {
+            if (++it2 > WAIT_LIMIT) {
+                ok = false;
+                break;
+            }
+        }
+        xph ^= bit;
+        return ok;
+    };
 
     const bool timing = a.dbg != nullptr && rank == 0 && tid == 0;
     long long tmark = clock64();
@@ -954,10 +1029,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 if (it > 0) issue_row_copy(row, 0);
                 if (row + ncl < a.rows) prefetch_row(row + ncl);
             }
-            if (rank == 0) {
-                sh.xs.slots = 0;
-                hdr->nstash = 0;
-            }
+            // CTA 0's slot counter of the next row (its last claims, two rows back, are done)
+            if (rank == 0) sh.slots[(it + 1) & 1] = 0;
+            sh.xs.cut_idx = -1;
         }
         for (int i = tid; i < a.htab; i += NT) {
             hkeys[i] = -1;
@@ -1083,12 +1157,15 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             float *po = a.pen_out + (int64_t)row * a.pen_stride + slice0;
             for (int i = tid; i < slen; i += NT) po[i] = vals[i];
         }
+        const int par = it & 1;
         if (tid == 0) {
             sh.xs.m = lm;
             sh.xs.flags = flags;
+            mbar_arrive_expect_tx(&sh.xbar[0][par], (uint32_t)(C * sizeof(Push1)));
         }
+        if (tid < C) push8(&sh.in1[par][rank], &sh.xbar[0][par], tid, __float_as_uint(lm), (uint32_t)flags);
         mark(DBG_P1);
-        cluster.sync();  // ---- #1
+        const bool to1 = !xwait(0, par);  // ---- #1
         mark(DBG_W1);
         float M = -INFINITY;
         int rowflags = 0;
@@ -1096,12 +1173,12 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             float mv = -INFINITY;
             int fv = 0;
             if (lane < C) {
-                Xch *x = remote_xs(lane);
-                mv = x->m;
-                fv = x->flags;
+                mv = sh.in1[par][lane].m;
+                fv = sh.in1[par][lane].flags;
             }
             M = warp_allreduce(mv, [](float x, float y) { return fmaxf(x, y); });
             rowflags = warp_allreduce(fv, [](int x, int y) { return x | y; });
+            if (to1) rowflags |= ROW_ERR_TIMEOUT;
         }
 
         const bool greedy = p.temperature == 0.0f;
@@ -1384,21 +1461,21 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             QE[0] = 0.0;
 #pragma unroll
             for (int q = 0; q < 4; q++) QE[q + 1] = QE[q] + totE[q];
-            if (tid == 0) {
-                sh.xs.dsum = QE[4];
-                sh.xs.first_e = vals[0];
-                sh.xs.cut_idx = -1;
+            if (tid == 0) mbar_arrive_expect_tx(&sh.xbar[1][par], (uint32_t)(C * sizeof(Push2)));
+            if (tid < C) {
+                const unsigned long long db = (unsigned long long)__double_as_longlong(QE[4]);
+                push16(&sh.in2[par][rank], &sh.xbar[1][par], tid, (uint32_t)db, (uint32_t)(db >> 32),
+                       __float_as_uint(vals[0]), 0u);
             }
             mark(DBG_P2);
-            cluster.sync();  // ---- #2
+            if (!xwait(1, par)) rowflags |= ROW_ERR_TIMEOUT;  // ---- #2
             mark(DBG_W2);
-            // peers' values read in parallel (lane rr reads CTA rr), folded in rank order
+            // the pushed values, folded in rank order
             double sum = 0.0, offE = 0.0;
             float e_first;
             {
-                Xch *x = remote_xs(lane < C ? lane : 0);
-                const double xd = lane < C ? x->dsum : 0.0;
-                e_first = __shfl_sync(0xffffffffu, x->first_e, 0);
+                const double xd = lane < C ? sh.in2[par][lane].dsum : 0.0;
+                e_first = sh.in2[par][0].first_e;
                 for (int rr = 0; rr < C; rr++) {
                     if (rr == rank) offE = sum;
                     sum = sum + __shfl_sync(0xffffffffu, xd, rr);
@@ -1602,11 +1679,17 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                             }
                         }
                     }
-                    cluster.sync();  // ---- #4
+                    __syncthreads();
+                    if (tid == 0) mbar_arrive_expect_tx(&sh.xbar[2][par], (uint32_t)(C * sizeof(Push4)));
+                    if (tid < C) {
+                        const unsigned long long sb = (unsigned long long)__double_as_longlong(sh.xs.cut_s3);
+                        push16(&sh.in4[par][rank], &sh.xbar[2][par], tid, (uint32_t)sh.xs.cut_idx, 0u, (uint32_t)sb,
+                               (uint32_t)(sb >> 32));
+                    }
+                    if (!xwait(2, par)) rowflags |= ROW_ERR_TIMEOUT;  // ---- #4
                     {
-                        Xch *x = remote_xs(lane < C ? lane : 0);
-                        const int xc = lane < C ? x->cut_idx : -1;
-                        const double xs3 = lane < C ? x->cut_s3 : 0.0;
+                        const int xc = lane < C ? sh.in4[par][lane].cut_idx : -1;
+                        const double xs3 = lane < C ? sh.in4[par][lane].cut_s3 : 0.0;
                         const unsigned hm = __ballot_sync(0xffffffffu, xc >= 0);
                         if (hm) {
                             const int src = __ffs(hm) - 1;
@@ -1748,12 +1831,10 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 int st_next = 0, wd_next = 0;
                 if (n_st + n_wd) {
                     int base = 0;
-                    if (lane == 0) base = atomicAdd(&remote_xs(0)->slots, n_st | (n_wd << 16));
+                    if (lane == 0) base = atomicAdd(cluster.map_shared_rank(&sh.slots[par], 0), n_st | (n_wd << 16));
                     base = __shfl_sync(0xffffffffu, base, 0);
                     st_next = base & 0xffff;
                     wd_next = base >> 16;
-                    // stash slots in use for the walk kernel (no value returned: nothing waits)
-                    if (lane == 0 && n_st) atomicMax(&hdr->nstash, min(st_next + n_st, STASH_SLOTS));
                 }
 #pragma unroll 1
                 for (int q = 0; q < 4; q++) {
@@ -1850,7 +1931,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
         const unsigned char *grec = reinterpret_cast<const unsigned char *>(row_recs(a, row));
         const int nrec16 = (int)(((size_t)a.nrec * sizeof(WRec) + 15) / 16);
         for (int i = lane; i < nrec16; i += 32) cp_async16(wsm + 16 * i, grec + 16 * i);
-        const int ns = min(h.nstash, STASH_SLOTS);
+        const int ns = STASH_SLOTS;  // all slots: which ones are used shows only in the records
         const unsigned char *gst = reinterpret_cast<const unsigned char *>(row_stash(a, row));
         for (int i = lane; i < ns * STASH_STRIDE / 4; i += 32) cp_async16(wsm + recb + 16 * i, gst + 16 * i);
         cp_async_wait_all();
