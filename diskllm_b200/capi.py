@@ -33,6 +33,7 @@ ROW_ERR_TIMEOUT = 16
 EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
     "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
+    "dllm_cuda_set_timing_events",
     "dllm_sampler_get_rng_state", "dllm_sampler_set_rng_state",
     "sampler_create", "sampler_free", "sampler_apply_repetition_penalty",
     "sampler_apply_presence_penalty", "sampler_sample", "greedy_sample",
@@ -113,6 +114,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_sample_batch.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
     lib.dllm_cuda_set_debug_counters.restype = C.c_int
     lib.dllm_cuda_set_debug_counters.argtypes = [C.c_void_p]
+    lib.dllm_cuda_set_timing_events.restype = C.c_int
+    lib.dllm_cuda_set_timing_events.argtypes = [C.c_void_p, C.c_void_p]
     lib.dllm_cuda_sample_batch_static.restype = C.c_int
     lib.dllm_cuda_sample_batch_static.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
     lib.dllm_cuda_workspace_bytes.restype = C.c_size_t
@@ -137,6 +140,16 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
         f.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_float]
     _lib = lib
     return lib
+
+
+def set_timing_events(before=None, after=None):
+    """Has every later sampling call record the two torch.cuda.Event objects right before and
+    right after the cluster kernel (None, None switches it off)."""
+    b = None if before is None else before.cuda_event
+    a = None if after is None else after.cuda_event
+    rc = load_library().dllm_cuda_set_timing_events(b, a)
+    if rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_set_timing_events: {STATUS_NAMES.get(rc, rc)}")
 
 
 def set_debug_counters(tensor_or_none):

@@ -31,6 +31,9 @@ namespace dllm {
 void set_last_error_message(const char *msg) { snprintf(g_last_error, sizeof g_last_error, "%s", msg); }
 }  // namespace dllm
 
+extern "C" dllm_status dllm_cuda_set_timing_events(void *before, void *after) {
+    return set_timing_events((cudaEvent_t)before, (cudaEvent_t)after);
+}
 extern "C" dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters) {
     return set_debug_counters(device_counters);
 }

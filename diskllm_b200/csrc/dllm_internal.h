@@ -88,6 +88,7 @@ __host__ __device__ inline size_t walk_smem_per_warp(int nrec) {
 
 dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
 dllm_status set_debug_counters(unsigned long long *dev_counters);
+dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
 dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream);
 int nrec_for(const LaunchCfg &cfg);
 

@@ -747,15 +747,21 @@ __device__ __forceinline__ void block_scan4_d(const double v[4], double *scratch
 #pragma unroll
         for (int q = 0; q < 4; q++) scratch[q * MAXW + w] = x[q];
     __syncthreads();
+    // warp totals scanned by shuffles (lane i holds warp i's total); every warp computes the same
+    // sums in the same order, so all threads agree on the offsets and totals bit for bit
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-        double off = 0.0;
-        for (int i = 0; i < w; i++) off = off + scratch[q * MAXW + i];
-        double t = off;
-        for (int i = w; i < nw; i++) t = t + scratch[q * MAXW + i];
+        double y = lane < nw ? scratch[q * MAXW + lane] : 0.0;
+#pragma unroll
+        for (int o = 1; o < MAXW; o <<= 1) {
+            const double z = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) y = z + y;
+        }
+        const double ex = __shfl_up_sync(0xffffffffu, y, 1);
+        const double off = __shfl_sync(0xffffffffu, lane == 0 ? 0.0 : ex, w);
+        tot[q] = __shfl_sync(0xffffffffu, y, nw - 1);
         excl[q] = lane == 0 ? off : off + prev[q];
         incl[q] = off + x[q];
-        tot[q] = t;
     }
 }
 

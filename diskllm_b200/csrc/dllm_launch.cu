@@ -118,15 +118,18 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
                 KernelFn fn = kernel_for(dtype, L);
                 const int nact = active_clusters(fn, C, NT, smem);
                 if (nact <= 0) continue;
-                // cost: padded work x idle-SM factor, a penalty when only one CTA fits per SM (no
-                // overlap of one row's latency-bound phases with another row's streaming), and a
-                // term for short sub-chunks (more warp records for the walk)
-                const double pad = 4.0 * NT * L * C / vocab;  // the busiest thread owns four sub-chunks
-                const double used = (double)nact * C;
-                const double under = used >= g_sm_count ? 1.0 : (double)g_sm_count / used;
-                const double per_sm = used / g_sm_count;
-                const double overlap = nbuf == 2 || per_sm >= 2.0 ? 1.0 : 1.3;
-                const double cost = pad * under * overlap * (1.0 + 4.0 / L);
+                // cost: modelled time of a 1024-row batch: rows per co-resident cluster times a
+                // per-row latency made of a fixed part (barriers, exchanges, serial phases; grows
+                // with the cluster size) and the streaming loops (elements per thread, slowed by
+                // the threads sharing each SM).  Fitted to B200 measurements of vocab 256000.
+                const double per_sm = (double)nact * C / g_sm_count;
+                const double sm_threads = (per_sm < 1.0 ? 1.0 : per_sm) * NT;
+                const double load = sm_threads / 512.0 < 1.0 ? 1.0 : sm_threads / 512.0;  // fewer warps: latency-bound
+                // two or more CTAs of different clusters per SM overlap one row's serial phases
+                // with another's loops
+                const double fixed_us = (10.0 + 0.2 * C) * (per_sm >= 1.5 ? 0.75 : 1.0) + (nbuf == 2 ? 0.0 : 2.5);
+                const double row_us = fixed_us + 0.1 * (4.0 * L) * load;
+                const double cost = ((1024 + nact - 1) / nact) * row_us * (1.0 + 1.0 / L);
                 if (getenv("DLLM_LIST_CFGS"))
                     fprintf(stderr, "dllm candidate: C %d NT %d SUB %d S %d nbuf %d smem %zu clusters %d cost %.3f\n", C, NT, L, S,
                             nbuf, smem, nact, cost);
@@ -149,6 +152,14 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
         fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d SUB %d S %d htab %d smem %zu clusters %d nbuf %d\n",
                 vocab, dtype, bc.cluster, bc.threads, bc.SUB, bc.S, bc.htab, bc.smem, bc.max_clusters, bc.nbuf);
     *cfg = bc;
+    return DLLM_OK;
+}
+
+static cudaEvent_t g_ev_before = nullptr, g_ev_after = nullptr;  // optional cluster-kernel timing
+
+dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after) {
+    g_ev_before = before;
+    g_ev_after = after;
     return DLLM_OK;
 }
 
@@ -179,8 +190,10 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     lc.numAttrs = 1;
     KernelArgs args = a;
     args.dbg = g_host_dbg;
+    if (g_ev_before) cudaEventRecord(g_ev_before, stream);
     e = cudaLaunchKernelEx(&lc, fn, args);
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
+    if (g_ev_after) cudaEventRecord(g_ev_after, stream);
     // the walk kernel: one warp per row, after the cluster kernel on the same stream
     const int wb = (a.rows + WALK_WARPS - 1) / WALK_WARPS;
     const size_t wsmem = (size_t)WALK_WARPS * walk_smem_per_warp(a.nrec);

@@ -147,6 +147,12 @@ DLLM_API dllm_status dllm_cuda_sample_batch_static(const dllm_batch_desc *desc, 
  * statistics into it; NULL switches it off.  No effect on results. */
 DLLM_API dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters);
 
+/* Diagnostics: when given two CUDA events (cudaEvent_t, created by the caller), every later
+ * sampling call records `before` on its stream right before the cluster kernel and `after` right
+ * after it, so the caller can time that kernel alone; NULLs switch it off.  No counterpart in
+ * the reference. */
+DLLM_API dllm_status dllm_cuda_set_timing_events(void *before, void *after);
+
 /* Version and build information ("diskllm_cuda <ver> sm_100a"). */
 DLLM_API const char *dllm_cuda_version(void);
 
