@@ -33,7 +33,7 @@ ROW_ERR_TIMEOUT = 16
 EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
     "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
-    "dllm_cuda_set_timing_events",
+    "dllm_cuda_set_timing_events", "dllm_cuda_shard_candidates", "dllm_cuda_merge_sample",
     "dllm_sampler_get_rng_state", "dllm_sampler_set_rng_state",
     "sampler_create", "sampler_free", "sampler_apply_repetition_penalty",
     "sampler_apply_presence_penalty", "sampler_sample", "greedy_sample",
@@ -114,6 +114,13 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_sample_batch.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
     lib.dllm_cuda_set_debug_counters.restype = C.c_int
     lib.dllm_cuda_set_debug_counters.argtypes = [C.c_void_p]
+    lib.dllm_cuda_shard_candidates.restype = C.c_int
+    lib.dllm_cuda_shard_candidates.argtypes = [C.POINTER(BatchDesc), C.c_int64, C.c_int64, C.c_int,
+                                               C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.dllm_cuda_merge_sample.restype = C.c_int
+    lib.dllm_cuda_merge_sample.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                           C.POINTER(SamplerParams), C.c_void_p, C.c_void_p, C.c_void_p,
+                                           C.c_void_p]
     lib.dllm_cuda_set_timing_events.restype = C.c_int
     lib.dllm_cuda_set_timing_events.argtypes = [C.c_void_p, C.c_void_p]
     lib.dllm_cuda_sample_batch_static.restype = C.c_int
@@ -328,3 +335,44 @@ def params_array(rows_params, device):
     arr = (SamplerParams * len(rows_params))(*[make_params(**p) for p in rows_params])
     raw = np.frombuffer(bytes(arr), dtype=np.uint8).copy()
     return torch.from_numpy(raw).to(device)
+
+
+def shard_candidates(logits, vocab_offset, vocab_total, k, params=None, *, stream=None, check=True, **kw):
+    """Step 1 of vocabulary-sharded sampling on this GPU's columns: returns (values float32
+    [rows][k], global ids int32 [rows][k]) of each row's k best entries after mask and penalties.
+    `logits` holds columns [vocab_offset, vocab_offset + logits.shape[1]); `mask` (if given) the
+    words of those columns; history ids are global."""
+    import torch
+
+    rows = logits.shape[0]
+    dummy_u = torch.empty(max(rows, 1), dtype=torch.float32, device=logits.device)
+    d, _ = fill_desc(logits, dummy_u, params, **kw)
+    vals = torch.empty(rows, k, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(rows, k, dtype=torch.int32, device=logits.device)
+    s = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+    rc = load_library().dllm_cuda_shard_candidates(C.byref(d), int(vocab_offset), int(vocab_total), int(k),
+                                                   vals.data_ptr(), ids.data_ptr(), s)
+    if check and rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_shard_candidates: {STATUS_NAMES.get(rc, rc)} ({load_library().dllm_cuda_last_error().decode()})")
+    return vals, ids
+
+
+def merge_sample(vals, ids, uniforms, params=None, *, row_params=None, token=None, stream=None, check=True):
+    """Step 3: tokens from all-gathered candidates vals / ids [nshards][rows][k]."""
+    import torch
+
+    nsh, rows, k = vals.shape
+    assert vals.dtype == torch.float32 and ids.dtype == torch.int32 and vals.is_contiguous() and ids.is_contiguous()
+    if params is None:
+        params = make_params()
+    elif isinstance(params, dict):
+        params = make_params(**params)
+    if token is None:
+        token = torch.empty(rows, dtype=torch.int32, device=vals.device)
+    s = stream if stream is not None else torch.cuda.current_stream(vals.device).cuda_stream
+    rp = row_params.data_ptr() if row_params is not None else None
+    rc = load_library().dllm_cuda_merge_sample(rows, nsh, k, vals.data_ptr(), ids.data_ptr(), C.byref(params), rp,
+                                               uniforms.data_ptr(), token.data_ptr(), s)
+    if check and rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_merge_sample: {STATUS_NAMES.get(rc, rc)} ({load_library().dllm_cuda_last_error().decode()})")
+    return token

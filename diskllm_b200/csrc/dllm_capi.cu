@@ -138,6 +138,38 @@ static dllm_status validate(const dllm_batch_desc *d) {
     return DLLM_OK;
 }
 
+// ----------------------------------------------------------------------------------------
+// vocabulary-sharded sampling (no counterpart in the reference, whose sampler sees whole rows)
+
+extern "C" dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *d, int64_t vocab_offset, int64_t vocab_total,
+                                                  int k, float *cand_val, int32_t *cand_id, void *stream) {
+    if (!d || d->rows < 0 || d->vocab <= 0 || (d->rows > 0 && !d->logits)) return DLLM_ERR_INVALID_ARG;
+    if (d->row_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
+    if (d->dtype != DLLM_DTYPE_F32 && d->dtype != DLLM_DTYPE_BF16) return DLLM_ERR_INVALID_ARG;
+    if (d->mask && d->mask_stride < (d->vocab + 31) / 32) return DLLM_ERR_INVALID_ARG;
+    if ((d->hist_ids == nullptr) != (d->hist_off == nullptr)) return DLLM_ERR_INVALID_ARG;
+    if (vocab_offset < 0 || vocab_total <= 0 || vocab_offset + d->vocab > vocab_total) return DLLM_ERR_INVALID_ARG;
+    if (!cand_val || !cand_id || k < 1) return DLLM_ERR_INVALID_ARG;
+    if (d->flags & ~(unsigned)DLLM_MODE_PEN_TRUE_DIV) return DLLM_ERR_UNSUPPORTED;
+    const dllm_status st = launch_shard_candidates(d, vocab_offset, vocab_total, k, cand_val, cand_id,
+                                                   (cudaStream_t)stream);
+    if (st == DLLM_ERR_CUDA) set_error("shard candidate kernel launch", cudaGetLastError());
+    return st;
+}
+
+extern "C" dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const float *cand_val,
+                                              const int32_t *cand_id, const dllm_sampler_params *params,
+                                              const dllm_sampler_params *row_params, const float *uniforms,
+                                              int32_t *token, void *stream) {
+    if (rows < 0 || nshards < 1 || k < 1 || !params) return DLLM_ERR_INVALID_ARG;
+    if (rows > 0 && (!cand_val || !cand_id || !uniforms || !token)) return DLLM_ERR_INVALID_ARG;
+    if (!row_params && (params->top_k < 1 || params->top_k > k)) return DLLM_ERR_UNSUPPORTED;
+    const dllm_status st = launch_merge_sample(rows, nshards, k, cand_val, cand_id, params, row_params, uniforms,
+                                               token, (cudaStream_t)stream);
+    if (st == DLLM_ERR_CUDA) set_error("merge kernel launch", cudaGetLastError());
+    return st;
+}
+
 static int topk_bound(const dllm_batch_desc *d) {
     int topk_max = d->row_params ? d->topk_max : d->params.top_k;
     if (topk_max >= d->vocab || topk_max < 0) topk_max = 0;

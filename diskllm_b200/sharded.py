@@ -1,0 +1,56 @@
+"""Vocabulary-sharded sampling across GPUs (the tensor-parallel LM-head layout): each rank holds
+columns [rank * Vs, (rank + 1) * Vs) of every row.  One exchange step:
+
+    local candidates (k best per row on this shard, after mask and penalties)
+      -> all-gather over the process group (NCCL over NVLink on B200 nodes)
+      -> merge on every rank (global max, t = (v - M) / T, top-k by (t desc, id asc), softmax,
+         min-p, top-p, fp32 draw with the row's uniform)
+
+The reference sampler (src/sampler.c:136-234) sees whole rows; these tokens equal its tokens for
+rows with 0 < top_k <= k.  Every rank computes the same tokens.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import capi
+
+
+def gather_candidates(vals: torch.Tensor, ids: torch.Tensor, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """All-gathers this rank's [rows][k] candidates into [world][rows][k] (rank order)."""
+    world = dist.get_world_size(group)
+    rows, k = vals.shape
+    # concatenated along rows (the layout every backend accepts), viewed as [world][rows][k]
+    out_v = torch.empty((world * rows, k), dtype=vals.dtype, device=vals.device)
+    out_i = torch.empty((world * rows, k), dtype=ids.dtype, device=ids.device)
+    dist.all_gather_into_tensor(out_v, vals.contiguous(), group=group)
+    dist.all_gather_into_tensor(out_i, ids.contiguous(), group=group)
+    return out_v.view(world, rows, k), out_i.view(world, rows, k)
+
+
+def shard_range(vocab_total: int, rank: int, world: int) -> tuple[int, int]:
+    """Columns [start, end) of `rank` when vocab_total is split into `world` equal shards whose
+    boundaries fall on mask words (multiples of 32)."""
+    per = -(-vocab_total // world)
+    per = -(-per // 32) * 32
+    start = min(vocab_total, rank * per)
+    return start, min(vocab_total, start + per)
+
+
+def sample_vocab_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab_total: int,
+                         uniforms: torch.Tensor, params: dict, *, k: int | None = None, mask_shard=None,
+                         hist_ids=None, hist_off=None, hist_max=None, group=None) -> torch.Tensor:
+    """Samples one token per row; call on every rank of `group` with that rank's shard.  `mask_shard`
+    holds the mask words of this shard's columns ([rows][ceil(Vs/32)] int32, bit i&31 of word i>>5
+    allows local column i); history ids are global.  Returns int32 [rows] (identical on all ranks)."""
+    k = int(k if k is not None else params.get("top_k", 0))
+    if not (0 < int(params.get("top_k", 0)) <= k):
+        raise ValueError("vocabulary-sharded sampling needs 0 < top_k <= k")
+    vals, ids = capi.shard_candidates(logits_shard, vocab_offset, vocab_total, k, params, mask=mask_shard,
+                                      hist_ids=hist_ids, hist_off=hist_off, hist_max=hist_max)
+    if group is not None or (dist.is_available() and dist.is_initialized()):
+        all_v, all_i = gather_candidates(vals, ids, group)
+    else:
+        all_v, all_i = vals.unsqueeze(0), ids.unsqueeze(0)
+    return capi.merge_sample(all_v, all_i, uniforms, params)

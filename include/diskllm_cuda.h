@@ -147,6 +147,27 @@ DLLM_API dllm_status dllm_cuda_sample_batch_static(const dllm_batch_desc *desc, 
  * statistics into it; NULL switches it off.  No effect on results. */
 DLLM_API dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters);
 
+/* Vocabulary-sharded sampling (a row's logits split over N GPUs, as a tensor-parallel LM head
+ * leaves them).  No counterpart in the reference, whose sampler sees whole rows; together the
+ * two calls and one all-gather give the tokens sampler_sample would (src/sampler.c:136-234)
+ * for rows with 0 < top_k <= k.
+ *
+ * Step 1, on each GPU: `desc` describes this GPU's columns [vocab_offset, vocab_offset +
+ * desc->vocab) of vocab_total-wide rows (logits, mask words of those columns, history as global
+ * ids, params; uniforms and token are not used).  Writes the k best entries of each row after
+ * mask and penalties, by (value desc, id asc): cand_val / cand_id [rows][k] (device), values are
+ * the penalised logits (fp32), ids global.  k <= 256.
+ * Step 2, the caller: all-gather the two arrays over the N GPUs into [N][rows][k].
+ * Step 3, on any GPU: one token per row from the gathered candidates (per-row or broadcast
+ * params; top_k <= k; uniforms and token device arrays [rows]). */
+DLLM_API dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *desc, int64_t vocab_offset,
+                                                int64_t vocab_total, int k, float *cand_val,
+                                                int32_t *cand_id, void *stream);
+DLLM_API dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const float *cand_val,
+                                            const int32_t *cand_id, const dllm_sampler_params *params,
+                                            const dllm_sampler_params *row_params,
+                                            const float *uniforms, int32_t *token, void *stream);
+
 /* Diagnostics: when given two CUDA events (cudaEvent_t, created by the caller), every later
  * sampling call records `before` on its stream right before the cluster kernel and `after` right
  * after it, so the caller can time that kernel alone; NULLs switch it off.  No counterpart in

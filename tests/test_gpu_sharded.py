@@ -1,0 +1,135 @@
+"""Vocabulary-sharded sampling on the GPU against the whole-row oracle.
+
+On one GPU the N shards run one after another (dllm_cuda_shard_candidates per column range),
+their candidates are stacked as the all-gather would stack them, and dllm_cuda_merge_sample
+draws.  Checked: every shard's candidates (values and ids) bit for bit against the oracle's
+penalised row, and the tokens against the oracle's tokens (src/sampler.c:136-234 on whole rows).
+With two GPUs the same runs through NCCL in two processes.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from diskllm_b200 import capi, sharded
+from util import csr, ids_match, pack_mask, u24
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _shard_np(pen, s, e, k):
+    vals = np.zeros((pen.shape[0], k), dtype=np.float32)
+    ids = np.zeros((pen.shape[0], k), dtype=np.int32)
+    for r in range(pen.shape[0]):
+        seg = pen[r, s:e]
+        order = np.lexsort((np.arange(s, e), -seg.astype(np.float64)))[:k]
+        vals[r] = seg[order]
+        ids[r] = order + s
+    return vals, ids
+
+
+def _run(x, allow, hist, params, nsh, k, dtype=torch.bfloat16, seed=0):
+    rows, V = x.shape
+    rng = np.random.default_rng(seed)
+    uni = u24(rng, rows)
+    mask = pack_mask(allow) if allow is not None else None
+    ora = O.sample_restated(x, params, uni, mask=mask, hist=hist, want_pen=True, kept_cap=k, topk_cap=k)
+    dev = torch.device("cuda", 0)
+    xt = torch.from_numpy(x).to(dev).to(dtype)
+    mt = torch.from_numpy(mask.view(np.int32)).to(dev) if mask is not None else None
+    hid, hoff = (torch.from_numpy(a).to(dev) for a in csr(hist)) if hist is not None else (None, None)
+    ut = torch.from_numpy(uni).to(dev)
+    vs, is_ = [], []
+    for r in range(nsh):
+        s, e = sharded.shard_range(V, r, nsh)
+        kw = dict(hist_ids=hid, hist_off=hoff)
+        if mt is not None:
+            kw["mask"] = mt[:, s // 32:(e + 31) // 32].contiguous()
+        v, i = capi.shard_candidates(xt[:, s:e], s, V, k, params, **kw)
+        vs.append(v)
+        is_.append(i)
+        ev, ei = _shard_np(ora.pen_logits, s, e, k)
+        np.testing.assert_array_equal(i.cpu().numpy(), ei, err_msg=f"shard {r} candidate ids")
+        np.testing.assert_array_equal(v.cpu().numpy().view(np.uint32), ev.view(np.uint32),
+                                      err_msg=f"shard {r} candidate values")
+    tok = capi.merge_sample(torch.stack(vs).contiguous(), torch.stack(is_).contiguous(), ut, params)
+    torch.cuda.synchronize()
+    tok = tok.cpu().numpy()
+    bad = [r for r in range(rows) if not ids_match(int(tok[r]), ora, uni, r)]
+    assert not bad, f"rows {bad[:8]}: gpu {tok[bad[:8]]} oracle {ora.token[bad[:8]]}"
+    return tok, ora
+
+
+def _bf16_grid(a):
+    """values exactly representable in bf16 (so the oracle sees what the GPU reads)"""
+    return torch.from_numpy(a).to(torch.bfloat16).float().numpy()
+
+
+@pytest.mark.parametrize("nsh", [2, 4, 8])
+def test_config5_shape_bf16(nsh):
+    rng = np.random.default_rng(505 + nsh)
+    rows, V = 24, 262144
+    x = _bf16_grid((rng.standard_normal((rows, V)) * 2.0).astype(np.float32))
+    allow = rng.random((rows, V)) < 0.10
+    hist = [rng.integers(0, V, 128) for _ in range(rows)]
+    params = dict(temperature=0.9, top_k=64, top_p=0.9, repetition=1.1)
+    _run(x, allow, hist, params, nsh, 64, seed=nsh)
+
+
+def test_f32_penalties_minp_odd_vocab():
+    rng = np.random.default_rng(11)
+    rows, V = 16, 5000
+    x = (rng.standard_normal((rows, V)) * 3.0).astype(np.float32)
+    hist = [rng.integers(0, V, 40) for _ in range(rows)]
+    params = dict(temperature=0.7, top_k=50, top_p=0.95, min_p=0.01, repetition=1.2, presence=0.3)
+    _run(x, None, hist, params, 3, 64, dtype=torch.float32)
+
+
+def test_ties_take_lowest_ids():
+    rng = np.random.default_rng(12)
+    rows, V = 8, 8192
+    x = rng.integers(-3, 3, (rows, V)).astype(np.float32)  # thousands of equal values
+    params = dict(temperature=1.0, top_k=40, top_p=0.8)
+    _run(x, None, None, params, 4, 40, dtype=torch.float32)
+
+
+def test_fewer_allowed_than_k_and_fully_masked_rows():
+    rng = np.random.default_rng(13)
+    rows, V = 8, 4096
+    x = (rng.standard_normal((rows, V))).astype(np.float32)
+    allow = np.zeros((rows, V), dtype=bool)
+    for r in range(1, rows):
+        allow[r, rng.choice(V, size=r * 3, replace=False)] = True  # 3 .. 21 allowed, k = 32
+    params = dict(temperature=1.0, top_k=32, top_p=0.9)
+    tok, ora = _run(x, allow, None, params, 2, 32, dtype=torch.float32)
+    assert tok[0] == ora.token[0] == 31  # fully masked: the reference returns its list's last id
+
+
+def test_greedy():
+    rng = np.random.default_rng(14)
+    rows, V = 8, 20000
+    x = _bf16_grid((rng.standard_normal((rows, V)) * 2.0).astype(np.float32))
+    x[:, 777] = x.max()  # ties for the maximum: the first id wins
+    params = dict(temperature=0.0, top_k=8, repetition=1.1)
+    hist = [rng.integers(0, V, 16) for _ in range(rows)]
+    _run(x, None, hist, params, 4, 8)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpus_nccl():
+    script = os.path.join(ROOT, "tests", "sharded_nccl_worker.py")
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "tests"),
+                                                      os.path.join(ROOT, "oracle")]))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29613", script]
+    res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
+    assert "SHARDED_NCCL_OK" in res.stdout
