@@ -10,6 +10,11 @@ needed between steps.  Multi-GPU: one process per GPU, rows sharded (each rank s
 own 1024-row batch; no collective on the data path) -> weak scaling.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --workload cfg5 [--gpus N] ...   # vocabulary-sharded config 5 (strong scaling)
+
+Config 5 (--workload cfg5): 512 rows x vocab 262144 bf16 N(0, 2^2), 10 % of ids allowed by the
+mask, repetition 1.1 over 128 ids, temperature 0.9, top-k 64, top-p 0.9; every GPU holds 1/N of
+the columns of all rows.  A step: shard candidates, NCCL all-gather, merge and draw.
 
 Prints one JSON line on rank 0.
 """
@@ -26,6 +31,8 @@ import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
+# keep stdout to the one JSON line (NCCL prints its version banner otherwise)
+os.environ.setdefault("NCCL_DEBUG", "WARN")
 
 METRIC = "sampled rows/sec and achieved HBM GB/s vs ~8 TB/s at 1/2/4/8 B200"
 ROWS, VOCAB, HIST = 1024, 256000, 256
@@ -323,6 +330,107 @@ def run_ours(args, rank, world, dev):
     print(json.dumps(line), flush=True)
 
 
+CFG5_ROWS, CFG5_VOCAB, CFG5_HIST, CFG5_K = 512, 262144, 128, 64
+
+
+def run_cfg5(args, rank, world, dev):
+    import torch
+
+    from diskllm_b200 import capi, sharded
+    from diskllm_b200 import workloads as W
+
+    capi.load_library()
+    w = W.config5(device=dev, seed=505, rows=CFG5_ROWS)  # the same rows on every rank
+    s, e = sharded.shard_range(CFG5_VOCAB, rank, world)
+    x = w.logits[:, s:e].contiguous()
+    m = w.mask[:, s // 32:(e + 31) // 32].contiguous()
+    params = dict(w.params)
+    w.logits = None  # the rank keeps only its shard
+
+    def step():
+        return sharded.sample_vocab_sharded(x, s, CFG5_VOCAB, w.uniforms, params, k=CFG5_K, mask_shard=m,
+                                            hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=CFG5_HIST)
+
+    for _ in range(args.warmup):
+        step()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    stream = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(dev.index)
+    barrier()
+    clocks.start()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier()
+    clocks.stop()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+
+    # end to end: this GPU's shard of the logits from pinned host memory, tokens back to the host
+    h_x = x.cpu().pin_memory()
+    d_x = torch.empty_like(x)
+    h_tok = torch.empty(CFG5_ROWS, dtype=torch.int32).pin_memory()
+
+    def e2e_step():
+        d_x.copy_(h_x, non_blocking=True)
+        tok = sharded.sample_vocab_sharded(d_x, s, CFG5_VOCAB, w.uniforms, params, k=CFG5_K, mask_shard=m,
+                                           hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=CFG5_HIST)
+        h_tok.copy_(tok, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    barrier()
+    ms_e2e = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    if rank != 0:
+        return
+    cols = e - s
+    bytes_per_gpu = CFG5_ROWS * (2 * cols + (cols + 7) // 8 + CFG5_HIST * 4)
+    peak, peak_kind = measured_peak()
+    achieved = bytes_per_gpu / (ms_step / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": CFG5_ROWS / (ms_step / 1e3), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 in, f32 arithmetic",
+        "data": "synthetic (seeded N(0,2^2) bf16 rows, 10% mask, uniform histories, Philox uniforms)",
+        "config": {"workload": "cfg5_vocab_parallel_b512_v262144_bf16 (BASELINE config 5)",
+                   "global_batch": CFG5_ROWS, "vocab": CFG5_VOCAB, "columns_per_gpu": cols, "top_k_per_shard": CFG5_K,
+                   "params": params, "parallelism": f"vocab-sharded x{world} (NCCL all-gather of candidates)",
+                   "l2_policy": "per-GPU shard may fit in L2 at N >= 2; no flush (step time includes the exchange)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s",
+                     "traffic": None, "algorithmic_bytes_per_gpu_step": bytes_per_gpu,
+                     "kernel": "shard_topk_kernel + all-gather + merge_sample_kernel (whole step)"},
+        "e2e": {"value": CFG5_ROWS / (ms_e2e / e2e_steps / 1e3), "unit": "rows/s",
+                "h2d_bytes_per_step": h_x.numel() * 2, "d2h_bytes_per_step": CFG5_ROWS * 4},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -331,6 +439,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--workload", choices=["cfg4", "cfg5"], default="cfg4",
+                    help="cfg4: the headline row-sharded batch; cfg5: vocabulary-sharded config 5")
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (default: config 4's 1024; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -350,7 +460,10 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
     try:
-        run_ours(args, rank, world, dev)
+        if args.workload == "cfg5":
+            run_cfg5(args, rank, world, dev)
+        else:
+            run_ours(args, rank, world, dev)
     finally:
         if world > 1:
             torch.distributed.destroy_process_group()

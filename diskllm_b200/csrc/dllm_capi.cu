@@ -151,7 +151,14 @@ extern "C" dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *d, int6
     if (vocab_offset < 0 || vocab_total <= 0 || vocab_offset + d->vocab > vocab_total) return DLLM_ERR_INVALID_ARG;
     if (!cand_val || !cand_id || k < 1) return DLLM_ERR_INVALID_ARG;
     if (d->flags & ~(unsigned)DLLM_MODE_PEN_TRUE_DIV) return DLLM_ERR_UNSUPPORTED;
-    const dllm_status st = launch_shard_candidates(d, vocab_offset, vocab_total, k, cand_val, cand_id,
+    // per-chunk candidates of rows wider than one chunk: the grow-only internal buffer
+    const size_t pb = shard_part_bytes(d->rows, d->vocab, k);
+    void *part = pb ? internal_workspace(stream, pb) : nullptr;
+    if (pb && !part) {
+        set_error("shard candidate scratch", cudaErrorMemoryAllocation);
+        return DLLM_ERR_OOM;
+    }
+    const dllm_status st = launch_shard_candidates(d, vocab_offset, vocab_total, k, cand_val, cand_id, part,
                                                    (cudaStream_t)stream);
     if (st == DLLM_ERR_CUDA) set_error("shard candidate kernel launch", cudaGetLastError());
     return st;

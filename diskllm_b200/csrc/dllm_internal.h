@@ -89,8 +89,9 @@ __host__ __device__ inline size_t walk_smem_per_warp(int nrec) {
 dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
 dllm_status set_debug_counters(unsigned long long *dev_counters);
 dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
+size_t shard_part_bytes(int rows, int vlocal, int k);
 dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int64_t vtotal, int k, float *cand_val,
-                                    int32_t *cand_id, cudaStream_t stream);
+                                    int32_t *cand_id, void *part, cudaStream_t stream);
 dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, const int32_t *ids,
                                 const dllm_sampler_params *params, const dllm_sampler_params *row_params,
                                 const float *uniforms, int32_t *token, cudaStream_t stream);

@@ -1,10 +1,11 @@
 // dllm_shard.cu -- vocabulary-sharded sampling (a row's logits split over N GPUs, the
 // tensor-parallel LM-head layout).  The path has one exchange step:
 //
-//   1. dllm_cuda_shard_candidates: on each GPU, one CTA per row applies the grammar mask and the
-//      history penalties to the GPU's id range and selects its k best entries by (value desc,
-//      id asc) with a 4-pass radix select on order-preserving keys.  Output (value, global id),
-//      sorted, [rows][k].
+//   1. dllm_cuda_shard_candidates: on each GPU, one CTA per (8192-column chunk, row) applies the
+//      grammar mask and the history penalties to its columns, stages them as order-preserving
+//      keys in shared memory and selects the chunk's k best by (value desc, id asc) with a 4-pass
+//      radix select; a second kernel selects each row's k best of its chunks' candidates.
+//      Output (value, global id), sorted, [rows][k].
 //   2. The caller all-gathers the candidates ([N][rows][k], NCCL over NVLink).
 //   3. dllm_cuda_merge_sample: one CTA per row takes the row maximum over the N*k candidates,
 //      forms t = (v - M) * (1/T) like the reference (src/sampler.c:144-162), keeps the k best by
@@ -23,9 +24,10 @@
 namespace dllm {
 namespace {
 
-constexpr int SH_THREADS = 512;
-constexpr int SH_HTAB = 1024;  // history hash entries per row (power of two)
-constexpr int SH_KMAX = 256;   // largest k per shard
+constexpr int SH_T = 256;        // threads per CTA
+constexpr int SH_CHUNK = 8192;   // columns per CTA (keys staged in shared memory)
+constexpr int SH_HTAB = 512;     // history hash entries per chunk (power of two)
+constexpr int SH_KMAX = 256;     // largest k per shard
 
 struct ShardArgs {
     const void *logits;
@@ -37,106 +39,42 @@ struct ShardArgs {
     const int64_t *hist_off;
     dllm_sampler_params bparams;
     const dllm_sampler_params *rparams;
-    int rows, vlocal, k;
+    int rows, vlocal, k, nchunks;
     int64_t voff, vtotal;
     unsigned flags;
-    float *cand_val;
+    float *cand_val;       // final [rows][k]
     int32_t *cand_id;
+    uint32_t *part_key;    // per-chunk candidates [rows][nchunks][k] when nchunks > 1
+    int32_t *part_id;
     int32_t *status;
 };
 
-template <int DT>
-__global__ void __launch_bounds__(SH_THREADS) shard_topk_kernel(const ShardArgs a) {
-    __shared__ int hkeys[SH_HTAB];
-    __shared__ int hcnt[SH_HTAB];
-    __shared__ unsigned hist[256];
-    __shared__ float cv[SH_KMAX];
-    __shared__ int ci[SH_KMAX];
-    __shared__ int wsum[SH_THREADS / 32];
-    __shared__ int s_bin, s_above, s_ncand, s_flags;
-    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x;
-    const int NW = NT >> 5;
-    const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
-    const int Vs = a.vlocal, K = a.k;
+struct SelScratch {
+    unsigned hist[256];
+    uint32_t ck[SH_KMAX];
+    int cid[SH_KMAX];
+    int wsum[SH_T / 32];
+    int bin, above, ncand;
+};
 
-    // history ids of this shard: local index -> occurrence count (src/sampler.c:21-52)
-    for (int i = tid; i < SH_HTAB; i += NT) {
-        hkeys[i] = -1;
-        hcnt[i] = 0;
-    }
-    if (tid == 0) {
-        s_ncand = 0;
-        s_flags = 0;
-    }
-    __syncthreads();
-    const bool use_hist = a.hist_ids && a.hist_off && (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
-    if (use_hist) {
-        const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-        for (int64_t j = h0 + tid; j < h1; j += NT) {
-            const int id = a.hist_ids[j];
-            if (id < 0 || id >= a.vtotal) continue;
-            const int64_t li = (int64_t)id - a.voff;
-            if (li < 0 || li >= Vs) continue;
-            uint32_t h = hash_id((uint32_t)li) & (SH_HTAB - 1);
-            bool placed = false;
-            for (int probe = 0; probe < SH_HTAB; probe++) {
-                const int old = atomicCAS(&hkeys[h], -1, (int)li);
-                if (old == -1 || old == (int)li) {
-                    atomicAdd(&hcnt[h], 1);
-                    placed = true;
-                    break;
-                }
-                h = (h + 1u) & (SH_HTAB - 1);
-            }
-            if (!placed) atomicOr(&s_flags, ROW_ERR_HIST_TABLE);
-        }
-    }
-    __syncthreads();
-    const float inv_rep = __fdiv_rn(1.0f, p.repetition);
-    const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
-    const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
-
-    // masked, penalised logit of local element li (grammar.c:275-308, then sampler.c:35-52, 21-33)
-    auto value = [&](int li) -> float {
-        float v;
-        if (DT == DLLM_DTYPE_F32)
-            v = ((const float *)a.logits)[(int64_t)row * a.row_stride + li];
-        else
-            v = bitsf((uint32_t)((const unsigned short *)a.logits)[(int64_t)row * a.row_stride + li] << 16);
-        if (mrow && !((mrow[li >> 5] >> (li & 31)) & 1u)) v = -INFINITY;
-        if (use_hist) {
-            uint32_t h = hash_id((uint32_t)li) & (SH_HTAB - 1);
-            for (int probe = 0; probe < SH_HTAB; probe++) {
-                const int kk = hkeys[h];
-                if (kk == -1) break;
-                if (kk == li) {
-                    const int c = hcnt[h];
-                    if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
-                    if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
-                    if (p.repetition > 1.0f)
-                        for (int r = 0; r < c; r++) {
-                            if (v < 0.0f) v = __fmul_rn(v, p.repetition);
-                            else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
-                        }
-                    break;
-                }
-                h = (h + 1u) & (SH_HTAB - 1);
-            }
-        }
-        return v;
-    };
-
-    // radix select of the K-th largest key, 8 bits per pass from the top
+// The K best of n keys in shared memory by (key desc, id asc), written sorted to okey/oid
+// (K entries; positions past n, when n < K, get key 0 and id INT_MAX, which rank last).
+// Radix select of the K-th key, 8 bits per pass from the top.  Ids: ids[i], or id0 + i when
+// ids is null (then ids grow with position and ties are resolved by a positional scan).
+__device__ void block_select(const uint32_t *keys, const int *ids, int id0, int n, int K, SelScratch &s,
+                             uint32_t *okey, int *oid) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
+    const int Kn = min(K, n);
     uint32_t prefix = 0u, pmask = 0u;
-    int remaining = K;
+    int remaining = Kn;
     unsigned cnt_eq = 0u;
-    for (int pass = 3; pass >= 0; pass--) {
-        for (int i = tid; i < 256; i += NT) hist[i] = 0u;
+    for (int pass = 3; pass >= 0 && Kn > 0; pass--) {
+        for (int i = tid; i < 256; i += NT) s.hist[i] = 0u;
         __syncthreads();
         const int sh = 8 * pass;
-        for (int li = tid; li < Vs; li += NT) {
-            const uint32_t key = okey(value(li));
-            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> sh) & 255u], 1u);
+        for (int i = tid; i < n; i += NT) {
+            const uint32_t key = keys[i];
+            if ((key & pmask) == prefix) atomicAdd(&s.hist[(key >> sh) & 255u], 1u);
         }
         __syncthreads();
         if (wid == 0) {
@@ -144,7 +82,7 @@ __global__ void __launch_bounds__(SH_THREADS) shard_topk_kernel(const ShardArgs 
             unsigned c[8], tot = 0u;
 #pragma unroll
             for (int b = 0; b < 8; b++) {
-                c[b] = hist[255 - 8 * lane - b];
+                c[b] = s.hist[255 - 8 * lane - b];
                 tot += c[b];
             }
             unsigned incl = tot;
@@ -159,8 +97,8 @@ __global__ void __launch_bounds__(SH_THREADS) shard_topk_kernel(const ShardArgs 
 #pragma unroll
                 for (int b = 0; b < 8; b++) {
                     if (acc + c[b] >= (unsigned)remaining) {
-                        s_bin = 255 - 8 * lane - b;
-                        s_above = (int)acc;
+                        s.bin = 255 - 8 * lane - b;
+                        s.above = (int)acc;
                         break;
                     }
                     acc += c[b];
@@ -168,73 +106,221 @@ __global__ void __launch_bounds__(SH_THREADS) shard_topk_kernel(const ShardArgs 
             }
         }
         __syncthreads();
-        prefix |= (uint32_t)s_bin << sh;
+        prefix |= (uint32_t)s.bin << sh;
         pmask |= 255u << sh;
-        remaining -= s_above;
-        cnt_eq = hist[s_bin];
+        remaining -= s.above;
+        cnt_eq = s.hist[s.bin];
         __syncthreads();
     }
-    const uint32_t kstar = prefix;  // key of the K-th best entry; `remaining` entries equal to it are kept
-
-    // entries above the threshold, then the lowest-index entries equal to it
-    for (int li = tid; li < Vs; li += NT) {
-        const float v = value(li);
-        const uint32_t key = okey(v);
-        const bool take = key > kstar || (key == kstar && cnt_eq == (unsigned)remaining);
-        if (take) {
-            const int pos = atomicAdd(&s_ncand, 1);
-            if (pos < K) {
-                cv[pos] = v;
-                ci[pos] = li;
+    const uint32_t kstar = prefix;
+    if (tid == 0) s.ncand = 0;
+    __syncthreads();
+    for (int i = tid; i < n && Kn > 0; i += NT) {
+        const uint32_t key = keys[i];
+        if (key > kstar || (key == kstar && cnt_eq == (unsigned)remaining)) {
+            const int pos = atomicAdd(&s.ncand, 1);
+            if (pos < Kn) {
+                s.ck[pos] = key;
+                s.cid[pos] = ids ? ids[i] : id0 + i;
             }
         }
     }
     __syncthreads();
-    if (cnt_eq != (unsigned)remaining) {
-        int taken = 0;
-        for (int base = 0; base < Vs && taken < remaining; base += NT) {
-            const int li = base + tid;
-            float v = 0.0f;
-            bool eq = false;
-            if (li < Vs) {
-                v = value(li);
-                eq = okey(v) == kstar;
+    if (Kn > 0 && cnt_eq != (unsigned)remaining) {
+        // keep the `remaining` lowest ids among the entries equal to the threshold
+        if (!ids) {
+            int taken = 0;
+            for (int base = 0; base < n && taken < remaining; base += NT) {
+                const int i = base + tid;
+                const bool eq = i < n && keys[i] == kstar;
+                const unsigned bm = __ballot_sync(0xffffffffu, eq);
+                if (lane == 0) s.wsum[wid] = __popc(bm);
+                __syncthreads();
+                int before = 0, total = 0;
+                for (int w = 0; w < NW; w++) {
+                    if (w < wid) before += s.wsum[w];
+                    total += s.wsum[w];
+                }
+                const int rank = taken + before + __popc(bm & ((1u << lane) - 1u));
+                if (eq && rank < remaining) {
+                    const int pos = atomicAdd(&s.ncand, 1);
+                    if (pos < Kn) {
+                        s.ck[pos] = kstar;
+                        s.cid[pos] = id0 + i;
+                    }
+                }
+                taken += total;
+                __syncthreads();
             }
-            const unsigned bm = __ballot_sync(0xffffffffu, eq);
-            if (lane == 0) wsum[wid] = __popc(bm);
-            __syncthreads();
-            int before = 0, total = 0;
-            for (int w = 0; w < NW; w++) {
-                if (w < wid) before += wsum[w];
-                total += wsum[w];
-            }
-            const int rank = taken + before + __popc(bm & ((1u << lane) - 1u));
-            if (eq && rank < remaining) {
-                const int pos = atomicAdd(&s_ncand, 1);
-                if (pos < K) {
-                    cv[pos] = v;
-                    ci[pos] = li;
+        } else {
+            for (int i = tid; i < n; i += NT) {
+                if (keys[i] != kstar) continue;
+                int r = 0;
+                for (int j = 0; j < n; j++) r += keys[j] == kstar && ids[j] < ids[i];
+                if (r < remaining) {
+                    const int pos = atomicAdd(&s.ncand, 1);
+                    if (pos < Kn) {
+                        s.ck[pos] = kstar;
+                        s.cid[pos] = ids[i];
+                    }
                 }
             }
-            taken += total;
-            __syncthreads();
         }
     }
     __syncthreads();
-    // sorted by (value desc, id asc): each entry's rank among the K
     for (int i = tid; i < K; i += NT) {
-        const float vi = cv[i];
-        const uint32_t ki = okey(vi);
-        const int ii = ci[i];
-        int r = 0;
-        for (int j = 0; j < K; j++) {
-            const uint32_t kj = okey(cv[j]);
-            r += kj > ki || (kj == ki && ci[j] < ii);
+        if (i >= Kn) {
+            okey[i] = 0u;
+            oid[i] = INT_MAX;
+            continue;
         }
-        a.cand_val[(int64_t)row * K + r] = vi;
-        a.cand_id[(int64_t)row * K + r] = (int32_t)(ci[i] + a.voff);
+        const uint32_t ki = s.ck[i];
+        const int ii = s.cid[i];
+        int r = 0;
+        for (int j = 0; j < Kn; j++) r += s.ck[j] > ki || (s.ck[j] == ki && s.cid[j] < ii);
+        okey[r] = ki;
+        oid[r] = ii;
     }
-    if (tid == 0 && a.status) a.status[row] = s_flags;
+    __syncthreads();
+}
+
+// One CTA per (chunk of up to SH_CHUNK columns, row): mask, penalties, keys in shared memory, the
+// chunk's k best.  With one chunk per row they are the shard's final candidates.
+template <int DT>
+__global__ void __launch_bounds__(SH_T) shard_chunk_kernel(const ShardArgs a) {
+    __shared__ uint32_t keys[SH_CHUNK];
+    __shared__ int hkeys[SH_HTAB];
+    __shared__ int hcnt[SH_HTAB];
+    __shared__ SelScratch sel;
+    __shared__ uint32_t okey_s[SH_KMAX];
+    __shared__ int oid_s[SH_KMAX];
+    __shared__ int s_flags;
+    const int row = blockIdx.y, ch = blockIdx.x, tid = threadIdx.x, NT = blockDim.x;
+    const int c0 = ch * SH_CHUNK, n = min(SH_CHUNK, a.vlocal - c0);
+    const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
+
+    for (int i = tid; i < SH_HTAB; i += NT) {
+        hkeys[i] = -1;
+        hcnt[i] = 0;
+    }
+    if (tid == 0) s_flags = 0;
+    // raw logits of the chunk, masked (grammar.c:275-308), as order-preserving keys
+    const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
+    if (DT == DLLM_DTYPE_BF16) {
+        const unsigned short *src = (const unsigned short *)a.logits + (int64_t)row * a.row_stride + c0;
+        const bool vec = ((uintptr_t)src & 15u) == 0;
+        const int n8 = vec ? (n & ~7) : 0;
+        for (int i = 8 * tid; i < n8; i += 8 * NT) {
+            const uint4 raw = *reinterpret_cast<const uint4 *>(src + i);
+            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+            const uint32_t mw = mrow ? mrow[(c0 + i) >> 5] >> ((c0 + i) & 31) : 0xffu;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint32_t hb = (j & 1) ? (w[j >> 1] & 0xffff0000u) : (w[j >> 1] << 16);
+                keys[i + j] = okey(((mw >> j) & 1u) ? bitsf(hb) : -INFINITY);
+            }
+        }
+        for (int i = n8 + tid; i < n; i += NT) {
+            const int li = c0 + i;
+            const float v = bitsf((uint32_t)src[i] << 16);
+            keys[i] = okey(!mrow || ((mrow[li >> 5] >> (li & 31)) & 1u) ? v : -INFINITY);
+        }
+    } else {
+        const float *src = (const float *)a.logits + (int64_t)row * a.row_stride + c0;
+        const bool vec = ((uintptr_t)src & 15u) == 0;
+        const int n4 = vec ? (n & ~3) : 0;
+        for (int i = 4 * tid; i < n4; i += 4 * NT) {
+            const float4 x = *reinterpret_cast<const float4 *>(src + i);
+            const uint32_t mw = mrow ? mrow[(c0 + i) >> 5] >> ((c0 + i) & 31) : 0xfu;
+            keys[i] = okey((mw & 1u) ? x.x : -INFINITY);
+            keys[i + 1] = okey((mw & 2u) ? x.y : -INFINITY);
+            keys[i + 2] = okey((mw & 4u) ? x.z : -INFINITY);
+            keys[i + 3] = okey((mw & 8u) ? x.w : -INFINITY);
+        }
+        for (int i = n4 + tid; i < n; i += NT) {
+            const int li = c0 + i;
+            keys[i] = okey(!mrow || ((mrow[li >> 5] >> (li & 31)) & 1u) ? src[i] : -INFINITY);
+        }
+    }
+    __syncthreads();
+    // history penalties of this chunk's ids (sampler.c:35-52 presence once, 21-33 repetition per
+    // occurrence): occurrence counts in a hash table, then each counted entry's key rewritten
+    const bool use_hist = a.hist_ids && a.hist_off && (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
+    if (use_hist) {
+        const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+        for (int64_t j = h0 + tid; j < h1; j += NT) {
+            const int id = a.hist_ids[j];
+            if (id < 0 || id >= a.vtotal) continue;
+            const int64_t li = (int64_t)id - a.voff - c0;
+            if (li < 0 || li >= n) continue;
+            uint32_t h = hash_id((uint32_t)li) & (SH_HTAB - 1);
+            bool placed = false;
+            for (int probe = 0; probe < SH_HTAB; probe++) {
+                const int old = atomicCAS(&hkeys[h], -1, (int)li);
+                if (old == -1 || old == (int)li) {
+                    atomicAdd(&hcnt[h], 1);
+                    placed = true;
+                    break;
+                }
+                h = (h + 1u) & (SH_HTAB - 1);
+            }
+            if (!placed) atomicOr(&s_flags, ROW_ERR_HIST_TABLE);
+        }
+        __syncthreads();
+        const float inv_rep = __fdiv_rn(1.0f, p.repetition);
+        const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
+        for (int sl = tid; sl < SH_HTAB; sl += NT) {
+            const int li = hkeys[sl];
+            if (li < 0) continue;
+            const int c = hcnt[sl];
+            float v = okey_inv(keys[li]);
+            if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
+            if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
+            if (p.repetition > 1.0f)
+                for (int r = 0; r < c; r++) {
+                    if (v < 0.0f) v = __fmul_rn(v, p.repetition);
+                    else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
+                }
+            keys[li] = okey(v);
+        }
+    }
+    __syncthreads();
+    block_select(keys, nullptr, c0, n, a.k, sel, okey_s, oid_s);
+    if (a.nchunks == 1) {
+        for (int i = tid; i < a.k; i += NT) {
+            a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
+            a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
+        }
+    } else {
+        const int64_t o = ((int64_t)row * a.nchunks + ch) * a.k;
+        for (int i = tid; i < a.k; i += NT) {
+            a.part_key[o + i] = okey_s[i];
+            a.part_id[o + i] = oid_s[i];
+        }
+    }
+    if (a.status && tid == 0 && s_flags) atomicOr(&a.status[row], s_flags);
+}
+
+// One CTA per row: the k best of the row's chunk candidates, as the shard's final candidates.
+__global__ void __launch_bounds__(SH_T) shard_rowmerge_kernel(const ShardArgs a) {
+    extern __shared__ __align__(16) unsigned char rdyn[];
+    __shared__ SelScratch sel;
+    __shared__ uint32_t okey_s[SH_KMAX];
+    __shared__ int oid_s[SH_KMAX];
+    const int row = blockIdx.x, tid = threadIdx.x, NT = blockDim.x;
+    const int n = a.nchunks * a.k;
+    uint32_t *keys = reinterpret_cast<uint32_t *>(rdyn);
+    int *ids = reinterpret_cast<int *>(keys + n);
+    for (int i = tid; i < n; i += NT) {
+        keys[i] = a.part_key[(int64_t)row * n + i];
+        ids[i] = a.part_id[(int64_t)row * n + i];
+    }
+    __syncthreads();
+    block_select(keys, ids, 0, n, a.k, sel, okey_s, oid_s);
+    for (int i = tid; i < a.k; i += NT) {
+        a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
+        a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
+    }
 }
 
 struct MergeArgs {
@@ -248,7 +334,7 @@ struct MergeArgs {
 };
 
 constexpr int MG_THREADS = 256;
-constexpr int MG_MAX = 8 * SH_KMAX;  // candidates per row (shards x k)
+constexpr int MG_MAX = 16 * SH_KMAX;  // candidates per row (shards x k)
 
 __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArgs a) {
     extern __shared__ __align__(16) unsigned char mdyn[];
@@ -321,8 +407,13 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
 
 }  // namespace
 
+size_t shard_part_bytes(int rows, int vlocal, int k) {
+    const int nch = (vlocal + SH_CHUNK - 1) / SH_CHUNK;
+    return nch > 1 ? (size_t)rows * nch * k * 8 : 0;
+}
+
 dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int64_t vtotal, int k, float *cand_val,
-                                    int32_t *cand_id, cudaStream_t stream) {
+                                    int32_t *cand_id, void *part, cudaStream_t stream) {
     if (k < 1 || k > SH_KMAX || k > d->vocab) return DLLM_ERR_UNSUPPORTED;
     ShardArgs a = {};
     a.logits = d->logits;
@@ -337,6 +428,7 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     a.rows = d->rows;
     a.vlocal = d->vocab;
     a.k = k;
+    a.nchunks = (d->vocab + SH_CHUNK - 1) / SH_CHUNK;
     a.voff = voff;
     a.vtotal = vtotal;
     a.flags = d->flags;
@@ -344,10 +436,23 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     a.cand_id = cand_id;
     a.status = d->status;
     if (a.rows == 0) return DLLM_OK;
+    if (a.nchunks > 1) {
+        if (!part) return DLLM_ERR_OOM;
+        a.part_key = reinterpret_cast<uint32_t *>(part);
+        a.part_id = reinterpret_cast<int32_t *>(a.part_key + (size_t)a.rows * a.nchunks * k);
+        const size_t rs = (size_t)a.nchunks * k * 8;
+        if (rs > 200 * 1024) return DLLM_ERR_UNSUPPORTED;
+        if (cudaFuncSetAttribute((const void *)shard_rowmerge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)rs) != cudaSuccess)
+            return DLLM_ERR_CUDA;
+    }
+    if (a.status) cudaMemsetAsync(a.status, 0, (size_t)a.rows * sizeof(int32_t), stream);
+    const dim3 grid(a.nchunks, a.rows);
     if (d->dtype == DLLM_DTYPE_BF16)
-        shard_topk_kernel<DLLM_DTYPE_BF16><<<a.rows, SH_THREADS, 0, stream>>>(a);
+        shard_chunk_kernel<DLLM_DTYPE_BF16><<<grid, SH_T, 0, stream>>>(a);
     else
-        shard_topk_kernel<DLLM_DTYPE_F32><<<a.rows, SH_THREADS, 0, stream>>>(a);
+        shard_chunk_kernel<DLLM_DTYPE_F32><<<grid, SH_T, 0, stream>>>(a);
+    if (a.nchunks > 1) shard_rowmerge_kernel<<<a.rows, SH_T, (size_t)a.nchunks * k * 8, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
 }
 
