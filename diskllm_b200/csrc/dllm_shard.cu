@@ -57,24 +57,90 @@ struct SelScratch {
     int bin, above, ncand;
 };
 
-// The K best of n keys in shared memory by (key desc, id asc), written sorted to okey/oid
-// (K entries; positions past n, when n < K, get key 0 and id INT_MAX, which rank last).
-// Radix select of the K-th key, 8 bits per pass from the top.  Ids: ids[i], or id0 + i when
-// ids is null (then ids grow with position and ties are resolved by a positional scan).
-__device__ void block_select(const uint32_t *keys, const int *ids, int id0, int n, int K, SelScratch &s,
-                             uint32_t *okey, int *oid) {
+// Appends to s.ck / s.cid (from s.ncand) the `need` entries equal to `target` with the lowest ids.
+// Without ids (ids grow with position) each warp scans a contiguous segment with ballots, twice:
+// once to count, once to rank against the earlier segments' counts.  With ids, ranks by counting.
+__device__ void select_ties(const uint32_t *keys, const int *ids, int id0, int n, uint32_t target, int need, int cap,
+                            SelScratch &s) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
+    if (need <= 0) return;
+    if (ids) {
+        for (int i = tid; i < n; i += NT) {
+            if (keys[i] != target) continue;
+            int r = 0;
+            for (int j = 0; j < n; j++) r += keys[j] == target && ids[j] < ids[i];
+            if (r < need) {
+                const int pos = atomicAdd(&s.ncand, 1);
+                if (pos < cap) {
+                    s.ck[pos] = target;
+                    s.cid[pos] = ids[i];
+                }
+            }
+        }
+        __syncthreads();
+        return;
+    }
+    const int seg = ((n + NW - 1) / NW + 31) & ~31;
+    const int b0 = min(n, wid * seg), b1 = min(n, b0 + seg);
+    int cnt = 0;
+    for (int base = b0; base < b1; base += 32) {
+        const int i = base + lane;
+        cnt += __popc(__ballot_sync(0xffffffffu, i < b1 && keys[i] == target));
+    }
+    if (lane == 0) s.wsum[wid] = cnt;
+    __syncthreads();
+    int running = 0;
+    for (int w = 0; w < wid; w++) running += s.wsum[w];
+    for (int base = b0; base < b1 && running < need; base += 32) {
+        const int i = base + lane;
+        const bool eq = i < b1 && keys[i] == target;
+        const unsigned bm = __ballot_sync(0xffffffffu, eq);
+        const int rank = running + __popc(bm & ((1u << lane) - 1u));
+        if (eq && rank < need) {
+            const int pos = atomicAdd(&s.ncand, 1);
+            if (pos < cap) {
+                s.ck[pos] = target;
+                s.cid[pos] = id0 + i;
+            }
+        }
+        running += __popc(bm);
+    }
+    __syncthreads();
+}
+
+// The K best of n keys in shared memory by (key desc, id asc), written sorted to out_key / out_id
+// (K entries; positions past n, when n < K, get key 0 and id INT_MAX, which rank last).
+// Masked entries (-inf) are left out of the radix select of the K-th key (8 bits per pass from
+// the top) and taken, lowest ids first, only when fewer than K entries are finite.  Ids: ids[i],
+// or id0 + i when ids is null (then ids grow with position).
+__device__ void block_select(const uint32_t *keys, const int *ids, int id0, int n, int K, SelScratch &s,
+                             uint32_t *out_key, int *out_id) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
+    const uint32_t KNEG = okey(-INFINITY);
     const int Kn = min(K, n);
+    // entries above -inf
+    int nf = 0;
+    for (int base = 0; base < n; base += NT) {
+        const int i = base + tid;
+        nf += __popc(__ballot_sync(0xffffffffu, i < n && keys[i] > KNEG));
+    }
+    if (lane == 0) s.wsum[wid] = nf;
+    __syncthreads();
+    nf = 0;
+    for (int w = 0; w < NW; w++) nf += s.wsum[w];
+    if (tid == 0) s.ncand = 0;
+    __syncthreads();
+    const int Kf = min(Kn, nf);
     uint32_t prefix = 0u, pmask = 0u;
-    int remaining = Kn;
+    int remaining = Kf;
     unsigned cnt_eq = 0u;
-    for (int pass = 3; pass >= 0 && Kn > 0; pass--) {
+    for (int pass = 3; pass >= 0 && Kf > 0; pass--) {
         for (int i = tid; i < 256; i += NT) s.hist[i] = 0u;
         __syncthreads();
         const int sh = 8 * pass;
         for (int i = tid; i < n; i += NT) {
             const uint32_t key = keys[i];
-            if ((key & pmask) == prefix) atomicAdd(&s.hist[(key >> sh) & 255u], 1u);
+            if (key > KNEG && (key & pmask) == prefix) atomicAdd(&s.hist[(key >> sh) & 255u], 1u);
         }
         __syncthreads();
         if (wid == 0) {
@@ -112,74 +178,37 @@ __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int 
         cnt_eq = s.hist[s.bin];
         __syncthreads();
     }
-    const uint32_t kstar = prefix;
-    if (tid == 0) s.ncand = 0;
-    __syncthreads();
-    for (int i = tid; i < n && Kn > 0; i += NT) {
-        const uint32_t key = keys[i];
-        if (key > kstar || (key == kstar && cnt_eq == (unsigned)remaining)) {
-            const int pos = atomicAdd(&s.ncand, 1);
-            if (pos < Kn) {
-                s.ck[pos] = key;
-                s.cid[pos] = ids ? ids[i] : id0 + i;
-            }
-        }
-    }
-    __syncthreads();
-    if (Kn > 0 && cnt_eq != (unsigned)remaining) {
-        // keep the `remaining` lowest ids among the entries equal to the threshold
-        if (!ids) {
-            int taken = 0;
-            for (int base = 0; base < n && taken < remaining; base += NT) {
-                const int i = base + tid;
-                const bool eq = i < n && keys[i] == kstar;
-                const unsigned bm = __ballot_sync(0xffffffffu, eq);
-                if (lane == 0) s.wsum[wid] = __popc(bm);
-                __syncthreads();
-                int before = 0, total = 0;
-                for (int w = 0; w < NW; w++) {
-                    if (w < wid) before += s.wsum[w];
-                    total += s.wsum[w];
-                }
-                const int rank = taken + before + __popc(bm & ((1u << lane) - 1u));
-                if (eq && rank < remaining) {
-                    const int pos = atomicAdd(&s.ncand, 1);
-                    if (pos < Kn) {
-                        s.ck[pos] = kstar;
-                        s.cid[pos] = id0 + i;
-                    }
-                }
-                taken += total;
-                __syncthreads();
-            }
-        } else {
-            for (int i = tid; i < n; i += NT) {
-                if (keys[i] != kstar) continue;
-                int r = 0;
-                for (int j = 0; j < n; j++) r += keys[j] == kstar && ids[j] < ids[i];
-                if (r < remaining) {
-                    const int pos = atomicAdd(&s.ncand, 1);
-                    if (pos < Kn) {
-                        s.ck[pos] = kstar;
-                        s.cid[pos] = ids[i];
-                    }
+    if (Kf > 0) {
+        const uint32_t kstar = prefix;
+        const bool all_eq = cnt_eq == (unsigned)remaining;
+        for (int i = tid; i < n; i += NT) {
+            const uint32_t key = keys[i];
+            if (key > kstar || (key == kstar && all_eq)) {
+                const int pos = atomicAdd(&s.ncand, 1);
+                if (pos < Kn) {
+                    s.ck[pos] = key;
+                    s.cid[pos] = ids ? ids[i] : id0 + i;
                 }
             }
         }
+        __syncthreads();
+        if (!all_eq) select_ties(keys, ids, id0, n, kstar, remaining, Kn, s);
     }
+    // fewer finite entries than K: the lowest-id masked ones
+    if (Kn > nf) select_ties(keys, ids, id0, n, KNEG, Kn - nf, Kn, s);
     __syncthreads();
     for (int i = tid; i < K; i += NT) {
         if (i >= Kn) {
-            okey[i] = 0u;
-            oid[i] = INT_MAX;
+            out_key[i] = 0u;
+            out_id[i] = INT_MAX;
             continue;
         }
         const uint32_t ki = s.ck[i];
         const int ii = s.cid[i];
         int r = 0;
         for (int j = 0; j < Kn; j++) r += s.ck[j] > ki || (s.ck[j] == ki && s.cid[j] < ii);
-        okey[r] = ki;
-        oid[r] = ii;
+        out_key[r] = ki;
+        out_id[r] = ii;
     }
     __syncthreads();
 }
@@ -188,7 +217,7 @@ __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int 
 // chunk's k best.  With one chunk per row they are the shard's final candidates.
 template <int DT>
 __global__ void __launch_bounds__(SH_T) shard_chunk_kernel(const ShardArgs a) {
-    __shared__ uint32_t keys[SH_CHUNK];
+    extern __shared__ __align__(16) uint32_t keys[];  // SH_CHUNK keys
     __shared__ int hkeys[SH_HTAB];
     __shared__ int hcnt[SH_HTAB];
     __shared__ SelScratch sel;
@@ -448,10 +477,15 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     }
     if (a.status) cudaMemsetAsync(a.status, 0, (size_t)a.rows * sizeof(int32_t), stream);
     const dim3 grid(a.nchunks, a.rows);
+    const size_t ks = (size_t)SH_CHUNK * 4;
+    const void *fn = d->dtype == DLLM_DTYPE_BF16 ? (const void *)shard_chunk_kernel<DLLM_DTYPE_BF16>
+                                                 : (const void *)shard_chunk_kernel<DLLM_DTYPE_F32>;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks) != cudaSuccess)
+        return DLLM_ERR_CUDA;
     if (d->dtype == DLLM_DTYPE_BF16)
-        shard_chunk_kernel<DLLM_DTYPE_BF16><<<grid, SH_T, 0, stream>>>(a);
+        shard_chunk_kernel<DLLM_DTYPE_BF16><<<grid, SH_T, ks, stream>>>(a);
     else
-        shard_chunk_kernel<DLLM_DTYPE_F32><<<grid, SH_T, 0, stream>>>(a);
+        shard_chunk_kernel<DLLM_DTYPE_F32><<<grid, SH_T, ks, stream>>>(a);
     if (a.nchunks > 1) shard_rowmerge_kernel<<<a.rows, SH_T, (size_t)a.nchunks * k * 8, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
 }
