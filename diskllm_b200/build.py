@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiskllm_cuda.so")
 
 SUB_LENGTHS = [4, 12, 20, 28, 36, 44, 52, 60]
-UNITS = [("dllm_launch.cu", []), ("dllm_capi.cu", []), ("dllm_noalloc.cu", []), ("dllm_shard.cu", [])] + [
+UNITS = [("dllm_launch.cu", []), ("dllm_capi.cu", []), ("dllm_noalloc.cu", []), ("dllm_shard.cu", []), ("dllm_grammar.cu", [])] + [
     ("dllm_kernel_inst.cu", [f"-DDLLM_SUB={s}"]) for s in SUB_LENGTHS
 ]
 SOURCES = sorted({u[0] for u in UNITS})
@@ -47,7 +47,7 @@ def _stale() -> bool:
         return True
     t = os.path.getmtime(LIB)
     deps = [os.path.join(CSRC, s) for s in SOURCES + HEADERS]
-    deps += [os.path.join(ROOT, "include", h) for h in ("diskllm_cuda.h", "sampler.h")]
+    deps += [os.path.join(ROOT, "include", h) for h in ("diskllm_cuda.h", "sampler.h", "grammar.h")]
     return any(os.path.getmtime(d) > t for d in deps)
 
 

@@ -34,6 +34,10 @@ EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
     "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
     "dllm_cuda_set_timing_events", "dllm_cuda_shard_candidates", "dllm_cuda_merge_sample",
+    "diskllm_grammar_init_from_file", "diskllm_grammar_init_from_str", "diskllm_grammar_init_json",
+    "diskllm_grammar_free", "diskllm_grammar_reset", "diskllm_grammar_accept_str", "diskllm_grammar_advance",
+    "diskllm_grammar_is_finished", "diskllm_grammar_apply_mask", "dllm_grammar_build_bitmask",
+    "dllm_grammar_vocab_create", "dllm_grammar_vocab_free", "dllm_grammar_build_bitmask_cached",
     "dllm_sampler_get_rng_state", "dllm_sampler_set_rng_state",
     "sampler_create", "sampler_free", "sampler_apply_repetition_penalty",
     "sampler_apply_presence_penalty", "sampler_sample", "greedy_sample",
@@ -376,3 +380,113 @@ def merge_sample(vals, ids, uniforms, params=None, *, row_params=None, token=Non
     if check and rc != DLLM_OK:
         raise DllmError(f"dllm_cuda_merge_sample: {STATUS_NAMES.get(rc, rc)} ({load_library().dllm_cuda_last_error().decode()})")
     return token
+
+
+# ---- grammar constraint (include/grammar.h) -------------------------------------------------
+
+TOKEN_STR_CB = C.CFUNCTYPE(C.c_void_p, C.c_void_p, C.c_int)  # returns const char *
+
+
+def _grammar_lib():
+    lib = load_library()
+    if not getattr(lib, "_grammar_typed", False):
+        lib.diskllm_grammar_init_from_str.restype = C.c_void_p
+        lib.diskllm_grammar_init_from_str.argtypes = [C.c_char_p]
+        lib.diskllm_grammar_init_from_file.restype = C.c_void_p
+        lib.diskllm_grammar_init_from_file.argtypes = [C.c_char_p]
+        lib.diskllm_grammar_init_json.restype = C.c_void_p
+        lib.diskllm_grammar_init_json.argtypes = []
+        lib.diskllm_grammar_free.argtypes = [C.c_void_p]
+        lib.diskllm_grammar_reset.argtypes = [C.c_void_p]
+        lib.diskllm_grammar_accept_str.restype = C.c_bool
+        lib.diskllm_grammar_accept_str.argtypes = [C.c_void_p, C.c_char_p]
+        lib.diskllm_grammar_advance.argtypes = [C.c_void_p, C.c_char_p]
+        lib.diskllm_grammar_is_finished.restype = C.c_bool
+        lib.diskllm_grammar_is_finished.argtypes = [C.c_void_p]
+        lib.diskllm_grammar_apply_mask.restype = C.c_int
+        lib.diskllm_grammar_apply_mask.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, TOKEN_STR_CB, C.c_int]
+        lib.dllm_grammar_build_bitmask.restype = C.c_int
+        lib.dllm_grammar_build_bitmask.argtypes = [C.c_void_p, C.c_int, C.c_void_p, TOKEN_STR_CB, C.c_int, C.c_void_p]
+        lib.dllm_grammar_vocab_create.restype = C.c_void_p
+        lib.dllm_grammar_vocab_create.argtypes = [C.c_int, C.c_void_p, TOKEN_STR_CB, C.c_int]
+        lib.dllm_grammar_vocab_free.argtypes = [C.c_void_p]
+        lib.dllm_grammar_build_bitmask_cached.restype = C.c_int
+        lib.dllm_grammar_build_bitmask_cached.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
+        lib._grammar_typed = True
+    return lib
+
+
+class Grammar:
+    """DiskLLM's grammar constraint (diskllm_grammar_*) with the bitmask builder."""
+
+    def __init__(self, text: str | None = None, *, json_mode: bool = False):
+        lib = _grammar_lib()
+        self._lib = lib
+        self._g = lib.diskllm_grammar_init_json() if json_mode else lib.diskllm_grammar_init_from_str(
+            text.encode() if text is not None else None)
+        if not self._g:
+            raise DllmError("diskllm_grammar_init failed")
+
+    def __del__(self):
+        if getattr(self, "_g", None):
+            self._lib.diskllm_grammar_free(self._g)
+            self._g = None
+
+    def reset(self):
+        self._lib.diskllm_grammar_reset(self._g)
+
+    def accept(self, piece: bytes) -> bool:
+        return bool(self._lib.diskllm_grammar_accept_str(self._g, piece))
+
+    def advance(self, piece: bytes):
+        self._lib.diskllm_grammar_advance(self._g, piece)
+
+    def finished(self) -> bool:
+        return bool(self._lib.diskllm_grammar_is_finished(self._g))
+
+    def bitmask(self, pieces, eos: int) -> tuple[np.ndarray, int]:
+        """(uint32 words, allowed count) for a vocabulary given as a list of bytes (None: no piece)."""
+        cb, keep = _pieces_callback(pieces)
+        words = np.zeros((len(pieces) + 31) // 32, dtype=np.uint32)
+        n = self._lib.dllm_grammar_build_bitmask(self._g, len(pieces), None, cb, eos, words.ctypes.data)
+        return words, n
+
+    def apply_mask(self, logits: np.ndarray, pieces, eos: int) -> int:
+        cb, keep = _pieces_callback(pieces)
+        assert logits.dtype == np.float32 and logits.flags.c_contiguous
+        return self._lib.diskllm_grammar_apply_mask(self._g, logits.ctypes.data, len(pieces), None, cb, eos)
+
+
+class GrammarVocab:
+    """Pieces read once (dllm_grammar_vocab_create) for per-step bitmasks without callbacks."""
+
+    def __init__(self, pieces, eos: int):
+        lib = _grammar_lib()
+        self._lib = lib
+        cb, keep = _pieces_callback(pieces)
+        self.n = len(pieces)
+        self._v = lib.dllm_grammar_vocab_create(len(pieces), None, cb, eos)
+        if not self._v:
+            raise DllmError("dllm_grammar_vocab_create failed")
+
+    def __del__(self):
+        if getattr(self, "_v", None):
+            self._lib.dllm_grammar_vocab_free(self._v)
+            self._v = None
+
+    def bitmask(self, grammar: Grammar, out: np.ndarray | None = None) -> tuple[np.ndarray, int]:
+        words = out if out is not None else np.zeros((self.n + 31) // 32, dtype=np.uint32)
+        n = self._lib.dllm_grammar_build_bitmask_cached(grammar._g, self._v, words.ctypes.data)
+        return words, n
+
+
+def _pieces_callback(pieces):
+    """A get_token_str callback over NUL-terminated copies of `pieces` (kept alive by the caller
+    through the second return value)."""
+    bufs = [None if p is None else C.create_string_buffer(p) for p in pieces]
+    addrs = [None if b is None else C.addressof(b) for b in bufs]
+
+    def get(_ctx, i):
+        return addrs[i]
+
+    return TOKEN_STR_CB(get), bufs
