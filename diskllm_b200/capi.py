@@ -34,6 +34,7 @@ EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
     "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
     "dllm_cuda_set_timing_events", "dllm_cuda_shard_candidates", "dllm_cuda_merge_sample",
+    "dllm_cuda_append_history",
     "diskllm_grammar_init_from_file", "diskllm_grammar_init_from_str", "diskllm_grammar_init_json",
     "diskllm_grammar_free", "diskllm_grammar_reset", "diskllm_grammar_accept_str", "diskllm_grammar_advance",
     "diskllm_grammar_is_finished", "diskllm_grammar_apply_mask", "dllm_grammar_build_bitmask",
@@ -125,6 +126,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_merge_sample.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                            C.POINTER(SamplerParams), C.c_void_p, C.c_void_p, C.c_void_p,
                                            C.c_void_p]
+    lib.dllm_cuda_append_history.restype = C.c_int
+    lib.dllm_cuda_append_history.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
     lib.dllm_cuda_set_timing_events.restype = C.c_int
     lib.dllm_cuda_set_timing_events.argtypes = [C.c_void_p, C.c_void_p]
     lib.dllm_cuda_sample_batch_static.restype = C.c_int

@@ -139,6 +139,37 @@ static dllm_status validate(const dllm_batch_desc *d) {
 }
 
 // ----------------------------------------------------------------------------------------
+// decode-loop glue: append each row's sampled token to its device-resident history
+
+// One sequence's history is hist_ids[hist_off[0], hist_off[1]) with room for `cap` ids from
+// hist_off[0]; the sampled token is appended (when full, the window slides: the oldest id goes),
+// so a decode loop can run step after step -- sample, append -- with no host round trip, and can
+// be captured once as a CUDA graph.
+__global__ void append_history_kernel(const int32_t *token, int32_t *hist_ids, int64_t *hist_off, int64_t cap) {
+    if (threadIdx.x != 0) return;
+    const int64_t start = hist_off[0], end = hist_off[1];
+    if (end - start < cap) {
+        hist_ids[end] = token[0];
+        hist_off[1] = end + 1;
+        return;
+    }
+    for (int64_t j = start; j + 1 < end; j++) hist_ids[j] = hist_ids[j + 1];
+    hist_ids[end - 1] = token[0];
+}
+
+extern "C" dllm_status dllm_cuda_append_history(const int32_t *token, int32_t *hist_ids, int64_t *hist_off,
+                                                int64_t cap, void *stream) {
+    if (!token || !hist_ids || !hist_off || cap <= 0) return DLLM_ERR_INVALID_ARG;
+    append_history_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(token, hist_ids, hist_off, cap);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error("history append kernel launch", e);
+        return DLLM_ERR_CUDA;
+    }
+    return DLLM_OK;
+}
+
+// ----------------------------------------------------------------------------------------
 // vocabulary-sharded sampling (no counterpart in the reference, whose sampler sees whole rows)
 
 extern "C" dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *d, int64_t vocab_offset, int64_t vocab_total,

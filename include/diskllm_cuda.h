@@ -168,6 +168,15 @@ DLLM_API dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const 
                                             const dllm_sampler_params *row_params,
                                             const float *uniforms, int32_t *token, void *stream);
 
+/* Decode-loop glue (no counterpart in the reference, whose caller appends to its seen-token
+ * array on the host): appends token[0] (device) to one sequence's device history
+ * hist_ids[hist_off[0], hist_off[1]), which has room for `cap` ids from hist_off[0]; when full,
+ * the oldest id is dropped.  Stream-ordered, so "sample, append" steps can run back to back and
+ * be captured in a CUDA graph (sample with a caller-provided workspace, or make one call before
+ * the capture, so that nothing is allocated during it). */
+DLLM_API dllm_status dllm_cuda_append_history(const int32_t *token, int32_t *hist_ids, int64_t *hist_off,
+                                              int64_t cap, void *stream);
+
 /* Diagnostics: when given two CUDA events (cudaEvent_t, created by the caller), every later
  * sampling call records `before` on its stream right before the cluster kernel and `after` right
  * after it, so the caller can time that kernel alone; NULLs switch it off.  No counterpart in
