@@ -330,6 +330,106 @@ def run_ours(args, rank, world, dev):
     print(json.dumps(line), flush=True)
 
 
+CFG1_VOCAB, CFG1_STEPS, CFG1_RING = 128256, 1000, 8
+
+
+def run_cfg1(args, rank, world, dev):
+    """Config 1: one sequence, 1000 dependent steps (sample, append the id to the history the
+    next step penalises), replayed as one CUDA graph.  Reported as steps (rows) per second."""
+    import numpy as np
+    import torch
+
+    from diskllm_b200 import workloads as W
+    from diskllm_b200.decode import DecodeLoop
+
+    w = W.config1(device=dev, seed=101 + rank)
+    g = torch.Generator(device=dev)
+    g.manual_seed(11 + rank)
+    ring = w.logits.repeat(CFG1_RING, 1) + 0.05 * torch.randn(CFG1_RING, CFG1_VOCAB, generator=g, device=dev)
+    u = torch.from_numpy(W.philox_uniforms(101 + rank, CFG1_STEPS)).to(dev)
+    loop = DecodeLoop(ring, u, dict(w.params), w.hist_ids, cap=64 + CFG1_STEPS)
+    loop.capture()
+    for _ in range(args.warmup):
+        loop.replay()
+    stream = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    reps = max(1, args.steps // 10)
+    clocks = ClockSampler(dev.index)
+    torch.cuda.synchronize(dev)
+    clocks.start()
+    e0.record(stream)
+    for _ in range(reps):
+        loop.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks.stop()
+    us_step = e0.elapsed_time(e1) * 1e3 / (reps * CFG1_STEPS)
+    # the same steps launched one by one from the host
+    e0.record(stream)
+    loop.run_eager()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us_eager = e0.elapsed_time(e1) * 1e3 / CFG1_STEPS
+    # end to end: each step's logits row from pinned host memory, the id back to the host
+    h_ring = ring.cpu().pin_memory()
+    h_tok = torch.empty(1, dtype=torch.int32).pin_memory()
+    n_e2e = 200
+    loop._reset()
+    e0.record(stream)
+    for i in range(n_e2e):
+        loop.ring[i % CFG1_RING].copy_(h_ring[i % CFG1_RING], non_blocking=True)
+        loop._step(i)
+        h_tok.copy_(loop.tokens[i:i + 1], non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    us_e2e = e0.elapsed_time(e1) * 1e3 / n_e2e
+    if rank != 0:
+        return
+    bytes_step = CFG1_VOCAB * 4 + 64 * 4
+    peak, peak_kind = measured_peak()
+    line = {
+        "metric": METRIC, "value": 1e6 / us_step, "unit": "rows/s", "n_gpus": world, "steps": reps * CFG1_STEPS,
+        "warmup": args.warmup, "ms_per_step": us_step / 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,2.5^2) row + 20 boosted ids, ring of 8 perturbed rows, Philox uniforms)",
+        "config": {"workload": "cfg1_single_row_v128256 (BASELINE config 1, latency)", "rows_per_gpu": 1,
+                   "vocab": CFG1_VOCAB, "history": "64 ids, appended each step", "params": dict(w.params),
+                   "parallelism": "one sequence per GPU", "us_per_step_graph": us_step,
+                   "us_per_step_eager": us_eager,
+                   "l2_policy": "8-row ring (4.1 MB) stays in L2: latency, not bandwidth, is measured"},
+        "roofline": {"bound": "latency", "achieved": bytes_step / (us_step * 1e-6) / 1e9, "peak": peak,
+                     "unit": "GB/s", "frac": bytes_step / (us_step * 1e-6) / 1e9 / peak,
+                     "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                     else "fallback 6650 GB/s", "traffic": None, "kernel": "one decode step (graph replay)"},
+        "e2e": {"value": 1e6 / us_e2e, "unit": "rows/s", "h2d_bytes_per_step": CFG1_VOCAB * 4,
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": reps * CFG1_STEPS * 3,
+        "clocks": clocks.summary(),
+    }
+    if not args.no_cpu:
+        # the reference's step on one host core, the same row and history
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        lg = w.logits.cpu().numpy()
+        hist = [w.hist_ids.cpu().numpy()]
+        reps_cpu, tot, kind = 0, 0.0, "port"
+        while tot < args.cpu_seconds:
+            if O.have_reference():
+                _, secs = O.sample_reference(lg, dict(w.params), hist=hist, threads=1, stream=True)
+                kind = "reference"
+            else:
+                t0 = time.perf_counter()
+                O.sample_restated(lg, dict(w.params), np.full(1, 0.5, np.float32), hist=hist, threads=1)
+                secs = time.perf_counter() - t0
+            tot += secs
+            reps_cpu += 1
+        line["cpu_baseline"] = {"value": reps_cpu / tot, "unit": "rows/s", "cores": 1, "kind": kind,
+                                "sample": f"{reps_cpu} single-row config 1 steps on one core"}
+    print(json.dumps(line), flush=True)
+
+
 CFG5_ROWS, CFG5_VOCAB, CFG5_HIST, CFG5_K = 512, 262144, 128, 64
 
 
@@ -439,8 +539,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["cfg4", "cfg5"], default="cfg4",
-                    help="cfg4: the headline row-sharded batch; cfg5: vocabulary-sharded config 5")
+    ap.add_argument("--workload", choices=["cfg4", "cfg5", "cfg1"], default="cfg4",
+                    help="cfg4: the headline row-sharded batch; cfg5: vocabulary-sharded config 5; "
+                         "cfg1: one-sequence decode latency (CUDA graph)")
     ap.add_argument("--rows", type=int, default=ROWS,
                     help="rows per GPU (default: config 4's 1024; smaller only for profiling captures)")
     args = ap.parse_args()
@@ -462,6 +563,8 @@ def main():
     try:
         if args.workload == "cfg5":
             run_cfg5(args, rank, world, dev)
+        elif args.workload == "cfg1":
+            run_cfg1(args, rank, world, dev)
         else:
             run_ours(args, rank, world, dev)
     finally:
