@@ -20,7 +20,7 @@
 //       and softmax / min-p / top-p / draw run on that short list (a 4-pass radix select is
 //       the fallback when too many elements survive the threshold)
 //   otherwise (top-k off: the reference's index-order list):
-//   P2  t = (x - M) * (1/T), e = expf(t - max_t) in place, compensated sum -> cluster sum
+//   P2  t = (x - M) * (1/T), e = exp(t - max_t) in place, compensated sum -> cluster sum
 //   P2b min-p (absolute threshold) kept count / renormalisation sum      -> cluster sums
 //   P3  sub-chunk sums of the list probabilities, exclusive scan over the cluster; the one warp
 //       holding the sub-chunk where (float)cumsum first reaches top_p finds the cut element
@@ -183,10 +183,23 @@ struct Shared {
     int bcast_i[4];
 };
 
-// Compensated fp32 sum of values in [0, 1]: the running sum starts at CSUM_BASE (2.0), so it is
-// never below the next addend and Fast2Sum (t = s + x; err = x - (t - s)) recovers each
-// rounding error exactly; s + c - CSUM_BASE carries ~48 bits.
-constexpr float CSUM_BASE = 2.0f;
+// Exponential of the index-order path, from the identity e^t = 2^(t * log2(e)) on the hardware
+// base-2 exponential (PTX ex2.approx.ftz.f32, relative error about 2^-22): two instructions.  For
+// t <= 0 the result is within about 2.5e-7 of e^t relative (the product's rounding adds
+// |t| * 2^-24 * ln 2, which only matters where e^t is already tiny); -inf gives +0.  The
+// reference's own softmax mixes glibc's scalar and 4-wide vector expf, which differ by up to
+// 3 ulp, so agreement is to the sampler's probability tolerance, not to the bit.  The cluster
+// kernel and the walk kernel both use this function, so they agree with each other exactly.
+__device__ __forceinline__ float exp_t(float t) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fmul_rn(t, 1.44269504088896341f)));
+    return r;
+}
+
+// Compensated fp32 sum of values in [0, 4] (single probabilities, or sums of four): the running
+// sum starts at CSUM_BASE (8.0), so it is never below the next addend and Fast2Sum (t = s + x;
+// err = x - (t - s)) recovers each rounding error exactly; s + c - CSUM_BASE carries ~44 bits.
+constexpr float CSUM_BASE = 8.0f;
 struct CSum {
     float s, c;
 };
@@ -822,6 +835,8 @@ __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, 
         sub[q] = csum_zero();
         real[q] = kb[q] < S;
     }
+    // temperature 1 (and no shift): ((x - M) * 1) - 0 == x - M exactly, so skip the two no-ops
+    const bool plain = inv_temp == 1.0f && mv == 0.0f;
 #pragma unroll 2
     for (int j = 0; j < NV4; j++) {
 #pragma unroll
@@ -829,15 +844,21 @@ __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, 
             if (real[q]) {
                 float4 *p = reinterpret_cast<float4 *>(vals + kb[q] + 4 * j);
                 float4 x = *p;
-                x.x = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
-                x.y = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
-                x.z = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
-                x.w = expf(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
+                if (plain) {
+                    x.x = exp_t(__fsub_rn(x.x, M));
+                    x.y = exp_t(__fsub_rn(x.y, M));
+                    x.z = exp_t(__fsub_rn(x.z, M));
+                    x.w = exp_t(__fsub_rn(x.w, M));
+                } else {
+                    x.x = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
+                    x.y = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
+                    x.z = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
+                    x.w = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
+                }
                 *p = x;
-                csum_add(sub[q], x.x);
-                csum_add(sub[q], x.y);
-                csum_add(sub[q], x.z);
-                csum_add(sub[q], x.w);
+                // the four summed plainly (error ~2^-24 of a 4-element sum), the group sum
+                // compensated
+                csum_add(sub[q], __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(x.z, x.w)));
             }
         }
     }
@@ -2023,7 +2044,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                     }
             }
         }
-        const float e = expf(__fsub_rn(__fmul_rn(__fsub_rn(v, h.M), h.inv_temp), h.mv));
+        const float e = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(v, h.M), h.inv_temp), h.mv));
         return q_of(ch, e, li);
     };
     // replays elements [start, start + n) (n <= 32 * SUBT) on the exact running sum, from the
