@@ -425,6 +425,20 @@ __device__ __forceinline__ void compose_scan(uint32_t &a0, uint32_t &a1) {
 // Four independent composition scans side by side (general parity form).
 __device__ __forceinline__ void compose_scan4(uint32_t (&a0)[4], uint32_t (&a1)[4]) {
     const int lane = threadIdx.x & 31;
+    if (__ballot_sync(0xffffffffu, a0[0] != a1[0] || a0[1] != a1[1] || a0[2] != a1[2] || a0[3] != a1[3]) == 0u) {
+        // no run depends on the parity: plain prefix sums
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const uint32_t p0 = __shfl_up_sync(0xffffffffu, a0[q], d);
+                if (lane >= d) a0[q] += p0;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 4; q++) a1[q] = a0[q];
+        return;
+    }
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
 #pragma unroll
@@ -1830,6 +1844,18 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     a1[q] = pin ? c1[q] : 0u;
                 }
                 compose_scan4(a0, a1);
+                const bool any_nonconf = (nonconf[0] | nonconf[1] | nonconf[2] | nonconf[3]) != 0u;
+                if (!any_nonconf) {
+                    // every quarter is one run (or empty): no boundary, no suffix
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        sfrom[q] = 32;
+                        bchunk[q] = -1;
+                        e_s[q] = 0;
+                        type[q] = cleanm[q] ? REC_CLEAN : REC_IDENT;
+                        b0[q] = b1[q] = 0u;
+                    }
+                } else {
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
                     const int tj = __shfl_sync(0xffffffffu, ctype[q], jx[q] & 31);
@@ -1845,6 +1871,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     b1[q] = sin ? c1[q] : 0u;
                 }
                 compose_scan4(b0, b1);
+                }
                 // stash / wide slots for the four quarters: one claim per warp on CTA 0's counter
                 bool need_st[4], need_wd[4];
                 int n_st = 0, n_wd = 0;
@@ -1863,6 +1890,23 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     st_next = base & 0xffff;
                     wd_next = base >> 16;
                 }
+                if (n_st + n_wd == 0) {
+                    // nothing to keep: the four records only
+                    if (lane == 31) {
+#pragma unroll
+                        for (int q = 0; q < 4; q++) {
+                            WRec wr;
+                            wr.meta = pack_meta(type[q], bchunk[q], sfrom[q], e_first[q], e_s[q]);
+                            wr.p0 = a0[q];
+                            wr.p1 = a1[q];
+                            wr.s0 = b0[q];
+                            wr.s1 = b1[q];
+                            wr.nslot = -1;
+                            wr.wslot = -1;
+                            recs[rank * 4 * NW + q * NW + wid] = wr;
+                        }
+                    }
+                } else
 #pragma unroll 1
                 for (int q = 0; q < 4; q++) {
                     const int typeq = pick4(type, q), bchunkq = pick4(bchunk, q);
