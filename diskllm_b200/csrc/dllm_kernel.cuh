@@ -1066,10 +1066,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 
         // ---------------- P1: bulk copy in flight while the history table is built ---------------
         if (tid == 0) {
-            if (use_tma && !dbuf) {
-                if (it > 0) issue_row_copy(row, 0);
-                if (row + ncl < a.rows) prefetch_row(row + ncl);
-            }
+            // the slice of this CTA's next row is copied in from the end of this row on; the one
+            // after it is pulled into L2 now
+            if (use_tma && !dbuf && row + 2 * ncl < a.rows) prefetch_row(row + 2 * ncl);
             // CTA 0's slot counter of the next row (its last claims, two rows back, are done)
             if (rank == 0) sh.slots[(it + 1) & 1] = 0;
             sh.xs.cut_idx = -1;
@@ -1919,7 +1918,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                             const int sb = (q * NT + 32 * wid + bchunkq) * SUBT;
                             float *qs = stash + nslot * STASH_STRIDE;
                             if (lane == 0) qs[0] = __int_as_float(slice0 + sb);
-                            for (int k = lane; k < SUBT; k += 32) qs[1 + k] = q_of(ch, vals[sb + k], slice0 + sb + k);
+                            for (int k = lane; k < SUBT; k += 32) qs[1 + k] = vals[sb + k];  // e; the walk forms q
                         } else if (timing) {
                             dbg_add(DBG_STASH_MISS, 1);
                         }
@@ -1933,14 +1932,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                             const int kq = pick4(kb, q);
                             float *ws = row_wide(a, row) + wslot * WIDE_STRIDE + lane * SUBT;
 #pragma unroll 1
-                            for (int k = 0; k < SUBT; k += 4) {
-                                float4 o;
-                                o.x = q_of(ch, vals[kq + k], slice0 + kq + k);
-                                o.y = q_of(ch, vals[kq + k + 1], slice0 + kq + k + 1);
-                                o.z = q_of(ch, vals[kq + k + 2], slice0 + kq + k + 2);
-                                o.w = q_of(ch, vals[kq + k + 3], slice0 + kq + k + 3);
-                                *reinterpret_cast<float4 *>(ws + k) = o;
-                            }
+                            for (int k = 0; k < SUBT; k += 4)  // exponentials; the walk forms q
+                                *reinterpret_cast<float4 *>(ws + k) = *reinterpret_cast<const float4 *>(vals + kq + k);
                         } else if (timing) {
                             dbg_add(DBG_STASH_MISS, 1);
                         }
@@ -1963,6 +1956,15 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
 
     row_done:
+        if (use_tma && !dbuf) {
+            // every read of this row's slice is done: the next row's bulk copy starts now and
+            // overlaps the end of this row and the start of the next
+            __syncthreads();
+            if (tid == 0 && row + ncl < a.rows) {
+                fence_proxy_async();
+                issue_row_copy(row + ncl, 0);
+            }
+        }
         if (done && rank == 0 && tid == 0) {
             if (token < 0) token = 0;
             a.token[row] = token + a.vocab_offset;
@@ -2154,6 +2156,9 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                     for (int i = lane; i < 8 * SUBT; i += 32) cp_async16(rv + 4 * i, wsrc + 4 * i);
                     cp_async_wait_all();
                     __syncwarp();
+                    // the slot holds exponentials: draw probabilities as the cluster kernel forms them
+                    for (int i = lane; i < 32 * SUBT; i += 32) rv[i] = q_of(ch, rv[i], start + i);
+                    __syncwarp();
                     wide_in = true;
                 }
                 const int res = replay_elems(n, st, cbv, r, rv + (st - start));
@@ -2179,7 +2184,13 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                     stage = 2;
                     if (bc != 63 && slot >= 0) {
                         const float *qs = stash + slot * STASH_STRIDE;
-                        const int found = replay_elems(SUBT, __float_as_int(qs[0]), c, r, qs + 1);
+                        const int sbase = __float_as_int(qs[0]);
+                        // the slot holds exponentials: probabilities into the region buffer
+                        for (int k = lane; k < SUBT; k += 32) rv[k] = q_of(ch, qs[1 + k], sbase + k);
+                        __syncwarp();
+                        const int found = replay_elems(SUBT, sbase, c, r, rv);
+                        __syncwarp();
+                        wide_in = false;  // the region buffer no longer holds the wide slot
                         if (found != -1) return found;
                     } else if (bc != 63) {
                         st = start + bc * SUBT;
