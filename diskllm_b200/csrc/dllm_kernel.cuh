@@ -1272,14 +1272,27 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 // threshold: the k-th largest per-thread maximum (>= k elements at or above it)
                 uint32_t tmax = 0u;
                 for (int i = tid; i < slen; i += NT) tmax = max(tmax, key_of(vals[i]));
-                uint32_t pref = 0u;
-                for (int bit = 31; bit >= 0; bit--) {
-                    const uint32_t cv = pref | (1u << bit);
-                    if (__syncthreads_count(tmax >= cv) >= k) pref = cv;
-                }
-                if (tid == 0) {
-                    sh.xs.theta = pref;
-                    sh.xs.ncand = 0;
+                // the k-th largest of the NT maxima, found by one warp bit by bit with ballots
+                // (the CTA's candidate area is free until the survivors are gathered)
+                unsigned *tm_s = reinterpret_cast<unsigned *>(uni);
+                tm_s[tid] = tmax;
+                __syncthreads();
+                if (wid == 0) {
+                    uint32_t mine[MAXW];
+#pragma unroll
+                    for (int t = 0; t < MAXW; t++) mine[t] = 32 * t + lane < NT ? tm_s[32 * t + lane] : 0u;
+                    uint32_t pref = 0u;
+                    for (int bit = 31; bit >= 0; bit--) {
+                        const uint32_t cv = pref | (1u << bit);
+                        int cnt = 0;
+#pragma unroll
+                        for (int t = 0; t < MAXW; t++) cnt += __popc(__ballot_sync(0xffffffffu, mine[t] >= cv));
+                        if (cnt >= k) pref = cv;
+                    }
+                    if (lane == 0) {
+                        sh.xs.theta = pref;
+                        sh.xs.ncand = 0;
+                    }
                 }
                 cluster.sync();  // ---- threshold
                 uint32_t tv = 0u;
@@ -1439,34 +1452,49 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 const int n = sh.xs.ncand;
                 int P = 1;
                 while (P < n) P <<= 1;
-                for (int i = n + tid; i < P; i += NT) cand[i] = 0ull;
-                __syncthreads();
-                // bitonic sort, descending on (key, ~id)
-                for (int size = 2; size <= P; size <<= 1) {
-                    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-                        for (int i = tid; i < P; i += NT) {
-                            const int j = i ^ stride;
-                            if (j > i) {
-                                const bool desc = (i & size) == 0;
-                                const unsigned long long x = cand[i], y = cand[j];
-                                if (desc ? (x < y) : (x > y)) {
-                                    cand[i] = y;
-                                    cand[j] = x;
-                                }
-                            }
-                        }
-                        __syncthreads();
-                    }
-                }
                 float *tl = reinterpret_cast<float *>(cand + P);
                 int *il = reinterpret_cast<int *>(tl + k);
-                for (int i = tid; i < k; i += NT) {
-                    const unsigned long long c = cand[i];
-                    tl[i] = okey_inv((uint32_t)(c >> 32));
-                    il[i] = (int)(0xffffffffu - (uint32_t)(c & 0xffffffffu));
-                    if (a.topk_ids) a.topk_ids[(int64_t)row * a.topk_stride + i] = il[i] + a.vocab_offset;
+                if (n <= 512) {
+                    // the k best by rank: (key, ~id) composites are distinct, so a survivor's rank
+                    // is the count of larger ones; ranks < k are kept (t descending, lower id first)
+                    for (int i = tid; i < n; i += NT) {
+                        const unsigned long long ci = cand[i];
+                        int rk = 0;
+                        for (int j = 0; j < n; j++) rk += cand[j] > ci;
+                        if (rk < k) {
+                            tl[rk] = okey_inv((uint32_t)(ci >> 32));
+                            il[rk] = (int)(0xffffffffu - (uint32_t)(ci & 0xffffffffu));
+                        }
+                    }
+                } else {
+                    for (int i = n + tid; i < P; i += NT) cand[i] = 0ull;
+                    __syncthreads();
+                    // bitonic sort, descending on (key, ~id)
+                    for (int size = 2; size <= P; size <<= 1) {
+                        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                            for (int i = tid; i < P; i += NT) {
+                                const int j = i ^ stride;
+                                if (j > i) {
+                                    const bool desc = (i & size) == 0;
+                                    const unsigned long long x = cand[i], y = cand[j];
+                                    if (desc ? (x < y) : (x > y)) {
+                                        cand[i] = y;
+                                        cand[j] = x;
+                                    }
+                                }
+                            }
+                            __syncthreads();
+                        }
+                    }
+                    for (int i = tid; i < k; i += NT) {
+                        const unsigned long long c = cand[i];
+                        tl[i] = okey_inv((uint32_t)(c >> 32));
+                        il[i] = (int)(0xffffffffu - (uint32_t)(c & 0xffffffffu));
+                    }
                 }
                 __syncthreads();
+                if (a.topk_ids)
+                    for (int i = tid; i < k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = il[i] + a.vocab_offset;
                 if (wid == 0) {
                     float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride : nullptr;
                     token = sample_sorted_list(tl, il, k, p, r, pr);
