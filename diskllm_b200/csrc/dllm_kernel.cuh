@@ -196,6 +196,39 @@ __device__ __forceinline__ float exp_t(float t) {
     return r;
 }
 
+// Packed fp32 pairs (sm_100 f32x2): each lane rounds exactly like the scalar .rn.ftz operation,
+// one instruction per pair.
+__device__ __forceinline__ float2 fsub2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "sub.rn.ftz.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.ftz.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.ftz.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+// 2^x (hardware base-2 exponential), the second step of exp_t
+__device__ __forceinline__ float ex2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
 // Compensated fp32 sum of values in [0, 4] (single probabilities, or sums of four): the running
 // sum starts at CSUM_BASE (8.0), so it is never below the next addend and Fast2Sum (t = s + x;
 // err = x - (t - s)) recovers each rounding error exactly; s + c - CSUM_BASE carries ~44 bits.
@@ -851,6 +884,8 @@ __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, 
     }
     // temperature 1 (and no shift): ((x - M) * 1) - 0 == x - M exactly, so skip the two no-ops
     const bool plain = inv_temp == 1.0f && mv == 0.0f;
+    const float2 M2 = make_float2(M, M), IT2 = make_float2(inv_temp, inv_temp), MV2 = make_float2(mv, mv);
+    const float2 L2E2 = make_float2(1.44269504088896341f, 1.44269504088896341f);
 #pragma unroll 2
     for (int j = 0; j < NV4; j++) {
 #pragma unroll
@@ -858,21 +893,20 @@ __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, 
             if (real[q]) {
                 float4 *p = reinterpret_cast<float4 *>(vals + kb[q] + 4 * j);
                 float4 x = *p;
-                if (plain) {
-                    x.x = exp_t(__fsub_rn(x.x, M));
-                    x.y = exp_t(__fsub_rn(x.y, M));
-                    x.z = exp_t(__fsub_rn(x.z, M));
-                    x.w = exp_t(__fsub_rn(x.w, M));
-                } else {
-                    x.x = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.x, M), inv_temp), mv));
-                    x.y = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.y, M), inv_temp), mv));
-                    x.z = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.z, M), inv_temp), mv));
-                    x.w = exp_t(__fsub_rn(__fmul_rn(__fsub_rn(x.w, M), inv_temp), mv));
+                // t = ((x - M) * (1/T)) - mv, then e = 2^(t * log2 e), two elements per instruction
+                float2 t01 = fsub2(make_float2(x.x, x.y), M2), t23 = fsub2(make_float2(x.z, x.w), M2);
+                if (!plain) {
+                    t01 = fsub2(fmul2(t01, IT2), MV2);
+                    t23 = fsub2(fmul2(t23, IT2), MV2);
                 }
+                t01 = fmul2(t01, L2E2);
+                t23 = fmul2(t23, L2E2);
+                x = make_float4(ex2(t01.x), ex2(t01.y), ex2(t23.x), ex2(t23.y));
                 *p = x;
                 // the four summed plainly (error ~2^-24 of a 4-element sum), the group sum
                 // compensated
-                csum_add(sub[q], __fadd_rn(__fadd_rn(x.x, x.y), __fadd_rn(x.z, x.w)));
+                const float2 s2 = fadd2(make_float2(x.x, x.y), make_float2(x.z, x.w));
+                csum_add(sub[q], __fadd_rn(s2.x, s2.y));
             }
         }
     }
@@ -921,17 +955,25 @@ __device__ __forceinline__ void p3_scan(const float *vals, const int (&kb)[4], i
 template <bool MINP, int NV4>
 __device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], const int (&lim)[4], const Chain &ch,
                                         float scale3, float (&g0)[4], float (&g1)[4], float (&qmax)[4]) {
+    const float2 IS2 = make_float2(ch.inv_sum, ch.inv_sum), S32 = make_float2(scale3, scale3);
 #pragma unroll 2
     for (int j = 0; j < NV4; j++) {
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
-            const float e4[4] = {x.x, x.y, x.z, x.w};
+            // w = e * inv_sum (then min-p), q = w * scale3, two elements per multiply
+            float2 w01 = fmul2(make_float2(x.x, x.y), IS2), w23 = fmul2(make_float2(x.z, x.w), IS2);
+            if (MINP) {
+                w01.x = (ch.nokept || w01.x >= ch.min_p) ? __fmul_rn(w01.x, ch.inv_s2) : 0.0f;
+                w01.y = (ch.nokept || w01.y >= ch.min_p) ? __fmul_rn(w01.y, ch.inv_s2) : 0.0f;
+                w23.x = (ch.nokept || w23.x >= ch.min_p) ? __fmul_rn(w23.x, ch.inv_s2) : 0.0f;
+                w23.y = (ch.nokept || w23.y >= ch.min_p) ? __fmul_rn(w23.y, ch.inv_s2) : 0.0f;
+            }
+            const float2 q01 = fmul2(w01, S32), q23 = fmul2(w23, S32);
+            const float q4[4] = {q01.x, q01.y, q23.x, q23.y};
 #pragma unroll
             for (int c = 0; c < 4; c++) {
-                float w = __fmul_rn(e4[c], ch.inv_sum);
-                if (MINP) w = (ch.nokept || w >= ch.min_p) ? __fmul_rn(w, ch.inv_s2) : 0.0f;
-                float qv = __fmul_rn(w, scale3);
+                float qv = q4[c];
                 qv = (4 * j + c <= lim[q]) ? qv : 0.0f;
                 qmax[q] = fmaxf(qmax[q], qv);
                 g0[q] = __fadd_rn(g0[q], qv);
