@@ -1113,6 +1113,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             if (use_tma && !dbuf && row + 2 * ncl < a.rows) prefetch_row(row + 2 * ncl);
             // CTA 0's slot counter of the next row (its last claims, two rows back, are done)
             if (rank == 0) sh.slots[(it + 1) & 1] = 0;
+            sh.bcast_i[2] = 0;  // the CTA's row status bits
             sh.xs.cut_idx = -1;
         }
         for (int i = tid; i < a.htab; i += NT) {
@@ -1163,10 +1164,34 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
             }
         }
+        if (flags) atomicOr(&sh.bcast_i[2], flags);
         __syncthreads();
         mark(DBG_LOADWAIT);
 
-        // mask + raw maximum (strided float4 pass over the slice)
+        // ---------------- P1: penalties on the raw logits (sparse), then mask + maximum ---------
+        // Penalising before masking gives the reference's values (mask -> presence ->
+        // repetition): a masked entry ends at -inf either way, and the others are not masked.
+        if (use_hist) {
+            const float inv_rep = __fdiv_rn(1.0f, p.repetition);
+            const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
+            for (int s = tid; s < a.htab; s += NT) {
+                const int li = hkeys[s];
+                if (li < 0) continue;
+                const int c = hcnt[s];
+                float v = vals[li];
+                if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
+                if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
+                if (p.repetition > 1.0f) {
+                    for (int k = 0; k < c; k++) {
+                        if (v < 0.0f) v = __fmul_rn(v, p.repetition);
+                        else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
+                    }
+                }
+                vals[li] = v;
+            }
+            __syncthreads();
+        }
+        // mask + maximum (strided float4 pass over the slice)
         float lmax = -INFINITY;
         {
             float4 *v4 = reinterpret_cast<float4 *>(vals);
@@ -1191,50 +1216,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             }
         }
         mark(DBG_MAXP);
-        const float mraw = block_allreduce(lmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
-
-        // ---------------- P1: penalties ----------------------------------------------------------
-        float pmax = -INFINITY;
-        int rescan = 0;
-        if (use_hist) {
-            const float inv_rep = __fdiv_rn(1.0f, p.repetition);
-            const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
-            for (int s = tid; s < a.htab; s += NT) {
-                const int li = hkeys[s];
-                if (li < 0) continue;
-                const int c = hcnt[s];
-                float v = vals[li];
-                const float raw = v;
-                if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
-                if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
-                if (p.repetition > 1.0f) {
-                    for (int k = 0; k < c; k++) {
-                        if (v < 0.0f) v = __fmul_rn(v, p.repetition);
-                        else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
-                    }
-                }
-                vals[li] = v;
-                if (raw == mraw) rescan = 1;
-                pmax = fmaxf(pmax, v);
-            }
-        }
-        float lm;
-        {
-            const float pm = block_allreduce(pmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
-            const int rf = block_allreduce((rescan ? 0x10000 : 0) | flags, sh.red_i, [](int x, int y) { return x | y; }, 0);
-            flags = rf & 0xffff;
-            if (rf & 0x10000) {
-                float m2 = -INFINITY;
-                const float4 *v4 = reinterpret_cast<const float4 *>(vals);
-                for (int i = tid; i < S / 4; i += NT) {
-                    const float4 x = v4[i];
-                    m2 = fmaxf(m2, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
-                }
-                lm = block_allreduce(m2, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
-            } else {
-                lm = fmaxf(mraw, pm);
-            }
-        }
+        const float lm = block_allreduce(lmax, sh.red_f, [](float x, float y) { return fmaxf(x, y); }, -INFINITY);
+        flags = sh.bcast_i[2];
         if (a.pen_out) {
             float *po = a.pen_out + (int64_t)row * a.pen_stride + slice0;
             for (int i = tid; i < slen; i += NT) po[i] = vals[i];
