@@ -220,7 +220,7 @@ extern "C" size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *d) {
     if (tk > KMAX) return 0;
     LaunchCfg cfg;
     if (get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, tk, &cfg) != DLLM_OK) return 0;
-    return (size_t)d->rows * row_ws_bytes(nrec_for(cfg));
+    return (size_t)d->rows * row_ws_bytes(nrec_for(cfg), cfg.SUB);
 }
 
 extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *stream) {
@@ -234,7 +234,7 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
     st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
     if (st != DLLM_OK) return st;
     const int nrec = nrec_for(cfg);
-    const size_t ws_need = (size_t)d->rows * row_ws_bytes(nrec);
+    const size_t ws_need = (size_t)d->rows * row_ws_bytes(nrec, cfg.SUB);
     void *ws = d->workspace;
     if (ws) {
         if (d->workspace_bytes < ws_need) return DLLM_ERR_INVALID_ARG;

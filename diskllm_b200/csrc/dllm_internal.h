@@ -74,11 +74,12 @@ constexpr int STASH_SLOTS = 32;
 constexpr int STASH_STRIDE = 64;   // floats per stash slot: [0] = first index (as int), then SUB values
 constexpr int MAX_SUB = 60;
 constexpr int WIDE_SLOTS = 4;              // warp ranges (32 sub-chunks) kept whole for the walk
-constexpr int WIDE_STRIDE = 32 * MAX_SUB;  // floats per wide slot
+// floats per wide slot: one warp range, 32 sub-chunks of `sub` elements
+__host__ __device__ inline int wide_stride(int sub) { return 32 * sub; }
 // RowHdr (128 B) + nrec 24-byte warp records (rounded to 128 B) + the stash + the wide slots
-__host__ __device__ inline size_t row_ws_bytes(int nrec) {
+__host__ __device__ inline size_t row_ws_bytes(int nrec, int sub) {
     return 128 + (((size_t)nrec * 24 + 127) & ~(size_t)127) + (size_t)STASH_SLOTS * STASH_STRIDE * 4 +
-           (size_t)WIDE_SLOTS * WIDE_STRIDE * 4;
+           (size_t)WIDE_SLOTS * wide_stride(sub) * 4;
 }
 
 // shared memory of one walk-kernel warp: its row's warp records and stash, copied in at the start

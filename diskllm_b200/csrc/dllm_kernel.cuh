@@ -111,7 +111,7 @@ __device__ __forceinline__ void cp_async16(void *smem_dst, const void *gsrc) {
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 __device__ __forceinline__ RowHdr *row_hdr(const KernelArgs &a, int row) {
-    return reinterpret_cast<RowHdr *>(a.ws + (size_t)row * row_ws_bytes(a.nrec));
+    return reinterpret_cast<RowHdr *>(a.ws + (size_t)row * row_ws_bytes(a.nrec, a.SUB));
 }
 __device__ __forceinline__ WRec *row_recs(const KernelArgs &a, int row) {
     return reinterpret_cast<WRec *>(reinterpret_cast<unsigned char *>(row_hdr(a, row)) + sizeof(RowHdr));
@@ -1983,7 +1983,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         wd_next++;
                         if (wslot >= 0) {
                             const int kq = pick4(kb, q);
-                            float *ws = row_wide(a, row) + wslot * WIDE_STRIDE + lane * SUBT;
+                            float *ws = row_wide(a, row) + wslot * wide_stride(SUBT) + lane * SUBT;
 #pragma unroll 1
                             for (int k = 0; k < SUBT; k += 4)  // exponentials; the walk forms q
                                 *reinterpret_cast<float4 *>(ws + k) = *reinterpret_cast<const float4 *>(vals + kq + k);
@@ -2205,7 +2205,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                 if (n <= 0) return -1;
                 if (wslot < 0) return replay_region(st, n, cbv);
                 if (!wide_in) {
-                    const float *wsrc = row_wide(a, row) + wslot * WIDE_STRIDE;
+                    const float *wsrc = row_wide(a, row) + wslot * wide_stride(SUBT);
                     for (int i = lane; i < 8 * SUBT; i += 32) cp_async16(rv + 4 * i, wsrc + 4 * i);
                     cp_async_wait_all();
                     __syncwarp();

@@ -133,7 +133,7 @@ DLLM_API size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *desc);
  * of cudaMalloc/cudaFree.  Instead of a caller buffer or a library-grown one, it uses a
  * 16 MiB scratch array compiled into the library (held on every GPU that loads the library
  * until the process exits); desc->workspace is ignored.  Batches whose
- * dllm_cuda_workspace_bytes() exceeds 16 MiB (about 1,200 rows of vocab 256000) are rejected
+ * dllm_cuda_workspace_bytes() exceeds 16 MiB (about 550 rows of vocab 256000) are rejected
  * with DLLM_ERR_UNSUPPORTED and a message in dllm_cuda_last_error().  The first call on a
  * device looks up the array's device address and picks the launch configuration, so make it
  * before any stream capture.  Every call shares the one array: calls whose work overlaps on the
