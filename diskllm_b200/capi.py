@@ -34,7 +34,7 @@ EXPORTS = [
     "dllm_cuda_sample_batch", "dllm_cuda_version", "dllm_cuda_last_error",
     "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
     "dllm_cuda_set_timing_events", "dllm_cuda_shard_candidates", "dllm_cuda_merge_sample",
-    "dllm_cuda_append_history",
+    "dllm_cuda_append_history", "dllm_cuda_lmhead_logits",
     "diskllm_grammar_init_from_file", "diskllm_grammar_init_from_str", "diskllm_grammar_init_json",
     "diskllm_grammar_free", "diskllm_grammar_reset", "diskllm_grammar_accept_str", "diskllm_grammar_advance",
     "diskllm_grammar_is_finished", "diskllm_grammar_apply_mask", "dllm_grammar_build_bitmask",
@@ -126,6 +126,9 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_merge_sample.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                            C.POINTER(SamplerParams), C.c_void_p, C.c_void_p, C.c_void_p,
                                            C.c_void_p]
+    lib.dllm_cuda_lmhead_logits.restype = C.c_int
+    lib.dllm_cuda_lmhead_logits.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_int,
+                                            C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p]
     lib.dllm_cuda_append_history.restype = C.c_int
     lib.dllm_cuda_append_history.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]
     lib.dllm_cuda_set_timing_events.restype = C.c_int
@@ -493,3 +496,25 @@ def _pieces_callback(pieces):
         return addrs[i]
 
     return TOKEN_STR_CB(get), bufs
+
+
+def lmhead_logits(h, w, *, norm_w=None, eps=1e-6, add_one=False, softcap=0.0, logits=None, stream=None, check=True):
+    """Final RMSNorm + logits matvec + softcap (dllm_cuda_lmhead_logits): h fp32 [rows][hidden],
+    w [vocab][hidden] fp32 / bf16 / fp16 (CUDA tensors); returns fp32 logits [rows][vocab]."""
+    import torch
+
+    rows, hidden = h.shape
+    vocab = w.shape[0]
+    assert h.dtype == torch.float32 and h.is_contiguous() and w.is_contiguous() and w.shape[1] == hidden
+    wdt = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: 2}[w.dtype]
+    if logits is None:
+        logits = torch.empty(rows, vocab, dtype=torch.float32, device=h.device)
+    s = stream if stream is not None else torch.cuda.current_stream(h.device).cuda_stream
+    rc = load_library().dllm_cuda_lmhead_logits(rows, hidden, vocab, h.data_ptr(),
+                                                None if norm_w is None else norm_w.data_ptr(), float(eps),
+                                                int(bool(add_one)), w.data_ptr(), wdt, float(softcap),
+                                                logits.data_ptr(), s)
+    if check and rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_lmhead_logits: {STATUS_NAMES.get(rc, rc)} "
+                        f"({load_library().dllm_cuda_last_error().decode()})")
+    return logits

@@ -170,6 +170,30 @@ extern "C" dllm_status dllm_cuda_append_history(const int32_t *token, int32_t *h
 }
 
 // ----------------------------------------------------------------------------------------
+// LM-head tail: final norm, logits matvec, softcap (no sampling)
+
+extern "C" dllm_status dllm_cuda_lmhead_logits(int rows, int hidden, int vocab, const float *h, const float *norm_w,
+                                               float eps, int add_one, const void *w, int w_dtype, float softcap,
+                                               float *logits, void *stream) {
+    if (rows < 0 || hidden < 8 || hidden % 8 != 0 || vocab < 1) return DLLM_ERR_INVALID_ARG;
+    if (rows > 0 && (!h || !w || !logits)) return DLLM_ERR_INVALID_ARG;
+    if ((uintptr_t)w % 16 != 0) return DLLM_ERR_INVALID_ARG;
+    if (w_dtype != DLLM_DTYPE_F32 && w_dtype != DLLM_DTYPE_BF16 && w_dtype != DLLM_DTYPE_F16)
+        return DLLM_ERR_INVALID_ARG;
+    if (lmh_max_rows(hidden) < 1) return DLLM_ERR_UNSUPPORTED;
+    if (rows == 0) return DLLM_OK;
+    float *scratch = (float *)internal_workspace(stream, (size_t)rows * hidden * sizeof(float));
+    if (!scratch) {
+        set_error("lm-head scratch", cudaErrorMemoryAllocation);
+        return DLLM_ERR_OOM;
+    }
+    const dllm_status st = launch_lmhead(rows, hidden, vocab, h, norm_w, eps, add_one, w, w_dtype, softcap, logits,
+                                         scratch, (cudaStream_t)stream);
+    if (st == DLLM_ERR_CUDA) set_error("lm-head kernel launch", cudaGetLastError());
+    return st;
+}
+
+// ----------------------------------------------------------------------------------------
 // vocabulary-sharded sampling (no counterpart in the reference, whose sampler sees whole rows)
 
 extern "C" dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *d, int64_t vocab_offset, int64_t vocab_total,

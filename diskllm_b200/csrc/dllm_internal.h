@@ -91,6 +91,10 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
 dllm_status set_debug_counters(unsigned long long *dev_counters);
 dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
 size_t shard_part_bytes(int rows, int vlocal, int k);
+int lmh_max_rows(int hidden);
+dllm_status launch_lmhead(int rows, int hidden, int vocab, const float *h, const float *norm_w, float eps, int add_one,
+                          const void *w, int w_dtype, float softcap, float *logits, float *scratch,
+                          cudaStream_t stream);
 dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int64_t vtotal, int k, float *cand_val,
                                     int32_t *cand_id, void *part, cudaStream_t stream);
 dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, const int32_t *ids,

@@ -44,6 +44,7 @@ typedef enum {
 enum {
     DLLM_DTYPE_F32 = 0,
     DLLM_DTYPE_BF16 = 1,
+    DLLM_DTYPE_F16 = 2,   /* output weights of dllm_cuda_lmhead_logits only */
 };
 
 /* mode flags */
@@ -167,6 +168,17 @@ DLLM_API dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const 
                                             const int32_t *cand_id, const dllm_sampler_params *params,
                                             const dllm_sampler_params *row_params,
                                             const float *uniforms, int32_t *token, void *stream);
+
+/* The step before the sampler (src/core/context.c:854-876): the final RMSNorm of `rows` hidden
+ * states h [rows][hidden] (fp32; src/rmsnorm.c:4-27, norm_w may be NULL, add_one for Gemma's
+ * (w + 1)), the logits matvec against unquantised output weights w [vocab][hidden]
+ * (DLLM_DTYPE_F32 / BF16 / F16, 16-byte aligned; src/matvec.c:251-366, a double-precision dot
+ * product per row rounded once), and, when softcap > 0, logit = softcap * tanhf(logit / softcap).
+ * Writes logits [rows][vocab] (fp32) ready for dllm_cuda_sample_batch.  hidden must be a multiple
+ * of 8.  All pointers are device memory. */
+DLLM_API dllm_status dllm_cuda_lmhead_logits(int rows, int hidden, int vocab, const float *h, const float *norm_w,
+                                             float eps, int add_one, const void *w, int w_dtype, float softcap,
+                                             float *logits, void *stream);
 
 /* Decode-loop glue (no counterpart in the reference, whose caller appends to its seen-token
  * array on the host): appends token[0] (device) to one sequence's device history

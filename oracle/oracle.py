@@ -270,3 +270,58 @@ def reference_cdf(logits_row, params, mask_row=None, hist_row=None, n_boundaries
         cur_bits = z
         cur_id = draw(z)
     return np.array(ids, dtype=np.int64), np.array(cdf, dtype=np.float64)
+
+
+# ---- LM-head tail (the step before the sampler) ----------------------------------------------
+
+RMSNORM_SO = os.path.join(HERE, "_ref", "librmsnorm_asbuilt.so")
+
+
+def rmsnorm_restated(x: np.ndarray, w, eps: float, add_one: bool) -> np.ndarray:
+    """src/rmsnorm.c:4-27 for each row: sum of squares in double, mean, + eps,
+    scale = (float)(1 / sqrt(.)), then in fp32 the products as the reference compiles them at
+    -O3 -ffast-math (measured against oracle/_ref/librmsnorm_asbuilt.so): x * scale without a
+    weight, (x * scale) * (w + 1) with add_one, and (x * w) * scale with a plain weight (the
+    compiler reassociates the source's x * scale * w)."""
+    x = np.asarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    for r in range(x.shape[0]):
+        ss = float(np.sum(x[r].astype(np.float64) ** 2)) / x.shape[1] + float(np.float32(eps))
+        scale = np.float32(1.0 / np.sqrt(ss))
+        if w is None:
+            v = x[r] * scale
+        elif add_one:
+            ww = (np.asarray(w, dtype=np.float32) + np.float32(1.0)).astype(np.float32)
+            v = (x[r] * scale).astype(np.float32) * ww
+        else:
+            v = (x[r] * np.asarray(w, dtype=np.float32)).astype(np.float32) * scale
+        out[r] = v.astype(np.float32)
+    return out
+
+
+def rmsnorm_reference(x: np.ndarray, w, eps: float, add_one: bool) -> np.ndarray:
+    """The reference's own rmsnorm_ext (oracle/_ref/librmsnorm_asbuilt.so) on each row."""
+    lib = _lib(RMSNORM_SO)
+    lib.rmsnorm_ext.restype = None
+    lib.rmsnorm_ext.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_float, C.c_int]
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    ww = None if w is None else np.ascontiguousarray(w, dtype=np.float32)
+    for r in range(x.shape[0]):
+        lib.rmsnorm_ext(out[r].ctypes.data, x[r].ctypes.data, None if ww is None else ww.ctypes.data,
+                        x.shape[1], float(eps), int(add_one))
+    return out
+
+
+def lmhead_restated(h: np.ndarray, w_f32: np.ndarray, norm_w=None, eps=1e-6, add_one=False,
+                    softcap=0.0) -> np.ndarray:
+    """src/core/context.c:854-876 for unquantised output weights: rmsnorm_ext, then per output
+    row the double-precision dot product of src/matvec.c:251-366 (products of the fp32-upcast
+    weights and inputs, summed in double, rounded to float once), then the softcap
+    cap * tanhf(x / cap).  w_f32 holds the weights upcast exactly to fp32."""
+    hn = rmsnorm_restated(h, norm_w, eps, add_one).astype(np.float64)
+    out = (hn @ np.asarray(w_f32, dtype=np.float64).T).astype(np.float32)
+    if softcap > 0:
+        cap = np.float32(softcap)
+        out = (cap * np.tanh((out / cap).astype(np.float32)).astype(np.float32)).astype(np.float32)
+    return out
