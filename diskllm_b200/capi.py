@@ -23,6 +23,7 @@ DTYPE_F32 = 0
 DTYPE_BF16 = 1
 MODE_TOPP_SORTED = 0x1
 MODE_PEN_TRUE_DIV = 0x2
+MODE_MINP_RELATIVE = 0x4
 ROW_ERR_HIST_TABLE = 1
 ROW_ERR_NONFINITE = 2
 ROW_ERR_TOPK_LARGE = 4

@@ -133,7 +133,9 @@ static dllm_status validate(const dllm_batch_desc *d) {
     if (d->pen_logits && d->pen_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
     if (d->topk_ids && d->topk_stride < (d->row_params ? d->topk_max : d->params.top_k))
         return DLLM_ERR_INVALID_ARG;
-    if (d->flags & ~(unsigned)DLLM_MODE_PEN_TRUE_DIV) return DLLM_ERR_UNSUPPORTED;
+    if (d->flags & ~(unsigned)(DLLM_MODE_PEN_TRUE_DIV | DLLM_MODE_TOPP_SORTED | DLLM_MODE_MINP_RELATIVE))
+        return DLLM_ERR_UNSUPPORTED;
+    if ((d->flags & DLLM_MODE_TOPP_SORTED) && d->vocab > (1 << 21)) return DLLM_ERR_UNSUPPORTED;
     if (d->workspace && ((uintptr_t)d->workspace % 256 != 0)) return DLLM_ERR_INVALID_ARG;
     return DLLM_OK;
 }
@@ -238,27 +240,58 @@ static int topk_bound(const dllm_batch_desc *d) {
     return topk_max;
 }
 
+// Which kernels a descriptor runs: the fused sampler, the sorted-nucleus passes, or both (per-row
+// parameters under the sorted flag: the fused kernel samples every row, then the sorted passes
+// resample the rows with top-k off and temperature > 0).
+static void plan(const dllm_batch_desc *d, bool *fused, bool *sorted) {
+    *sorted = (d->flags & DLLM_MODE_TOPP_SORTED) != 0;
+    *fused = true;
+    if (*sorted && !d->row_params) {
+        const dllm_sampler_params &p = d->params;
+        const bool eligible = p.temperature > 0.0f && !(p.top_k > 0 && p.top_k < d->vocab);
+        *fused = !eligible;
+        *sorted = eligible;
+    }
+}
+
+static size_t sorted_offset(size_t fused_bytes) { return (fused_bytes + 255) & ~(size_t)255; }
+
 extern "C" size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *d) {
     if (validate(d) != DLLM_OK || d->rows == 0) return 0;
-    const int tk = topk_bound(d);
-    if (tk > KMAX) return 0;
-    LaunchCfg cfg;
-    if (get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, tk, &cfg) != DLLM_OK) return 0;
-    return (size_t)d->rows * row_ws_bytes(nrec_for(cfg), cfg.SUB);
+    bool fused, sorted;
+    plan(d, &fused, &sorted);
+    size_t bytes = 0;
+    if (fused) {
+        const int tk = topk_bound(d);
+        if (tk > KMAX) return 0;
+        LaunchCfg cfg;
+        if (get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, tk, &cfg) != DLLM_OK) return 0;
+        bytes = (size_t)d->rows * row_ws_bytes(nrec_for(cfg), cfg.SUB);
+    }
+    if (sorted) bytes = sorted_offset(bytes) + sorted_ws_bytes(d->rows, d->vocab);
+    return bytes;
 }
 
 extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *stream) {
     dllm_status st = validate(d);
     if (st != DLLM_OK) return st;
     if (d->rows == 0) return DLLM_OK;
+    bool fused, sorted;
+    plan(d, &fused, &sorted);
     const int topk_max = topk_bound(d);
-    if (topk_max > KMAX) return DLLM_ERR_UNSUPPORTED;
+    if (fused && topk_max > KMAX) return DLLM_ERR_UNSUPPORTED;
 
-    LaunchCfg cfg;
-    st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
-    if (st != DLLM_OK) return st;
-    const int nrec = nrec_for(cfg);
-    const size_t ws_need = (size_t)d->rows * row_ws_bytes(nrec, cfg.SUB);
+    LaunchCfg cfg = {};
+    int nrec = 0;
+    size_t ws_need = 0;
+    if (fused) {
+        st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
+        if (st != DLLM_OK) return st;
+        nrec = nrec_for(cfg);
+        ws_need = (size_t)d->rows * row_ws_bytes(nrec, cfg.SUB);
+    }
+    const size_t fused_bytes = ws_need;
+    if (sorted) ws_need = sorted_offset(fused_bytes) + sorted_ws_bytes(d->rows, d->vocab);
     void *ws = d->workspace;
     if (ws) {
         if (d->workspace_bytes < ws_need) return DLLM_ERR_INVALID_ARG;
@@ -304,8 +337,17 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
     a.status = d->status;
     a.topk_ids = d->topk_ids;
     a.topk_stride = d->topk_stride;
-    st = launch_sample(a, cfg, (cudaStream_t)stream);
-    if (st != DLLM_OK) set_error("sample kernel launch", cudaGetLastError());
+    if (fused) {
+        st = launch_sample(a, cfg, (cudaStream_t)stream);
+        if (st != DLLM_OK) {
+            set_error("sample kernel launch", cudaGetLastError());
+            return st;
+        }
+    }
+    if (sorted) {
+        st = launch_sorted(d, fused, (unsigned char *)ws + sorted_offset(fused_bytes), (cudaStream_t)stream);
+        if (st == DLLM_ERR_CUDA) set_error("sorted-nucleus kernel launch", cudaGetLastError());
+    }
     return st;
 }
 

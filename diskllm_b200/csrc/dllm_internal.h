@@ -91,6 +91,8 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
 dllm_status set_debug_counters(unsigned long long *dev_counters);
 dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
 size_t shard_part_bytes(int rows, int vlocal, int k);
+size_t sorted_ws_bytes(int rows, int vocab);
+dllm_status launch_sorted(const dllm_batch_desc *d, bool after_fused, void *ws, cudaStream_t stream);
 int lmh_max_rows(int hidden);
 dllm_status launch_lmhead(int rows, int hidden, int vocab, const float *h, const float *norm_w, float eps, int add_one,
                           const void *w, int w_dtype, float softcap, float *logits, float *scratch,

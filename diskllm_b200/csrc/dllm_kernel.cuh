@@ -657,7 +657,7 @@ __device__ double warp_sum_list(const float *v, int k) {
 }
 
 __device__ int sample_sorted_list(float *t, int *id, int k, const dllm_sampler_params &p, float r,
-                                  float *probs_row) {
+                                  float *probs_row, bool minp_relative) {
     const int lane = threadIdx.x & 31;
     const float mv = t[0];
     for (int i = lane; i < k; i += 32) t[i] = expf(__fsub_rn(t[i], mv));
@@ -668,13 +668,14 @@ __device__ int sample_sorted_list(float *t, int *id, int k, const dllm_sampler_p
     __syncwarp();
     int kk = k;
     if (p.min_p > 0.0f) {
-        // stable compaction of the entries with p >= min_p
+        // stable compaction of the entries with p >= min_p (relative: min_p * p_max, p_max = t[0])
+        const float thr = minp_relative ? __fmul_rn(p.min_p, t[0]) : p.min_p;
         int nk = 0;
         for (int base = 0; base < kk; base += 32) {
             const int i = base + lane;
             const float v = i < kk ? t[i] : 0.0f;
             const int vid = i < kk ? id[i] : 0;
-            const bool keep = i < kk && v >= p.min_p;
+            const bool keep = i < kk && v >= thr;
             const unsigned m = __ballot_sync(0xffffffffu, keep);
             __syncwarp();
             if (keep) {
@@ -1522,7 +1523,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     for (int i = tid; i < k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = il[i] + a.vocab_offset;
                 if (wid == 0) {
                     float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride : nullptr;
-                    token = sample_sorted_list(tl, il, k, p, r, pr);
+                    token = sample_sorted_list(tl, il, k, p, r, pr, (a.flags & DLLM_MODE_MINP_RELATIVE) != 0);
                 }
             }
             }
@@ -1577,7 +1578,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
 
             Chain ch;
             ch.inv_sum = __double2float_rn(1.0 / sum);
-            ch.min_p = p.min_p;
+            // relative min-p: the largest probability is 1 * inv_sum (its exponential is exp(0))
+            ch.min_p = (a.flags & DLLM_MODE_MINP_RELATIVE) ? __fmul_rn(p.min_p, ch.inv_sum) : p.min_p;
             ch.minp = p.min_p > 0.0f;
             ch.nokept = 0;
             ch.inv_s2 = 1.0f;

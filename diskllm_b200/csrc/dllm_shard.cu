@@ -19,14 +19,13 @@
 // compare against the whole-row reference to catch any difference.
 #include <cuda_runtime.h>
 
-#include "dllm_kernel.cuh"
+#include "dllm_chunk.cuh"
 
 namespace dllm {
 namespace {
 
 constexpr int SH_T = 256;        // threads per CTA
 constexpr int SH_CHUNK = 8192;   // columns per CTA (keys staged in shared memory)
-constexpr int SH_HTAB = 512;     // history hash entries per chunk (power of two)
 constexpr int SH_KMAX = 256;     // largest k per shard
 
 struct ShardArgs {
@@ -218,8 +217,9 @@ __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int 
 template <int DT>
 __global__ void __launch_bounds__(SH_T) shard_chunk_kernel(const ShardArgs a) {
     extern __shared__ __align__(16) uint32_t keys[];  // SH_CHUNK keys
-    __shared__ int hkeys[SH_HTAB];
-    __shared__ int hcnt[SH_HTAB];
+    __shared__ int hkeys[CH_HTAB];
+    __shared__ int hcnt[CH_HTAB];
+    __shared__ uint32_t penbits[SH_CHUNK / 32];
     __shared__ SelScratch sel;
     __shared__ uint32_t okey_s[SH_KMAX];
     __shared__ int oid_s[SH_KMAX];
@@ -228,91 +228,16 @@ __global__ void __launch_bounds__(SH_T) shard_chunk_kernel(const ShardArgs a) {
     const int c0 = ch * SH_CHUNK, n = min(SH_CHUNK, a.vlocal - c0);
     const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
 
-    for (int i = tid; i < SH_HTAB; i += NT) {
-        hkeys[i] = -1;
-        hcnt[i] = 0;
-    }
     if (tid == 0) s_flags = 0;
-    // raw logits of the chunk, masked (grammar.c:275-308), as order-preserving keys
+    // mask (grammar.c:275-308) and history penalties (sampler.c:21-52), as order-preserving keys
+    ChunkPen cp{hkeys, hcnt, penbits, &s_flags, pen_active(a.hist_ids, a.hist_off, p)};
+    const HistPre hp = hist_prefetch(a.hist_ids, a.hist_off, row, cp.active);
+    chunk_pen_build(cp, a.hist_ids, hp, a.voff, a.vtotal, c0, n, SH_CHUNK / 32);
     const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
-    if (DT == DLLM_DTYPE_BF16) {
-        const unsigned short *src = (const unsigned short *)a.logits + (int64_t)row * a.row_stride + c0;
-        const bool vec = ((uintptr_t)src & 15u) == 0;
-        const int n8 = vec ? (n & ~7) : 0;
-        for (int i = 8 * tid; i < n8; i += 8 * NT) {
-            const uint4 raw = *reinterpret_cast<const uint4 *>(src + i);
-            const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
-            const uint32_t mw = mrow ? mrow[(c0 + i) >> 5] >> ((c0 + i) & 31) : 0xffu;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const uint32_t hb = (j & 1) ? (w[j >> 1] & 0xffff0000u) : (w[j >> 1] << 16);
-                keys[i + j] = okey(((mw >> j) & 1u) ? bitsf(hb) : -INFINITY);
-            }
-        }
-        for (int i = n8 + tid; i < n; i += NT) {
-            const int li = c0 + i;
-            const float v = bitsf((uint32_t)src[i] << 16);
-            keys[i] = okey(!mrow || ((mrow[li >> 5] >> (li & 31)) & 1u) ? v : -INFINITY);
-        }
-    } else {
-        const float *src = (const float *)a.logits + (int64_t)row * a.row_stride + c0;
-        const bool vec = ((uintptr_t)src & 15u) == 0;
-        const int n4 = vec ? (n & ~3) : 0;
-        for (int i = 4 * tid; i < n4; i += 4 * NT) {
-            const float4 x = *reinterpret_cast<const float4 *>(src + i);
-            const uint32_t mw = mrow ? mrow[(c0 + i) >> 5] >> ((c0 + i) & 31) : 0xfu;
-            keys[i] = okey((mw & 1u) ? x.x : -INFINITY);
-            keys[i + 1] = okey((mw & 2u) ? x.y : -INFINITY);
-            keys[i + 2] = okey((mw & 4u) ? x.z : -INFINITY);
-            keys[i + 3] = okey((mw & 8u) ? x.w : -INFINITY);
-        }
-        for (int i = n4 + tid; i < n; i += NT) {
-            const int li = c0 + i;
-            keys[i] = okey(!mrow || ((mrow[li >> 5] >> (li & 31)) & 1u) ? src[i] : -INFINITY);
-        }
-    }
-    __syncthreads();
-    // history penalties of this chunk's ids (sampler.c:35-52 presence once, 21-33 repetition per
-    // occurrence): occurrence counts in a hash table, then each counted entry's key rewritten
-    const bool use_hist = a.hist_ids && a.hist_off && (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
-    if (use_hist) {
-        const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
-        for (int64_t j = h0 + tid; j < h1; j += NT) {
-            const int id = a.hist_ids[j];
-            if (id < 0 || id >= a.vtotal) continue;
-            const int64_t li = (int64_t)id - a.voff - c0;
-            if (li < 0 || li >= n) continue;
-            uint32_t h = hash_id((uint32_t)li) & (SH_HTAB - 1);
-            bool placed = false;
-            for (int probe = 0; probe < SH_HTAB; probe++) {
-                const int old = atomicCAS(&hkeys[h], -1, (int)li);
-                if (old == -1 || old == (int)li) {
-                    atomicAdd(&hcnt[h], 1);
-                    placed = true;
-                    break;
-                }
-                h = (h + 1u) & (SH_HTAB - 1);
-            }
-            if (!placed) atomicOr(&s_flags, ROW_ERR_HIST_TABLE);
-        }
-        __syncthreads();
-        const float inv_rep = __fdiv_rn(1.0f, p.repetition);
-        const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
-        for (int sl = tid; sl < SH_HTAB; sl += NT) {
-            const int li = hkeys[sl];
-            if (li < 0) continue;
-            const int c = hcnt[sl];
-            float v = okey_inv(keys[li]);
-            if (p.presence != 0.0f) v = __fsub_rn(v, p.presence);
-            if (p.frequency != 0.0f) v = __fsub_rn(v, __fmul_rn(__int2float_rn(c), p.frequency));
-            if (p.repetition > 1.0f)
-                for (int r = 0; r < c; r++) {
-                    if (v < 0.0f) v = __fmul_rn(v, p.repetition);
-                    else v = true_div ? __fdiv_rn(v, p.repetition) : __fmul_rn(v, inv_rep);
-                }
-            keys[li] = okey(v);
-        }
-    }
+    const size_t esz = DT == DLLM_DTYPE_BF16 ? 2 : 4;
+    const unsigned char *src = (const unsigned char *)a.logits + ((int64_t)row * a.row_stride + c0) * esz;
+    const bool vec = ((uintptr_t)src & 15u) == 0;
+    chunk_visit<DT>(src, vec, mrow, c0, n, cp, p, a.flags, [&](int li, float v) { keys[li] = okey(v); });
     __syncthreads();
     block_select(keys, nullptr, c0, n, a.k, sel, okey_s, oid_s);
     if (a.nchunks == 1) {
@@ -429,7 +354,7 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
     }
     __syncthreads();
     if (wid == 0) {
-        const int tok = sample_sorted_list(tl, il, k, p, a.uniforms[row], nullptr);
+        const int tok = sample_sorted_list(tl, il, k, p, a.uniforms[row], nullptr, false);
         if (lane == 0) a.token[row] = tok;
     }
 }

@@ -48,11 +48,19 @@ enum {
 };
 
 /* mode flags */
-#define DLLM_MODE_TOPP_SORTED   0x1u  /* reserved: sorted-nucleus top-p when top-k is off
-                                         (not yet implemented; rejected) */
+#define DLLM_MODE_TOPP_SORTED   0x1u  /* sorted-nucleus mode for rows with top-k off and
+                                         temperature > 0: entries ordered by (t desc, id asc),
+                                         masses rint(expf(t) * 2^42) summed exactly, min-p the
+                                         sorted prefix above the threshold, top-p the shortest
+                                         prefix reaching top_p of the kept mass, the draw the
+                                         first entry whose prefix mass exceeds r * (nucleus
+                                         mass).  Not the reference's behaviour (its top-p keeps
+                                         an index-order prefix when top-k is off); vocab <= 2^21 */
 #define DLLM_MODE_PEN_TRUE_DIV  0x2u  /* positive logits divided by the repetition penalty
                                          (IEEE) instead of multiplied by 1/penalty, which is
                                          what the reference's -ffast-math build computes */
+#define DLLM_MODE_MINP_RELATIVE 0x4u  /* min-p keeps p >= min_p * (largest p) instead of the
+                                         reference's absolute p >= min_p */
 
 /* Sampling parameters of one row.  Fields mirror DiskLLM's sampler_config
  * (include/sampler.h:10-16) plus the penalties of diskllm_sampler_params

@@ -28,6 +28,12 @@
  *  - top-p: src/sampler.c:204-222 (prefix in the CURRENT order until (float)cumul >= p;
  *    with top-k off that order is token-id order).
  *  - draw: src/sampler.c:224-233 (float running sum, first r < cumul, else the last).
+ *
+ * Two modes that are not the reference's (flags; both off by default):
+ *  - DLLM_ORACLE_MINP_RELATIVE: min-p keeps p >= min_p * p_max, p_max the largest
+ *    probability (fp32 product), instead of the reference's absolute p >= min_p.
+ *  - DLLM_ORACLE_TOPP_SORTED (top-k off, temperature > 0): the sorted-nucleus sampler with
+ *    exact cumulative sums -- see sample_row_sorted.
  */
 #define _GNU_SOURCE
 #include "dllm_oracle.h"
@@ -109,6 +115,7 @@ typedef struct {
     float    *w;      /* penalised row */
     entry_t  *buf;    /* candidate list */
     int32_t  *cnt;    /* per-id occurrence counts (zero between rows) */
+    uint64_t *mass;   /* sorted-nucleus mode: fixed-point mass per sorted entry */
     int       vocab;
 } scratch_t;
 
@@ -232,6 +239,87 @@ static void penalise_row(const dllm_oracle_batch *b, int row, const dllm_oracle_
     }
 }
 
+/*
+ * Sorted-nucleus mode.  The reference's top-p keeps an index-order prefix when top-k is off
+ * (src/sampler.c:165-170 sort only under top-k) and draws with a float running sum that drifts
+ * by up to ~1e-5 over 256000 entries.  This mode is the corrected sampler, defined exactly:
+ *   1. t_i = (x_i - max) * (1.0f / temp) as the reference; order by (t desc, id asc) (the order
+ *      partial_sort_top_k gives, src/sampler.c:109-134);
+ *   2. mass E_i = rint(expf(t_i) * 2^42), an integer (exact for expf >= 2^-19), so every sum
+ *      below is exact;
+ *   3. min-p (optional): inv_sum = (float)(1 / (sum E * 2^-42)); keep the sorted prefix with
+ *      (float)(expf(t_i) * inv_sum) >= threshold (absolute min_p, or min_p * inv_sum with
+ *      DLLM_ORACLE_MINP_RELATIVE); none kept -> keep all (src/sampler.c:188-196);
+ *      S2 = mass of the kept entries;
+ *   4. top-p (top_p < 1): T = max(ceil((double)top_p * (double)S2), 1) - 1; the cut is the
+ *      first entry whose inclusive prefix mass exceeds T; S3 = that prefix mass (else S3 = S2);
+ *   5. draw: T = floor((double)r * (double)S3); the token is the first entry whose inclusive
+ *      prefix mass exceeds T.
+ * kept_prob / kept_cdf report E_i / S3 and prefix / S3 (rounded to float).
+ */
+static int32_t sample_row_sorted(const dllm_oracle_batch *b, int row, const dllm_oracle_params *p,
+                                 scratch_t *s, float m)
+{
+    const int V = b->vocab;
+    entry_t *buf = s->buf;
+    const float inv_temp = 1.0f / p->temperature;
+    for (int i = 0; i < V; i++) {
+        buf[i].idx = i;
+        buf[i].val = (s->w[i] - m) * inv_temp;
+    }
+    select_top_k(buf, V, V);
+    uint64_t *E = s->mass;
+    uint64_t sall = 0;
+    int npos = 0;
+    for (int i = 0; i < V; i++) {
+        const float e = expf(buf[i].val);
+        E[i] = (uint64_t)rint((double)e * 4398046511104.0);
+        sall += E[i];
+        if (E[i]) npos = i + 1;
+    }
+    int nk = npos;  /* entries past npos have no mass and are never kept */
+    if (p->min_p > 0.0f) {
+        const float inv_sum = (float)(1.0 / ((double)sall * 0x1p-42));
+        const float thr = (b->flags & DLLM_ORACLE_MINP_RELATIVE) ? p->min_p * inv_sum : p->min_p;
+        int n = 0;
+        while (n < npos && expf(buf[n].val) * inv_sum >= thr) n++;
+        if (n > 0) nk = n;
+    }
+    uint64_t s2 = 0;
+    for (int i = 0; i < nk; i++) s2 += E[i];
+    int kc = nk;
+    uint64_t s3 = s2;
+    if (p->top_p < 1.0f) {
+        double x = ceil((double)p->top_p * (double)s2);
+        const uint64_t T = (x < 1.0 ? 1ull : (uint64_t)x) - 1ull;
+        uint64_t cum = 0;
+        for (int i = 0; i < nk; i++) {
+            cum += E[i];
+            if (cum > T) { kc = i + 1; break; }
+        }
+        s3 = 0;
+        for (int i = 0; i < kc; i++) s3 += E[i];
+    }
+    if (b->kept_n) b->kept_n[row] = kc;
+    if (b->kept_idx || b->kept_prob || b->kept_cdf) {
+        uint64_t cum = 0;
+        for (int i = 0; i < kc && i < b->kept_cap; i++) {
+            size_t o = (size_t)row * b->kept_cap + i;
+            cum += E[i];
+            if (b->kept_idx) b->kept_idx[o] = buf[i].idx;
+            if (b->kept_prob) b->kept_prob[o] = (float)((double)E[i] / (double)s3);
+            if (b->kept_cdf) b->kept_cdf[o] = (float)((double)cum / (double)s3);
+        }
+    }
+    const uint64_t T = (uint64_t)floor((double)b->uniforms[row] * (double)s3);
+    uint64_t cum = 0;
+    for (int i = 0; i < kc; i++) {
+        cum += E[i];
+        if (cum > T) return buf[i].idx;
+    }
+    return buf[kc - 1].idx;
+}
+
 static int32_t sample_row(const dllm_oracle_batch *b, int row, const dllm_oracle_params *p,
                           scratch_t *s)
 {
@@ -259,8 +347,8 @@ static int32_t sample_row(const dllm_oracle_batch *b, int row, const dllm_oracle
     if (p->top_k > 0 && p->top_k < V) {
         k = p->top_k;
         select_top_k(buf, V, k);
-    } else if (b->flags & DLLM_ORACLE_TOPP_SORTED) {
-        select_top_k(buf, V, V);
+    } else if ((b->flags & DLLM_ORACLE_TOPP_SORTED) && m > -INFINITY && m < INFINITY) {
+        return sample_row_sorted(b, row, p, s, m);
     }
     if (b->topk_idx) {
         int32_t *o = b->topk_idx + (size_t)row * b->topk_cap;
@@ -276,9 +364,15 @@ static int32_t sample_row(const dllm_oracle_batch *b, int row, const dllm_oracle
     for (int i = 0; i < k; i++) buf[i].val = buf[i].val * inv_sum;
 
     if (p->min_p > 0.0f) {
+        float thr = p->min_p;
+        if (b->flags & DLLM_ORACLE_MINP_RELATIVE) {
+            float pmax = buf[0].val;
+            for (int i = 1; i < k; i++) if (buf[i].val > pmax) pmax = buf[i].val;
+            thr = p->min_p * pmax;
+        }
         int nk = 0;
         for (int i = 0; i < k; i++)
-            if (buf[i].val >= p->min_p) buf[nk++] = buf[i];
+            if (buf[i].val >= thr) buf[nk++] = buf[i];
         if (nk > 0) k = nk;
         const double s2 = sum_entries(buf, k, plain);
         const float inv2 = (float)(1.0 / s2);
@@ -339,7 +433,8 @@ static void *run_rows(void *arg)
     s.w = malloc(sizeof(float) * (size_t)b->vocab);
     s.buf = malloc(sizeof(entry_t) * (size_t)b->vocab);
     s.cnt = calloc((size_t)b->vocab, sizeof(int32_t));
-    if (!s.w || !s.buf || !s.cnt) {
+    s.mass = malloc(sizeof(uint64_t) * (size_t)b->vocab);
+    if (!s.w || !s.buf || !s.cnt || !s.mass) {
         j->err = -2;
     } else {
         for (int row = j->r0; row < j->r1; row++) {
@@ -351,7 +446,7 @@ static void *run_rows(void *arg)
             b->token[row] = sample_row(b, row, p, &s);
         }
     }
-    free(s.w); free(s.buf); free(s.cnt);
+    free(s.w); free(s.buf); free(s.cnt); free(s.mass);
 #if defined(__x86_64__) || defined(__i386__)
     _mm_setcsr(saved);
 #endif

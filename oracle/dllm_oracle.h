@@ -25,9 +25,12 @@ extern "C" {
 #endif
 
 /* mode flags (same bit values as the product's DLLM_MODE_* flags) */
-#define DLLM_ORACLE_TOPP_SORTED   0x1u  /* sort all candidates before top-p when top-k is off */
+#define DLLM_ORACLE_TOPP_SORTED   0x1u  /* sorted-nucleus mode when top-k is off (temperature
+                                           > 0): the corrected definition in dllm_oracle.c */
 #define DLLM_ORACLE_PEN_TRUE_DIV  0x2u  /* positive logits divided by the penalty (strict build)
                                            instead of multiplied by 1/penalty (as-built) */
+#define DLLM_ORACLE_MINP_RELATIVE 0x4u  /* min-p threshold min_p * (largest probability)
+                                           instead of the reference's absolute min_p */
 #define DLLM_ORACLE_PLAIN_MATH    0x100u /* oracle only: scalar expf + sequential sums instead
                                             of the as-built build's libmvec/2-lane numerics */
 

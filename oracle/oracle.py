@@ -26,6 +26,7 @@ REF_ASBUILT_SO = os.path.join(HERE, "_ref", "libref_asbuilt.so")
 REF_STRICT_SO = os.path.join(HERE, "_ref", "libref_strict.so")
 
 TOPP_SORTED = 0x1
+MINP_RELATIVE = 0x4
 PEN_TRUE_DIV = 0x2
 
 

@@ -47,8 +47,12 @@ def test_invalid_arguments_rejected_without_gpu():
     d.dtype = 7
     assert lib.dllm_cuda_sample_batch(C.byref(d), None) == 1
     d.dtype = 0
-    d.flags = capi.MODE_TOPP_SORTED                           # reserved mode
+    d.flags = 0x8                                             # unknown mode bit
     assert lib.dllm_cuda_sample_batch(C.byref(d), None) == 6
+    d.flags = capi.MODE_TOPP_SORTED                           # sorted mode beyond 2^21 ids
+    d.vocab = d.row_stride = (1 << 21) + 1
+    assert lib.dllm_cuda_sample_batch(C.byref(d), None) == 6
+    d.vocab = d.row_stride = 10
     d.flags = 0
     d.rows = 0                                                # empty batch: no launch
     assert lib.dllm_cuda_sample_batch(C.byref(d), None) == 0
