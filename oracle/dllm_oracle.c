@@ -386,6 +386,10 @@ static int32_t sample_row(const dllm_oracle_batch *b, int row, const dllm_oracle
             cum += buf[i].val;
             if ((float)cum >= p->top_p) { nk = i + 1; break; }
         }
+        /* test-only alternatives: the cut one entry earlier / later (a prefix within rounding
+           distance of top_p), used to classify GPU draws at knife-edge cuts */
+        if ((b->flags & DLLM_ORACLE_CUT_EARLIER) && nk > 1) nk--;
+        if ((b->flags & DLLM_ORACLE_CUT_LATER) && nk < k) nk++;
         k = nk;
         const double s3 = sum_entries(buf, k, plain);
         const float inv3 = (float)(1.0 / s3);

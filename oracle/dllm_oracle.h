@@ -31,6 +31,8 @@ extern "C" {
                                            instead of multiplied by 1/penalty (as-built) */
 #define DLLM_ORACLE_MINP_RELATIVE 0x4u  /* min-p threshold min_p * (largest probability)
                                            instead of the reference's absolute min_p */
+#define DLLM_ORACLE_CUT_EARLIER   0x200u /* oracle only: index-order top-p cut one entry earlier */
+#define DLLM_ORACLE_CUT_LATER     0x400u /* oracle only: index-order top-p cut one entry later */
 #define DLLM_ORACLE_PLAIN_MATH    0x100u /* oracle only: scalar expf + sequential sums instead
                                             of the as-built build's libmvec/2-lane numerics */
 

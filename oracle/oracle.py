@@ -28,6 +28,8 @@ REF_STRICT_SO = os.path.join(HERE, "_ref", "libref_strict.so")
 TOPP_SORTED = 0x1
 MINP_RELATIVE = 0x4
 PEN_TRUE_DIV = 0x2
+CUT_EARLIER = 0x200  # oracle only: index-order top-p cut one entry earlier
+CUT_LATER = 0x400    # oracle only: index-order top-p cut one entry later
 
 
 class Params(C.Structure):

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from util import TOL_PROB, csr, dense_probs, ids_match, pack_mask, u24
+from util import TOL_PROB, csr, dense_probs, ids_match, knife_edge_rescue, pack_mask, u24
 
 pytestmark = pytest.mark.gpu
 
@@ -67,6 +67,8 @@ def check(lg, params, u, mask=None, hist=None, flags=0, dtype="f32", check_probs
     assert np.all(status == 0), status
     assert np.array_equal(pen.view(np.uint32), ora.pen_logits.view(np.uint32))
     bad = [i for i in range(rows) if not ids_match(int(tok[i]), ora, u, i)]
+    if dtype == "f32":
+        bad = knife_edge_rescue(bad, tok, lg, params, u, mask=mask, hist=hist, flags=flags)
     assert not bad, f"id mismatch rows {bad[:8]}: gpu {tok[bad[:8]]} oracle {ora.token[bad[:8]]}"
     if params.get("temperature", 1.0) == 0.0:
         return tok, ora
@@ -255,3 +257,15 @@ def test_drop_in_penalties_in_place():
     ora = O.sample_restated(row[None], dict(temperature=0.0, presence=0.25, repetition=1.15),
                             np.zeros(1, np.float32), hist=[seen], want_pen=True)
     assert np.array_equal(a.view(np.uint32), ora.pen_logits[0].view(np.uint32))
+
+
+def test_parity_config4_shape_256_rows():
+    """config 4's shape (vocab 256000, flat N(0, 0.5^2), top-p 0.99, repetition 1.05 over 256
+    uniform ids) on 256 rows: enough rows that about one has a knife-edge top-p cut (accepted
+    only as util.knife_edge_rescue describes)"""
+    rng = np.random.default_rng(44)
+    rows, V = 256, 256000
+    lg = (rng.standard_normal((rows, V)) * 0.5).astype(np.float32)
+    hist = [rng.integers(0, V, 256) for _ in range(rows)]
+    u = u24(rng, rows)
+    check(lg, PARAM_SETS["cfg4"], u, hist=hist, check_probs=False)

@@ -125,3 +125,31 @@ def test_xorshift_stream_matches_reference(have_reference):
         for r in u:
             assert O.reference_seed_for_uniform(float(r)) != 0
         assert np.all((u >= 0) & (u < 1))
+
+
+def test_oracle_cut_shift_flags_and_knife_edge_rescue():
+    """The oracle's test-only cut shifts move the index-order top-p cut by exactly one entry,
+    and the knife-edge rule accepts a draw from the shifted cut only where the prefix at the
+    cut lies within rounding distance of top_p (config 4's shape, seed 44, row 5: its prefix
+    before the cut is 2.5e-8 below the threshold)."""
+    from util import knife_edge_rescue
+
+    rng = np.random.default_rng(44)
+    rows, V = 256, 256000
+    lg = (rng.standard_normal((rows, V)) * 0.5).astype(np.float32)
+    hist = [rng.integers(0, V, 256) for _ in range(rows)]
+    u = u24(rng, rows)
+    p = dict(temperature=1.0, top_p=0.99, repetition=1.05)
+    sel = [5, 6]
+    base = O.sample_restated(lg[sel], p, u[sel], hist=[hist[i] for i in sel], kept_cap=V, topk_cap=1)
+    early = O.sample_restated(lg[sel], p, u[sel], hist=[hist[i] for i in sel], flags=O.CUT_EARLIER, kept_cap=V,
+                              topk_cap=1)
+    late = O.sample_restated(lg[sel], p, u[sel], hist=[hist[i] for i in sel], flags=O.CUT_LATER, kept_cap=V,
+                             topk_cap=1)
+    assert np.array_equal(early.kept_n, base.kept_n - 1)
+    assert np.array_equal(late.kept_n, base.kept_n + 1)
+    assert int(base.token[0]) == 251363 and int(early.token[0]) == 251362
+    tok = np.zeros(rows, np.int32)
+    tok[5] = 251362                      # the draw under the earlier cut: explained
+    tok[6] = int(base.token[1]) + 7      # an arbitrary wrong id: not explained
+    assert knife_edge_rescue([5, 6], tok, lg, p, u, hist=hist) == [6]

@@ -50,3 +50,47 @@ def dense_probs(ora, row, vocab):
     if n:
         out[ora.kept_idx[row, :n]] = ora.kept_prob[row, :n]
     return out
+
+
+TOL_CUT = 5e-7  # a top-p prefix this close to the threshold is a knife-edge cut
+
+
+def knife_edge_rescue(bad, gpu_tok, lg, params, u, mask=None, hist=None, flags=0):
+    """Rows of `bad` whose GPU id is explained by a knife-edge index-order top-p cut.
+
+    The reference cuts where (float)(double prefix of p) first reaches top_p
+    (src/sampler.c:204-222), with p = expf(t) * (float)(1/sum).  The reference's own vector
+    expf is up to 3 ulp from the scalar one, and the GPU's exponential differs from both by a
+    few ulp, so the two sums can round (float)(1/sum) one ulp apart: every prefix then moves by
+    up to ~1.2e-7 relative.  When the prefix at the cut lies that close to the threshold the cut
+    legitimately moves by one entry, which renormalises the nucleus by ~p_cut and shifts the CDF
+    near r ~ top_p by more than the 1e-6 draw tolerance.  A row is rescued only if (a) the
+    prefix at the oracle's cut, or just before it, lies within TOL_CUT of the threshold, and
+    (b) the GPU id is the oracle's draw (with the usual 1e-6 boundary tolerance) for the cut one
+    entry earlier or later.  Returns the rows that stay unexplained."""
+    import oracle as O
+
+    if not bad or params.get("top_p", 1.0) >= 1.0 or 0 < params.get("top_k", 0) < lg.shape[1]:
+        return bad
+    rows = np.asarray(bad)
+    sub = lambda a: None if a is None else a[rows]
+    hsub = None if hist is None else [hist[i] for i in rows]
+    usub = u[rows]
+    base = O.sample_restated(lg[rows], params, usub, mask=sub(mask), hist=hsub, flags=flags, want_pen=True,
+                             kept_cap=lg.shape[1], topk_cap=1)
+    alts = [O.sample_restated(lg[rows], params, usub, mask=sub(mask), hist=hsub, flags=flags | f,
+                              kept_cap=lg.shape[1], topk_cap=1) for f in (O.CUT_EARLIER, O.CUT_LATER)]
+    tp = np.float32(params["top_p"])
+    thr = (float(np.nextafter(tp, np.float32(0))) + float(tp)) / 2.0  # (float)x >= tp  <=>  x >= thr
+    left = []
+    for j, i in enumerate(rows):
+        x = base.pen_logits[j].astype(np.float64)
+        t = ((x - x.max()) * (1.0 / params.get("temperature", 1.0)))
+        e = np.exp(t)
+        pref = np.cumsum(e / e.sum())
+        n = int(base.kept_n[j])
+        near = abs(pref[n - 1] - thr) <= TOL_CUT or (n >= 2 and abs(pref[n - 2] - thr) <= TOL_CUT)
+        ok = near and any(ids_match(int(gpu_tok[i]), a, usub, j) for a in alts)
+        if not ok:
+            left.append(int(i))
+    return left
