@@ -954,15 +954,17 @@ __device__ __forceinline__ void p3_scan(const float *vals, const int (&kb)[4], i
 }
 
 template <bool MINP, int NV4>
-__device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], const int (&lim)[4], const Chain &ch,
-                                        float scale3, float (&g0)[4], float (&g1)[4], float (&qmax)[4]) {
-    const float2 IS2 = make_float2(ch.inv_sum, ch.inv_sum), S32 = make_float2(scale3, scale3);
+__device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], const Chain &ch, const float (&s3q)[4],
+                                        float (&g0)[4], float (&g1)[4], float (&qmax)[4]) {
+    const float2 IS2 = make_float2(ch.inv_sum, ch.inv_sum);
 #pragma unroll 2
     for (int j = 0; j < NV4; j++) {
 #pragma unroll
         for (int q = 0; q < 4; q++) {
             const float4 x = *reinterpret_cast<const float4 *>(vals + kb[q] + 4 * j);
-            // w = e * inv_sum (then min-p), q = w * scale3, two elements per multiply
+            // w = e * inv_sum (then min-p), q = w * scale3, two elements per multiply; the scale is
+            // 0 for a sub-chunk wholly past the top-p cut, and the crossing sub-chunk's entries
+            // past the cut were zeroed, so no per-element cut test is needed
             float2 w01 = fmul2(make_float2(x.x, x.y), IS2), w23 = fmul2(make_float2(x.z, x.w), IS2);
             if (MINP) {
                 w01.x = (ch.nokept || w01.x >= ch.min_p) ? __fmul_rn(w01.x, ch.inv_s2) : 0.0f;
@@ -970,16 +972,17 @@ __device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], c
                 w23.x = (ch.nokept || w23.x >= ch.min_p) ? __fmul_rn(w23.x, ch.inv_s2) : 0.0f;
                 w23.y = (ch.nokept || w23.y >= ch.min_p) ? __fmul_rn(w23.y, ch.inv_s2) : 0.0f;
             }
-            const float2 q01 = fmul2(w01, S32), q23 = fmul2(w23, S32);
-            const float q4[4] = {q01.x, q01.y, q23.x, q23.y};
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                float qv = q4[c];
-                qv = (4 * j + c <= lim[q]) ? qv : 0.0f;
-                qmax[q] = fmaxf(qmax[q], qv);
-                g0[q] = __fadd_rn(g0[q], qv);
-                g1[q] = __fadd_rn(g1[q], qv);
-            }
+            const float2 S2 = make_float2(s3q[q], s3q[q]);
+            const float2 q01 = fmul2(w01, S2), q23 = fmul2(w23, S2);
+            if (MINP) qmax[q] = fmaxf(fmaxf(qmax[q], fmaxf(q01.x, q01.y)), fmaxf(q23.x, q23.y));
+            g0[q] = __fadd_rn(g0[q], q01.x);
+            g1[q] = __fadd_rn(g1[q], q01.x);
+            g0[q] = __fadd_rn(g0[q], q01.y);
+            g1[q] = __fadd_rn(g1[q], q01.y);
+            g0[q] = __fadd_rn(g0[q], q23.x);
+            g1[q] = __fadd_rn(g1[q], q23.x);
+            g0[q] = __fadd_rn(g0[q], q23.y);
+            g1[q] = __fadd_rn(g1[q], q23.y);
         }
     }
 }
@@ -1096,6 +1099,29 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         if (cid < a.rows) issue_row_copy(cid, 0);
         if (dbuf && cid + ncl < a.rows) issue_row_copy(cid + ncl, 1);
     }
+    // history of the rows ahead, loaded early so the latency of these dependent global loads
+    // (offsets, then ids) stays off each row's chain: the offsets two rows ahead and the first
+    // HPF ids per thread one row ahead
+    constexpr int HPF = 2;
+    const bool have_hist = a.hist_ids && a.hist_off;
+    int64_t cur_h0 = 0, cur_h1 = 0, nxt_h0 = 0, nxt_h1 = 0;
+    int cur_id[HPF];
+    auto load_ids = [&](int64_t h0, int64_t h1, int (&dst)[HPF]) {
+#pragma unroll
+        for (int k = 0; k < HPF; k++) {
+            const int64_t j = h0 + tid + (int64_t)k * NT;
+            dst[k] = j < h1 ? a.hist_ids[j] : -1;
+        }
+    };
+    if (have_hist && cid < a.rows) {
+        cur_h0 = a.hist_off[cid];
+        cur_h1 = a.hist_off[cid + 1];
+        load_ids(cur_h0, cur_h1, cur_id);
+        if (cid + ncl < a.rows) {
+            nxt_h0 = a.hist_off[cid + ncl];
+            nxt_h1 = a.hist_off[cid + ncl + 1];
+        }
+    }
     int it = 0;
     for (int row = cid; row < a.rows; row += ncl, it++) {
         if (timing) dbg_add(DBG_ROWS, 1);
@@ -1125,10 +1151,11 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         const bool use_hist = a.hist_ids && a.hist_off &&
                               (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
         if (use_hist) {
-            const int64_t h0 = a.hist_off[row], h1 = a.hist_off[row + 1];
+            const int64_t h0 = cur_h0, h1 = cur_h1;
             const uint32_t hm = (uint32_t)a.htab - 1u;
-            for (int64_t j = h0 + tid; j < h1; j += NT) {
-                const int id = a.hist_ids[j];
+            int k = 0;
+            for (int64_t j = h0 + tid; j < h1; j += NT, k++) {
+                const int id = k == 0 ? cur_id[0] : (k == 1 ? cur_id[1] : a.hist_ids[j]);
                 if (id < 0 || id >= a.vocab_total) continue;
                 const int li = id - a.vocab_offset - slice0;
                 if (li < 0 || li >= slen) continue;
@@ -1144,6 +1171,17 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     h = (h + 1u) & hm;
                 }
                 if (!placed) flags |= ROW_ERR_HIST_TABLE;
+            }
+        }
+        if (have_hist && row + ncl < a.rows) {
+            // this row's ids are in the table: load the next row's ids from its offsets (loaded a
+            // row ago) and the offsets of the row after it; they land while this row is sampled
+            cur_h0 = nxt_h0;
+            cur_h1 = nxt_h1;
+            load_ids(cur_h0, cur_h1, cur_id);
+            if (row + 2 * ncl < a.rows) {
+                nxt_h0 = a.hist_off[row + 2 * ncl];
+                nxt_h1 = a.hist_off[row + 2 * ncl + 1];
             }
         }
         if (use_tma) {
@@ -1210,10 +1248,21 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
             } else {
-                for (int i = tid; i < S / 4; i += NT) {
+                // four independent maxima, so four shared loads are in flight per thread
+                float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
+                int i = tid;
+                for (; i + 3 * NT < S / 4; i += 4 * NT) {
+                    const float4 x0 = v4[i], x1 = v4[i + NT], x2 = v4[i + 2 * NT], x3 = v4[i + 3 * NT];
+                    lmax = fmaxf(lmax, fmaxf(fmaxf(x0.x, x0.y), fmaxf(x0.z, x0.w)));
+                    m1 = fmaxf(m1, fmaxf(fmaxf(x1.x, x1.y), fmaxf(x1.z, x1.w)));
+                    m2 = fmaxf(m2, fmaxf(fmaxf(x2.x, x2.y), fmaxf(x2.z, x2.w)));
+                    m3 = fmaxf(m3, fmaxf(fmaxf(x3.x, x3.y), fmaxf(x3.z, x3.w)));
+                }
+                for (; i < S / 4; i += NT) {
                     const float4 x = v4[i];
                     lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
+                lmax = fmaxf(fmaxf(lmax, m1), fmaxf(m2, m3));
             }
         }
         mark(DBG_MAXP);
@@ -1251,6 +1300,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         const bool topk = p.top_k > 0 && p.top_k < a.vocab_total;
         int token = -1;
         bool done = true;   // token decided here (else the walk kernel draws it)
+        bool copy_issued = false;  // the next row's bulk copy was issued early (index-order path)
 
         if (greedy) {
             // ---------------- greedy: first index holding M ----------------------------------
@@ -1840,24 +1890,36 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 for (int q = 0; q < 4; q++) {
                     g0[q] = bitsf(gb[q]);
                     g1[q] = bitsf(gb[q] | 1u);
-                    anyq[q] = false;
                 }
                 float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride + slice0 : nullptr;
-                // elements of sub-chunk q at offset <= lim[q] lie inside the top-p prefix
-                int lim[4];
-                float qmax[4];
+                // elements of sub-chunk q at offset <= lim[q] lie inside the top-p prefix.  A
+                // sub-chunk wholly past the cut gets scale 0; the entries past the cut in the
+                // crossing sub-chunk are zeroed here (the walk forms q = 0 for them by index
+                // anyway).  Without min-p a sub-chunk has a nonzero draw probability iff some
+                // e > 0 in it (sube > 0), up to underflow of e * inv_sum, which leaves an all-zero
+                // run that the walk handles like any other; min-p removes whole sub-chunks, so
+                // there the loop tracks the largest probability instead.
+                const float scale3 = ch.topp ? ch.inv_s3 : 1.0f;
+                float s3q[4], qmax[4];
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
-                    const long long d = (long long)ch.cut_idx - (slice0 + kb[q]);
-                    lim[q] = !ch.topp ? SUBT : (int)(d < 0 ? -1 : (d > SUBT ? SUBT : d));
                     qmax[q] = 0.0f;
+                    const long long d = (long long)ch.cut_idx - (slice0 + kb[q]);
+                    const int lim = !ch.topp ? SUBT : (int)(d < 0 ? -1 : (d > SUBT ? SUBT : d));
+                    s3q[q] = lim < 0 ? 0.0f : scale3;
+                    anyq[q] = lim >= 0 && sube[q] > 0.0;
+                    if (lim >= 0 && lim < SUBT - 1 && kb[q] < S)
+                        for (int k = lim + 1; k < SUBT; k++) vals[kb[q] + k] = 0.0f;
                 }
-                const float scale3 = ch.topp ? ch.inv_s3 : 1.0f;
-                if (ch.minp) p4_scan<true, NV4>(vals, kb, lim, ch, scale3, g0, g1, qmax);
-                else p4_scan<false, NV4>(vals, kb, lim, ch, scale3, g0, g1, qmax);
-                mark(DBG_P4L);
+                __syncwarp();
+                if (ch.minp) {
+                    p4_scan<true, NV4>(vals, kb, ch, s3q, g0, g1, qmax);
 #pragma unroll
-                for (int q = 0; q < 4; q++) anyq[q] = qmax[q] > 0.0f;
+                    for (int q = 0; q < 4; q++) anyq[q] = anyq[q] && qmax[q] > 0.0f;
+                } else {
+                    p4_scan<false, NV4>(vals, kb, ch, s3q, g0, g1, qmax);
+                }
+                mark(DBG_P4L);
                 if (pr) {
 #pragma unroll 1
                     for (int q = 0; q < 4; q++)
@@ -1869,9 +1931,11 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 }
                 WRec *recs = row_recs(a, row);
                 float *stash = row_stash(a, row);
-                // warp records for the four quarters, computed side by side (their shuffle
-                // chains overlap).  Per quarter: the prefix of CLEAN sub-chunks in one binade,
-                // an optional boundary sub-chunk, and the suffix after it (PBS), else MIXED.
+                // warp records for the four quarters.  Per quarter: the prefix of CLEAN
+                // sub-chunks in one binade, an optional boundary sub-chunk, and the suffix after
+                // it (PBS), else MIXED.  The record types, the slot claims and the copies out of
+                // the slice come first; then the next row's bulk copy is issued, and the
+                // composition scans (registers and shuffles only) overlap it.
                 int ctype[4], ce[4];
                 uint32_t c0[4], c1[4];
                 unsigned cleanm[4], nonconf[4];
@@ -1897,7 +1961,6 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     a0[q] = pin ? c0[q] : 0u;
                     a1[q] = pin ? c1[q] : 0u;
                 }
-                compose_scan4(a0, a1);
                 const bool any_nonconf = (nonconf[0] | nonconf[1] | nonconf[2] | nonconf[3]) != 0u;
                 if (!any_nonconf) {
                     // every quarter is one run (or empty): no boundary, no suffix
@@ -1911,20 +1974,20 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     }
                 } else {
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int tj = __shfl_sync(0xffffffffu, ctype[q], jx[q] & 31);
-                    sfrom[q] = !nonconf[q] ? 32 : (tj == REC_MIXED ? jx[q] + 1 : jx[q]);
-                    bchunk[q] = nonconf[q] && tj == REC_MIXED ? jx[q] : -1;
-                    const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom[q] && ctype[q] == REC_CLEAN);
-                    e_s[q] = sclean ? __shfl_sync(0xffffffffu, ce[q], __ffs(sclean) - 1) : 0;
-                    const unsigned sbad = __ballot_sync(
-                        0xffffffffu, lane >= sfrom[q] && (ctype[q] == REC_MIXED || (ctype[q] == REC_CLEAN && ce[q] != e_s[q])));
-                    type[q] = !nonconf[q] ? (cleanm[q] ? REC_CLEAN : REC_IDENT) : (sbad ? REC_MIXED : REC_PBS);
-                    const bool sin = lane >= sfrom[q] && ctype[q] == REC_CLEAN;
-                    b0[q] = sin ? c0[q] : 0u;
-                    b1[q] = sin ? c1[q] : 0u;
-                }
-                compose_scan4(b0, b1);
+                    for (int q = 0; q < 4; q++) {
+                        const int tj = __shfl_sync(0xffffffffu, ctype[q], jx[q] & 31);
+                        sfrom[q] = !nonconf[q] ? 32 : (tj == REC_MIXED ? jx[q] + 1 : jx[q]);
+                        bchunk[q] = nonconf[q] && tj == REC_MIXED ? jx[q] : -1;
+                        const unsigned sclean = __ballot_sync(0xffffffffu, lane >= sfrom[q] && ctype[q] == REC_CLEAN);
+                        e_s[q] = sclean ? __shfl_sync(0xffffffffu, ce[q], __ffs(sclean) - 1) : 0;
+                        const unsigned sbad = __ballot_sync(
+                            0xffffffffu,
+                            lane >= sfrom[q] && (ctype[q] == REC_MIXED || (ctype[q] == REC_CLEAN && ce[q] != e_s[q])));
+                        type[q] = !nonconf[q] ? (cleanm[q] ? REC_CLEAN : REC_IDENT) : (sbad ? REC_MIXED : REC_PBS);
+                        const bool sin = lane >= sfrom[q] && ctype[q] == REC_CLEAN;
+                        b0[q] = sin ? c0[q] : 0u;
+                        b1[q] = sin ? c1[q] : 0u;
+                    }
                 }
                 // stash / wide slots for the four quarters: one claim per warp on CTA 0's counter
                 bool need_st[4], need_wd[4];
@@ -1936,74 +1999,75 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     n_st += need_st[q];
                     n_wd += need_wd[q];
                 }
-                int st_next = 0, wd_next = 0;
+                int nslot[4] = {-1, -1, -1, -1}, wslot[4] = {-1, -1, -1, -1};
                 if (n_st + n_wd) {
                     int base = 0;
                     if (lane == 0) base = atomicAdd(cluster.map_shared_rank(&sh.slots[par], 0), n_st | (n_wd << 16));
                     base = __shfl_sync(0xffffffffu, base, 0);
-                    st_next = base & 0xffff;
-                    wd_next = base >> 16;
+                    int st_next = base & 0xffff, wd_next = base >> 16;
+#pragma unroll 1
+                    for (int q = 0; q < 4; q++) {
+                        const int bchunkq = pick4(bchunk, q);
+                        // boundary sub-chunk exponentials -> a stash slot (when one is free)
+                        if (pick4(need_st, q)) {
+                            const int ns = st_next < STASH_SLOTS ? st_next : -1;
+                            st_next++;
+                            if (ns >= 0) {
+                                const int sb = (q * NT + 32 * wid + bchunkq) * SUBT;
+                                float *qs = stash + ns * STASH_STRIDE;
+                                if (lane == 0) qs[0] = __int_as_float(slice0 + sb);
+                                for (int k = lane; k < SUBT; k += 32) qs[1 + k] = vals[sb + k];  // e; the walk forms q
+                            } else if (timing) {
+                                dbg_add(DBG_STASH_MISS, 1);
+                            }
+                            if (q == 0) nslot[0] = ns;
+                            else if (q == 1) nslot[1] = ns;
+                            else if (q == 2) nslot[2] = ns;
+                            else nslot[3] = ns;
+                        }
+                        // several binade changes in this warp's range, or the draw may land in it:
+                        // keep every exponential so the walk replays them without recomputing
+                        if (pick4(need_wd, q)) {
+                            const int wsl = wd_next < WIDE_SLOTS ? wd_next : -1;
+                            wd_next++;
+                            if (wsl >= 0) {
+                                const int kq = pick4(kb, q);
+                                float *ws = row_wide(a, row) + wsl * wide_stride(SUBT) + lane * SUBT;
+#pragma unroll 1
+                                for (int k = 0; k < SUBT; k += 4)
+                                    *reinterpret_cast<float4 *>(ws + k) = *reinterpret_cast<const float4 *>(vals + kq + k);
+                            } else if (timing) {
+                                dbg_add(DBG_STASH_MISS, 1);
+                            }
+                            if (q == 0) wslot[0] = wsl;
+                            else if (q == 1) wslot[1] = wsl;
+                            else if (q == 2) wslot[2] = wsl;
+                            else wslot[3] = wsl;
+                        }
+                    }
                 }
-                if (n_st + n_wd == 0) {
-                    // nothing to keep: the four records only
-                    if (lane == 31) {
+                // the slice is no longer read: the next row's bulk copy starts here
+                if (use_tma && !dbuf) {
+                    fence_proxy_async();
+                    __syncthreads();
+                    if (tid == 0 && row + ncl < a.rows) issue_row_copy(row + ncl, 0);
+                    copy_issued = true;
+                }
+                compose_scan4(a0, a1);
+                if (any_nonconf) compose_scan4(b0, b1);
+                if (lane == 31) {
 #pragma unroll
-                        for (int q = 0; q < 4; q++) {
-                            WRec wr;
-                            wr.meta = pack_meta(type[q], bchunk[q], sfrom[q], e_first[q], e_s[q]);
-                            wr.p0 = a0[q];
-                            wr.p1 = a1[q];
-                            wr.s0 = b0[q];
-                            wr.s1 = b1[q];
-                            wr.nslot = -1;
-                            wr.wslot = -1;
-                            recs[rank * 4 * NW + q * NW + wid] = wr;
-                        }
-                    }
-                } else
-#pragma unroll 1
-                for (int q = 0; q < 4; q++) {
-                    const int typeq = pick4(type, q), bchunkq = pick4(bchunk, q);
-                    // boundary sub-chunk probabilities -> a stash slot (when one is free)
-                    int nslot = -1, wslot = -1;
-                    if (pick4(need_st, q)) {
-                        nslot = st_next < STASH_SLOTS ? st_next : -1;
-                        st_next++;
-                        if (nslot >= 0) {
-                            const int sb = (q * NT + 32 * wid + bchunkq) * SUBT;
-                            float *qs = stash + nslot * STASH_STRIDE;
-                            if (lane == 0) qs[0] = __int_as_float(slice0 + sb);
-                            for (int k = lane; k < SUBT; k += 32) qs[1 + k] = vals[sb + k];  // e; the walk forms q
-                        } else if (timing) {
-                            dbg_add(DBG_STASH_MISS, 1);
-                        }
-                    }
-                    // several binade changes in this warp's range, or the draw may land in it:
-                    // keep every probability so the walk replays them without recomputing
-                    if (pick4(need_wd, q)) {
-                        wslot = wd_next < WIDE_SLOTS ? wd_next : -1;
-                        wd_next++;
-                        if (wslot >= 0) {
-                            const int kq = pick4(kb, q);
-                            float *ws = row_wide(a, row) + wslot * wide_stride(SUBT) + lane * SUBT;
-#pragma unroll 1
-                            for (int k = 0; k < SUBT; k += 4)  // exponentials; the walk forms q
-                                *reinterpret_cast<float4 *>(ws + k) = *reinterpret_cast<const float4 *>(vals + kq + k);
-                        } else if (timing) {
-                            dbg_add(DBG_STASH_MISS, 1);
-                        }
-                    }
-                    if (lane == 31) {
+                    for (int q = 0; q < 4; q++) {
                         WRec wr;
-                        wr.meta = pack_meta(typeq, bchunkq, pick4(sfrom, q), pick4(e_first, q), pick4(e_s, q));
-                        wr.p0 = pick4(a0, q);
-                        wr.p1 = pick4(a1, q);
-                        wr.s0 = pick4(b0, q);
-                        wr.s1 = pick4(b1, q);
-                        wr.nslot = (int16_t)nslot;
-                        wr.wslot = (int16_t)wslot;
+                        wr.meta = pack_meta(type[q], bchunk[q], sfrom[q], e_first[q], e_s[q]);
+                        wr.p0 = a0[q];
+                        wr.p1 = a1[q];
+                        wr.s0 = b0[q];
+                        wr.s1 = b1[q];
+                        wr.nslot = (int16_t)nslot[q];
+                        wr.wslot = (int16_t)wslot[q];
                         recs[rank * 4 * NW + q * NW + wid] = wr;
-                        if (typeq == REC_PBS && timing) dbg_add(DBG_PBS, 1);
+                        if (type[q] == REC_PBS && timing) dbg_add(DBG_PBS, 1);
                     }
                 }
             }
@@ -2011,7 +2075,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
 
     row_done:
-        if (use_tma && !dbuf) {
+        if (use_tma && !dbuf && !copy_issued) {
             // every read of this row's slice is done: the next row's bulk copy starts now and
             // overlaps the end of this row and the start of the next
             __syncthreads();
