@@ -566,7 +566,9 @@ __device__ __forceinline__ int walk_records(int n, int type, int e, uint32_t n0,
         bool must_hit = false;
         res = walk_step(n, pos, type, e, n0, n1, cb, r, &xj, &must_hit);
         if (res == WALK_EXPAND) {
+            const long long t0 = g_dbg ? clock64() : 0;
             res = expand(xj, cb);
+            if (g_dbg && (threadIdx.x & 31) == 0) dbg_add(DBG_B_EXP, (unsigned long long)(clock64() - t0));
             if (must_hit) {
                 pos = n;
                 if (res < 0) res = -2;
@@ -583,7 +585,7 @@ __device__ __forceinline__ int walk_records(int n, int type, int e, uint32_t n0,
 // as a run record; runs that stay in one binade are composed in parallel, the others are
 // replayed serially by their lane.  `gbase + j` is the index of element j.  Returns the drawn
 // index, -1 (not in this range; cb advanced past it) or -2.
-__device__ __noinline__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float *src) {
+__device__ __noinline__ int replay_elems_impl(int n, int gbase, uint32_t &cb, float r, const float *src) {
     const int lane = threadIdx.x & 31;
     const int s = (n + 31) >> 5;
     const int j0 = lane * s;
@@ -641,6 +643,14 @@ __device__ __noinline__ int replay_elems(int n, int gbase, uint32_t &cb, float r
         if (res != -1) return res;
     }
     return pos < 32 ? -2 : -1;
+}
+
+// replay_elems_impl, with its cycles counted in the diagnostic counters when they are on
+__device__ __forceinline__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float *src) {
+    const long long t0 = g_dbg ? clock64() : 0;
+    const int res = replay_elems_impl(n, gbase, cb, r, src);
+    if (g_dbg && (threadIdx.x & 31) == 0) dbg_add(DBG_B_REPL, (unsigned long long)(clock64() - t0));
+    return res;
 }
 
 // ----------------------------------------------------------------------------------------
