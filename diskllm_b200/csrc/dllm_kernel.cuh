@@ -1000,7 +1000,9 @@ __device__ __forceinline__ void p4_scan(const float *vals, const int (&kb)[4], c
 // ----------------------------------------------------------------------------------------
 // kernel A
 
-template <int DT, int SUBT>
+// IDX: the index-order path only (every row has temperature > 0, top-k off, no min-p; the host
+// checks), so the greedy, top-k and min-p code is compiled out and the hot code is smaller
+template <int DT, int SUBT, bool IDX = false>
 __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a) {
     static_assert(SUBT % 8 == 4 && SUBT <= MAX_SUB, "sub-chunk length");
     constexpr int NV4 = SUBT / 4;   // float4 per sub-chunk
@@ -1306,8 +1308,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             if (to1) rowflags |= ROW_ERR_TIMEOUT;
         }
 
-        const bool greedy = p.temperature == 0.0f;
-        const bool topk = p.top_k > 0 && p.top_k < a.vocab_total;
+        const bool greedy = !IDX && p.temperature == 0.0f;
+        const bool topk = !IDX && p.top_k > 0 && p.top_k < a.vocab_total;
         int token = -1;
         bool done = true;   // token decided here (else the walk kernel draws it)
         bool copy_issued = false;  // the next row's bulk copy was issued early (index-order path)
@@ -1640,7 +1642,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             ch.inv_sum = __double2float_rn(1.0 / sum);
             // relative min-p: the largest probability is 1 * inv_sum (its exponential is exp(0))
             ch.min_p = (a.flags & DLLM_MODE_MINP_RELATIVE) ? __fmul_rn(p.min_p, ch.inv_sum) : p.min_p;
-            ch.minp = p.min_p > 0.0f;
+            ch.minp = !IDX && p.min_p > 0.0f;
             ch.nokept = 0;
             ch.inv_s2 = 1.0f;
             ch.topp = p.top_p < 1.0f;

@@ -12,6 +12,7 @@
 namespace dllm {
 KernelFn DLLM_CAT(kernel_a_f32_, DLLM_SUB)() { return sample_rows_kernel<DLLM_DTYPE_F32, DLLM_SUB>; }
 KernelFn DLLM_CAT(kernel_a_bf16_, DLLM_SUB)() { return sample_rows_kernel<DLLM_DTYPE_BF16, DLLM_SUB>; }
+KernelFn DLLM_CAT(kernel_a_idx_f32_, DLLM_SUB)() { return sample_rows_kernel<DLLM_DTYPE_F32, DLLM_SUB, true>; }
 KernelFn DLLM_CAT(kernel_b_f32_, DLLM_SUB)() { return walk_rows_kernel<DLLM_DTYPE_F32, DLLM_SUB>; }
 KernelFn DLLM_CAT(kernel_b_bf16_, DLLM_SUB)() { return walk_rows_kernel<DLLM_DTYPE_BF16, DLLM_SUB>; }
 }  // namespace dllm

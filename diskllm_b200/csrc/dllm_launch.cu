@@ -14,16 +14,19 @@ static const int kSUBs[] = {4, 12, 20, 28, 36, 44, 52, 60};
 
 // getters per instantiation, defined in dllm_kernel_inst.cu (compiled once per sub-chunk length)
 #define DLLM_DECL(L) KernelFn kernel_a_f32_##L(); KernelFn kernel_a_bf16_##L(); \
-    KernelFn kernel_b_f32_##L(); KernelFn kernel_b_bf16_##L();
+    KernelFn kernel_b_f32_##L(); KernelFn kernel_b_bf16_##L(); KernelFn kernel_a_idx_f32_##L();
 DLLM_DECL(4) DLLM_DECL(12) DLLM_DECL(20) DLLM_DECL(28) DLLM_DECL(36) DLLM_DECL(44) DLLM_DECL(52) DLLM_DECL(60)
 #undef DLLM_DECL
 
-// which = 0: the cluster kernel, 1: the walk kernel
+// which = 0: the cluster kernel, 1: the walk kernel, 2: the cluster kernel's index-order-only
+// variant (fp32)
 static KernelFn kernel_for(int dtype, int SUB, int which = 0) {
     const bool bf = dtype == DLLM_DTYPE_BF16;
+    if (which == 2 && bf) return nullptr;
     switch (SUB) {
-#define DLLM_CASE(L) case L: return which ? (bf ? kernel_b_bf16_##L() : kernel_b_f32_##L()) \
-                                          : (bf ? kernel_a_bf16_##L() : kernel_a_f32_##L());
+#define DLLM_CASE(L) case L: return which == 1 ? (bf ? kernel_b_bf16_##L() : kernel_b_f32_##L()) \
+                                  : which == 2 ? kernel_a_idx_f32_##L() \
+                                               : (bf ? kernel_a_bf16_##L() : kernel_a_f32_##L());
         DLLM_CASE(4) DLLM_CASE(12) DLLM_CASE(20) DLLM_CASE(28) DLLM_CASE(36) DLLM_CASE(44) DLLM_CASE(52) DLLM_CASE(60)
 #undef DLLM_CASE
         default: return nullptr;
@@ -172,6 +175,16 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     if (a.rows == 0) return DLLM_OK;
     KernelFn fn = kernel_for(a.dtype, cfg.SUB);
     KernelFn fnb = kernel_for(a.dtype, cfg.SUB, 1);
+    // every row on the index-order path (broadcast parameters: temperature > 0, top-k off, no
+    // min-p): the variant without the other paths' code
+    const dllm_sampler_params &bp = a.bparams;
+    const bool idx_only = !a.rparams && a.dtype == DLLM_DTYPE_F32 && bp.temperature > 0.0f &&
+                          !(bp.top_k > 0 && bp.top_k < a.vocab_total) && !(bp.min_p > 0.0f) &&
+                          !getenv("DLLM_NO_IDX_VARIANT");
+    if (idx_only) {
+        KernelFn fi = kernel_for(a.dtype, cfg.SUB, 2);
+        if (fi) fn = fi;
+    }
     if (!fn || !fnb) return DLLM_ERR_UNSUPPORTED;
     cudaError_t e = set_attrs(fn, cfg.smem);
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
