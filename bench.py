@@ -522,7 +522,7 @@ def run_cfg5(args, rank, world, dev):
                      "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
                      "traffic": None, "algorithmic_bytes_per_gpu_step": bytes_per_gpu,
-                     "kernel": "shard_topk_kernel + all-gather + merge_sample_kernel (whole step)"},
+                     "kernel": "shard_stream_kernel + all-gather + merge_sample_kernel (whole step)"},
         "e2e": {"value": CFG5_ROWS / (ms_e2e / e2e_steps / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": h_x.numel() * 2, "d2h_bytes_per_step": CFG5_ROWS * 4},
         "gpu_launches": 2 * args.steps,

@@ -18,6 +18,7 @@
 // for temperature 1 and row maxima within a binade of the values that holds, and the parity tests
 // compare against the whole-row reference to catch any difference.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 
 #include "dllm_chunk.cuh"
 
@@ -48,12 +49,17 @@ struct ShardArgs {
     int32_t *status;
 };
 
+constexpr int SH_SURV = 1024;    // survivors of the threshold pre-filter kept for the exact select
+
 struct SelScratch {
     unsigned hist[256];
     uint32_t ck[SH_KMAX];
     int cid[SH_KMAX];
     int wsum[SH_T / 32];
+    uint32_t wv[SH_T / 32];
     int bin, above, ncand;
+    uint32_t thr;
+    int nsurv;
 };
 
 // Appends to s.ck / s.cid (from s.ncand) the `need` entries equal to `target` with the lowest ids.
@@ -212,6 +218,66 @@ __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int 
     __syncthreads();
 }
 
+// block_select behind a pre-filter.  The threads form Kp groups (Kp = K rounded up to a power of
+// two, Kp <= blockDim.x); each group's largest key is a real entry, so at least Kp >= K entries
+// hold a key >= thr = the smallest group maximum, and the K best entries by (key desc, id asc),
+// ties at the K-th key included, all do.  Those survivors (typically a few hundred of 8192) are
+// gathered into sk / sid and block_select runs on them alone.  When thr is the masked key (some
+// group saw only masked or no entries) or more than `cap` entries survive, block_select runs on
+// all n.  `tmax` is the largest key among the entries this thread produced (0 if none).
+__device__ void thresh_select(const uint32_t *keys, const int *ids, int id0, int n, int K, uint32_t tmax,
+                              SelScratch &s, uint32_t *sk, int *sid, int cap, uint32_t *out_key, int *out_id) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
+    int Kp = 1;
+    while (Kp < K) Kp <<= 1;
+    const int gs = NT / Kp;  // threads per group
+    uint32_t g = tmax;
+    for (int o = 1; o < gs && o < 32; o <<= 1) g = max(g, __shfl_xor_sync(0xffffffffu, g, o));
+    uint32_t wmin = g;
+    for (int o = 16; o; o >>= 1) wmin = min(wmin, __shfl_xor_sync(0xffffffffu, wmin, o));
+    if (lane == 0) s.wv[wid] = gs <= 32 ? wmin : g;
+    if (tid == 0) s.nsurv = 0;
+    __syncthreads();
+    if (tid == 0) {
+        uint32_t thr = 0xffffffffu;
+        if (gs <= 32) {
+            for (int w = 0; w < NW; w++) thr = min(thr, s.wv[w]);
+        } else {
+            const int gw = gs / 32;  // warps per group
+            for (int w0 = 0; w0 < NW; w0 += gw) {
+                uint32_t gm = 0u;
+                for (int w = w0; w < w0 + gw; w++) gm = max(gm, s.wv[w]);
+                thr = min(thr, gm);
+            }
+        }
+        s.thr = thr;
+    }
+    __syncthreads();
+    const uint32_t thr = s.thr;
+    if (thr > okey(-INFINITY) && K <= NT) {
+        for (int base = 0; base < n; base += NT) {
+            const int i = base + tid;
+            const bool keep = i < n && keys[i] >= thr;
+            const unsigned bm = __ballot_sync(0xffffffffu, keep);
+            int pos0 = 0;
+            if (lane == 0 && bm) pos0 = atomicAdd(&s.nsurv, __popc(bm));
+            pos0 = __shfl_sync(0xffffffffu, pos0, 0);
+            const int pos = pos0 + __popc(bm & ((1u << lane) - 1u));
+            if (keep && pos < cap) {
+                sk[pos] = keys[i];
+                sid[pos] = ids ? ids[i] : id0 + i;
+            }
+        }
+        __syncthreads();
+        const int ns = s.nsurv;
+        if (ns <= cap) {
+            block_select(sk, sid, 0, ns, K, s, out_key, out_id);
+            return;
+        }
+    }
+    block_select(keys, ids, id0, n, K, s, out_key, out_id);
+}
+
 // One CTA per (chunk of up to SH_CHUNK columns, row): mask, penalties, keys in shared memory, the
 // chunk's k best.  With one chunk per row they are the shard's final candidates.
 template <int DT>
@@ -237,9 +303,16 @@ __global__ void __launch_bounds__(SH_T) shard_chunk_kernel(const ShardArgs a) {
     const size_t esz = DT == DLLM_DTYPE_BF16 ? 2 : 4;
     const unsigned char *src = (const unsigned char *)a.logits + ((int64_t)row * a.row_stride + c0) * esz;
     const bool vec = ((uintptr_t)src & 15u) == 0;
-    chunk_visit<DT>(src, vec, mrow, c0, n, cp, p, a.flags, [&](int li, float v) { keys[li] = okey(v); });
+    uint32_t tmax = 0u;
+    chunk_visit<DT>(src, vec, mrow, c0, n, cp, p, a.flags, [&](int li, float v) {
+        const uint32_t key = okey(v);
+        keys[li] = key;
+        tmax = max(tmax, key);
+    });
     __syncthreads();
-    block_select(keys, nullptr, c0, n, a.k, sel, okey_s, oid_s);
+    uint32_t *sk = keys + SH_CHUNK;
+    int *sid = reinterpret_cast<int *>(sk + SH_SURV);
+    thresh_select(keys, nullptr, c0, n, a.k, tmax, sel, sk, sid, SH_SURV, okey_s, oid_s);
     if (a.nchunks == 1) {
         for (int i = tid; i < a.k; i += NT) {
             a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
@@ -265,12 +338,364 @@ __global__ void __launch_bounds__(SH_T) shard_rowmerge_kernel(const ShardArgs a)
     const int n = a.nchunks * a.k;
     uint32_t *keys = reinterpret_cast<uint32_t *>(rdyn);
     int *ids = reinterpret_cast<int *>(keys + n);
+    uint32_t *sk = reinterpret_cast<uint32_t *>(ids + n);
+    int *sid = reinterpret_cast<int *>(sk + SH_SURV);
+    uint32_t tmax = 0u;
     for (int i = tid; i < n; i += NT) {
-        keys[i] = a.part_key[(int64_t)row * n + i];
+        const uint32_t key = a.part_key[(int64_t)row * n + i];
+        keys[i] = key;
         ids[i] = a.part_id[(int64_t)row * n + i];
+        tmax = max(tmax, key);
     }
     __syncthreads();
-    block_select(keys, ids, 0, n, a.k, sel, okey_s, oid_s);
+    thresh_select(keys, ids, 0, n, a.k, tmax, sel, sk, sid, SH_SURV, okey_s, oid_s);
+    for (int i = tid; i < a.k; i += NT) {
+        a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
+        a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
+    }
+}
+
+// One CTA per row streams all of the shard's columns once and keeps a running top-K' (K' = k + the
+// history bound) of the raw masked values, by (value desc, id asc):
+//  * candidates go to a shared-memory buffer; once the buffer has been cut to the best K' entries,
+//    only keys strictly above the K'-th (thr) can enter (an equal key arrives with a larger id and
+//    loses the tie), so after the first few tiles almost nothing is appended;
+//  * the first tile's threshold comes from group maxima (at least K' entries reach it);
+//  * one barrier per tile decides whether the buffer must be cut (block_select on it).
+// History penalties are applied afterwards, exactly: the true top-k is contained in (the K' best
+// raw entries that are not history ids) united with (every history id of this shard, with its
+// penalised value), because at most H of the K' best raw entries are history ids.  The union is
+// selected by (key desc, id asc) once more.  Used when k + the history bound <= SH_KMAX.
+constexpr int ST_T = 256;          // threads per row CTA
+constexpr int ST_U = 2;            // 16-byte vectors per thread per tile
+constexpr int ST_PD = 6;           // tiles pulled into L2 ahead of the loads
+constexpr int ST_CAP = 4608;       // candidate buffer entries
+constexpr int ST_FIN = 2 * SH_KMAX;  // final union entries
+
+template <int DT>
+__global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a, int kprime) {
+    extern __shared__ __align__(16) unsigned char sdyn[];
+    uint32_t *bk = reinterpret_cast<uint32_t *>(sdyn);   // [ST_CAP]
+    int *bid = reinterpret_cast<int *>(bk + ST_CAP);      // [ST_CAP]
+    uint32_t *fk = reinterpret_cast<uint32_t *>(bid + ST_CAP);  // [ST_FIN]
+    int *fid = reinterpret_cast<int *>(fk + ST_FIN);             // [ST_FIN]
+    int *hl = fid + ST_FIN;                                      // [SH_KMAX] history local ids
+    int *hall = hl + SH_KMAX;                                    // [SH_KMAX] the row's history ids
+    __shared__ SelScratch sel;
+    __shared__ uint32_t okey_s[SH_KMAX];
+    __shared__ int oid_s[SH_KMAX];
+    __shared__ int s_nb, s_strict, s_nh;
+    __shared__ uint32_t s_thr;
+    constexpr int VEC = DT == DLLM_DTYPE_BF16 ? 8 : 4;
+    constexpr int E = ST_T * ST_U * VEC;  // columns per tile
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, NT = blockDim.x;
+    const int n = a.vlocal;
+    const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
+    const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
+    const size_t esz = DT == DLLM_DTYPE_BF16 ? 2 : 4;
+    const unsigned char *src = (const unsigned char *)a.logits + (int64_t)row * a.row_stride * esz;
+    const bool vec = ((uintptr_t)src & 15u) == 0;
+    const int nv = vec ? (n & ~(VEC - 1)) : 0;
+    const uint32_t KNEG = okey(-INFINITY);
+    const bool pen = pen_active(a.hist_ids, a.hist_off, p);
+    int64_t h0 = 0, h1 = 0;
+    if (pen) {
+        h0 = a.hist_off[row];
+        h1 = a.hist_off[row + 1];
+    }
+    if (tid == 0) {
+        s_nb = 0;
+        s_strict = 0;
+        s_thr = 0u;
+    }
+    // the row's history (at most SH_KMAX - k ids: the host checks k + the bound <= SH_KMAX)
+    const int nhist = pen ? (int)(h1 - h0 < (int64_t)SH_KMAX ? h1 - h0 : (int64_t)SH_KMAX) : 0;
+    for (int j = tid; j < nhist; j += NT) hall[j] = a.hist_ids[h0 + j];
+    auto raw_at = [&](int li) -> float {
+        const bool al = !mrow || ((mrow[li >> 5] >> (li & 31)) & 1u);
+        return al ? chunk_raw(src, DT, li) : -INFINITY;
+    };
+    // the 16-byte vector at column i -> VEC keys (masked columns get the -inf key)
+    auto vec_keys = [&](int i, const uint4 raw, uint32_t mword, uint32_t (&key)[VEC]) {
+        const uint32_t mw = mword >> (i & 31);
+        float x[VEC];
+        if (DT == DLLM_DTYPE_BF16) {
+            const uint32_t w4[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                x[2 * j] = bitsf(w4[j] << 16);
+                x[2 * j + 1] = bitsf(w4[j] & 0xffff0000u);
+            }
+        } else {
+            x[0] = bitsf(raw.x);
+            x[1] = bitsf(raw.y);
+            x[2] = bitsf(raw.z);
+            x[3] = bitsf(raw.w);
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; j++) key[j] = ((mw >> j) & 1u) ? okey(x[j]) : KNEG;
+    };
+    // appends this thread's passing keys (bit j of m) of the vector at column i
+    auto append = [&](int i, const uint32_t (&key)[VEC], unsigned m) {
+        const int c = __popc(m);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        int base = 0;
+        if (lane == 31 && incl) base = atomicAdd(&s_nb, incl);
+        base = __shfl_sync(0xffffffffu, base, 31) + incl - c;
+#pragma unroll
+        for (int j = 0; j < VEC; j++)
+            if ((m >> j) & 1u) {
+                if (base < ST_CAP) {
+                    bk[base] = key[j];
+                    bid[base] = i + j;
+                }
+                base++;
+            }
+    };
+    // cuts the buffer to its best kprime entries (sorted); later keys must beat the K'-th
+    auto cut = [&]() {
+        const int nb = min(s_nb, ST_CAP);
+        block_select(bk, bid, 0, nb, kprime, sel, okey_s, oid_s);
+        const int kk = min(nb, kprime);
+        for (int i = tid; i < kk; i += NT) {
+            bk[i] = okey_s[i];
+            bid[i] = oid_s[i];
+        }
+        __syncthreads();
+        if (tid == 0) {
+            s_nb = kk;
+            if (kk == kprime) {
+                s_thr = okey_s[kprime - 1];
+                s_strict = 1;
+            }
+        }
+        __syncthreads();
+    };
+
+    // Tiles of E columns, ST_U 16-byte vectors per thread.  Two register sets take turns (the loop
+    // is unrolled by two, so a set is reloaded only after it has been processed and no register
+    // move waits on a load in flight), and thread 0 pulls the tile ST_PD tiles ahead into L2.
+    const uint4 *src4 = reinterpret_cast<const uint4 *>(src);
+    auto load_tile = [&](int b, uint4 (&dst)[ST_U], uint32_t (&mdst)[ST_U]) {
+#pragma unroll
+        for (int u = 0; u < ST_U; u++) {
+            const int i = b + VEC * (tid + u * NT);
+            dst[u] = i < nv ? src4[i / VEC] : make_uint4(0u, 0u, 0u, 0u);
+            mdst[u] = (mrow && i < nv) ? mrow[i >> 5] : 0xffffffffu;
+        }
+    };
+    auto prefetch_tile = [&](int b) {
+        if (tid != 0 || b >= nv) return;
+        const int cols = min(E, nv - b) & ~(VEC - 1);
+        const unsigned char *p0 = src + (size_t)b * esz;
+        if (cols > 0 && ((uintptr_t)p0 & 15u) == 0 && ((cols * esz) & 15u) == 0) prefetch_l2(p0, (uint32_t)(cols * esz));
+        if (mrow) {
+            const uint32_t *m0 = mrow + (b >> 5);
+            const int words = (cols + 31) >> 5;
+            if (((uintptr_t)m0 & 15u) == 0 && ((words * 4) & 15) == 0) prefetch_l2(m0, (uint32_t)(words * 4));
+        }
+    };
+    bool first = true;
+    // one tile: every column keyed while the threshold is not finite (the exact path); after that
+    // only vectors whose largest masked value reaches it (a packed maximum and one compare each;
+    // the mask only lowers values, NaN propagates to the exact path)
+    auto process = [&](int b, const uint4 (&r)[ST_U], const uint32_t (&mr)[ST_U]) {
+        prefetch_tile(b + ST_PD * E);
+        if (s_thr <= KNEG) {
+            uint32_t key[ST_U][VEC];
+#pragma unroll
+            for (int u = 0; u < ST_U; u++) {
+                const int i = b + VEC * (tid + u * NT);
+                if (i < nv) vec_keys(i, r[u], mr[u], key[u]);
+                else
+#pragma unroll
+                    for (int j = 0; j < VEC; j++) key[u][j] = 0u;
+            }
+            if (first) {
+                // group maxima of the first tile: at least kprime keys reach their minimum
+                uint32_t tmax = 0u;
+#pragma unroll
+                for (int u = 0; u < ST_U; u++)
+#pragma unroll
+                    for (int j = 0; j < VEC; j++) tmax = max(tmax, key[u][j]);
+                int Kp = 1;
+                while (Kp < kprime) Kp <<= 1;
+                const int gs = NT / Kp;
+                uint32_t g = tmax;
+                for (int o = 1; o < gs && o < 32; o <<= 1) g = max(g, __shfl_xor_sync(0xffffffffu, g, o));
+                if (gs > 32) g = 0u;  // groups wider than a warp: no pre-filter
+                uint32_t wmin = g;
+                for (int o = 16; o; o >>= 1) wmin = min(wmin, __shfl_xor_sync(0xffffffffu, wmin, o));
+                if (lane == 0) sel.wv[tid >> 5] = wmin;
+                __syncthreads();
+                if (tid == 0) {
+                    uint32_t t = 0xffffffffu;
+                    for (int w = 0; w < NT / 32; w++) t = min(t, sel.wv[w]);
+                    s_thr = t == 0xffffffffu ? 0u : t;
+                }
+                __syncthreads();
+                first = false;
+            }
+            const uint32_t thr = s_thr;
+            const bool strict = s_strict != 0;
+#pragma unroll
+            for (int u = 0; u < ST_U; u++) {
+                unsigned m = 0u;
+#pragma unroll
+                for (int j = 0; j < VEC; j++) m |= (strict ? key[u][j] > thr : key[u][j] >= thr) ? (1u << j) : 0u;
+                if (__any_sync(0xffffffffu, m != 0u)) append(b + VEC * (tid + u * NT), key[u], m);
+            }
+        } else {
+            const uint32_t thr = s_thr;
+            const bool strict = s_strict != 0;
+            const float tf = okey_inv(thr);
+            // lane-local: a bit per column whose masked value reaches tf (or is NaN), then each
+            // set bit is checked exactly on its key and appended with one shared atomic
+            auto add = [&](int col, float x) {
+                const uint32_t key = okey(x);
+                if (strict ? key > thr : key >= thr) {
+                    const int pos = atomicAdd(&s_nb, 1);
+                    if (pos < ST_CAP) {
+                        bk[pos] = key;
+                        bid[pos] = col;
+                    }
+                }
+            };
+#pragma unroll
+            for (int u = 0; u < ST_U; u++) {
+                const int i = b + VEC * (tid + u * NT);
+                if (i >= nv) continue;
+                const uint32_t mb = mr[u] >> (i & 31);  // this vector's mask bits (all ones: no mask)
+                unsigned bits;
+                if (DT == DLLM_DTYPE_BF16) {
+                    const __nv_bfloat162 t2 = __floats2bfloat162_rn(tf, tf);  // tf is a bf16 value
+                    const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
+                    bits = 0u;
+                    __nv_bfloat162 mx = *reinterpret_cast<const __nv_bfloat162 *>(&w[0]);
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const __nv_bfloat162 a2 = *reinterpret_cast<const __nv_bfloat162 *>(&w[q]);
+                        const unsigned m2 = __hge2_mask(a2, t2);
+                        bits |= ((m2 & 1u) | ((m2 >> 15) & 2u)) << (2 * q);
+                        if (q) mx = __hmax2_nan(mx, a2);
+                    }
+                    const float lo = __low2float(mx), hi = __high2float(mx);
+                    if (lo != lo || hi != hi) bits = 0xffu;
+                    bits &= mb & 0xffu;
+                    while (bits) {
+                        const int q = __ffs(bits) - 1;
+                        bits &= bits - 1u;
+                        const uint32_t ww = w[q >> 1];
+                        add(i + q, bitsf((q & 1) ? (ww & 0xffff0000u) : (ww << 16)));
+                    }
+                } else {
+                    const float x[4] = {bitsf(r[u].x), bitsf(r[u].y), bitsf(r[u].z), bitsf(r[u].w)};
+                    bits = 0u;
+#pragma unroll
+                    for (int q = 0; q < 4; q++) bits |= (!(x[q] < tf)) ? (1u << q) : 0u;  // >= tf or NaN
+                    bits &= mb & 0xfu;
+                    while (bits) {
+                        const int q = __ffs(bits) - 1;
+                        bits &= bits - 1u;
+                        add(i + q, x[q]);
+                    }
+                }
+            }
+        }
+        __syncthreads();
+        if (s_nb > ST_CAP - E) cut();
+    };
+    for (int d = 0; d < ST_PD; d++) prefetch_tile(d * E);
+    {
+        uint4 ra[ST_U], rb[ST_U];
+        uint32_t ma[ST_U], mb2[ST_U];
+        load_tile(0, ra, ma);
+        load_tile(E, rb, mb2);
+        int base = 0;
+        while (base < nv) {
+            process(base, ra, ma);
+            if (base + 2 * E < nv) load_tile(base + 2 * E, ra, ma);
+            base += E;
+            if (base >= nv) break;
+            process(base, rb, mb2);
+            if (base + 2 * E < nv) load_tile(base + 2 * E, rb, mb2);
+            base += E;
+        }
+    }
+    // unaligned tail, one column per thread per round
+    for (int i0 = nv; i0 < n; i0 += NT) {
+        const int i = i0 + tid;
+        uint32_t key[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; j++) key[j] = 0u;
+        unsigned m = 0u;
+        if (i < n) {
+            const float v = raw_at(i);
+            key[0] = okey(v);
+            const uint32_t thr = s_thr;
+            m = (s_strict ? key[0] > thr : key[0] >= thr) ? 1u : 0u;
+        }
+        if (__any_sync(0xffffffffu, m != 0u)) append(i, key, m);
+        __syncthreads();
+        if (s_nb > ST_CAP - NT) cut();
+    }
+    __syncthreads();
+    cut();
+    // the union: the K' best raw entries that are not history ids, and each history id of this
+    // shard once, with its penalised value (src/sampler.c:21-52, after the mask)
+    const int nraw = s_nb;
+    if (tid == 0) s_nh = 0;
+    __syncthreads();
+    if (pen) {
+        for (int j = tid; j < nhist; j += NT) {
+            const int id = hall[j];
+            if (id < 0 || id >= a.vtotal) continue;
+            const int64_t li = (int64_t)id - a.voff;
+            if (li < 0 || li >= n) continue;
+            // the first occurrence of the id stands for all of them
+            bool firstocc = true;
+            for (int q = 0; q < j && firstocc; q++) firstocc = hall[q] != id;
+            if (!firstocc) continue;
+            const int at = atomicAdd(&s_nh, 1);
+            if (at < SH_KMAX) hl[at] = (int)li;
+        }
+    }
+    __syncthreads();
+    const int nh = min(s_nh, SH_KMAX);
+    // the raw entries that are not history ids (their order does not matter: the select ranks
+    // by key and id)
+    if (tid == 0) s_nb = 0;
+    __syncthreads();
+    for (int i = tid; i < nraw; i += NT) {
+        bool inhist = false;
+        for (int q = 0; q < nh && !inhist; q++) inhist = hl[q] == bid[i];
+        if (!inhist) {
+            const int at = atomicAdd(&s_nb, 1);
+            fk[at] = bk[i];
+            fid[at] = bid[i];
+        }
+    }
+    __syncthreads();
+    const int nr = s_nb;
+    if (nh > 0) {
+        const float inv_rep = __fdiv_rn(1.0f, p.repetition);
+        const bool true_div = (a.flags & DLLM_MODE_PEN_TRUE_DIV) != 0;
+        for (int q = tid; q < nh; q += NT) {
+            const int li = hl[q];
+            const int64_t gid = (int64_t)li + a.voff;
+            int c = 0;
+            for (int j = 0; j < nhist; j++) c += hall[j] == gid;
+            fk[nr + q] = okey(penalise(raw_at(li), c, p, true_div, inv_rep));
+            fid[nr + q] = li;
+        }
+    }
+    __syncthreads();
+    block_select(fk, fid, 0, nr + nh, a.k, sel, okey_s, oid_s);
     for (int i = tid; i < a.k; i += NT) {
         a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
         a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
@@ -394,15 +819,30 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
         if (!part) return DLLM_ERR_OOM;
         a.part_key = reinterpret_cast<uint32_t *>(part);
         a.part_id = reinterpret_cast<int32_t *>(a.part_key + (size_t)a.rows * a.nchunks * k);
-        const size_t rs = (size_t)a.nchunks * k * 8;
+        const size_t rs = (size_t)a.nchunks * k * 8 + (size_t)SH_SURV * 8;
         if (rs > 200 * 1024) return DLLM_ERR_UNSUPPORTED;
         if (cudaFuncSetAttribute((const void *)shard_rowmerge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)rs) != cudaSuccess)
             return DLLM_ERR_CUDA;
     }
     if (a.status) cudaMemsetAsync(a.status, 0, (size_t)a.rows * sizeof(int32_t), stream);
+    // one streaming CTA per row when the union of K' = k + history bound raw candidates and the
+    // history entries fits the exact select
+    const int hb = (d->hist_ids && d->hist_off) ? (d->hist_max > 0 ? d->hist_max : 0) : 0;
+    if (k + hb <= SH_KMAX && !getenv("DLLM_SHARD_CHUNKED")) {
+        const size_t ss = (size_t)ST_CAP * 8 + (size_t)ST_FIN * 8 + (size_t)SH_KMAX * 8;
+        const void *fs = d->dtype == DLLM_DTYPE_BF16 ? (const void *)shard_stream_kernel<DLLM_DTYPE_BF16>
+                                                     : (const void *)shard_stream_kernel<DLLM_DTYPE_F32>;
+        if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss) != cudaSuccess)
+            return DLLM_ERR_CUDA;
+        if (d->dtype == DLLM_DTYPE_BF16)
+            shard_stream_kernel<DLLM_DTYPE_BF16><<<a.rows, ST_T, ss, stream>>>(a, k + hb);
+        else
+            shard_stream_kernel<DLLM_DTYPE_F32><<<a.rows, ST_T, ss, stream>>>(a, k + hb);
+        return cudaGetLastError() == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
+    }
     const dim3 grid(a.nchunks, a.rows);
-    const size_t ks = (size_t)SH_CHUNK * 4;
+    const size_t ks = (size_t)SH_CHUNK * 4 + (size_t)SH_SURV * 8;  // keys, then the survivors
     const void *fn = d->dtype == DLLM_DTYPE_BF16 ? (const void *)shard_chunk_kernel<DLLM_DTYPE_BF16>
                                                  : (const void *)shard_chunk_kernel<DLLM_DTYPE_F32>;
     if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks) != cudaSuccess)
@@ -411,7 +851,8 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
         shard_chunk_kernel<DLLM_DTYPE_BF16><<<grid, SH_T, ks, stream>>>(a);
     else
         shard_chunk_kernel<DLLM_DTYPE_F32><<<grid, SH_T, ks, stream>>>(a);
-    if (a.nchunks > 1) shard_rowmerge_kernel<<<a.rows, SH_T, (size_t)a.nchunks * k * 8, stream>>>(a);
+    if (a.nchunks > 1)
+        shard_rowmerge_kernel<<<a.rows, SH_T, (size_t)a.nchunks * k * 8 + (size_t)SH_SURV * 8, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
 }
 

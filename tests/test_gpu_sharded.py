@@ -4,7 +4,8 @@ On one GPU the N shards run one after another (dllm_cuda_shard_candidates per co
 their candidates are stacked as the all-gather would stack them, and dllm_cuda_merge_sample
 draws.  Checked: every shard's candidates (values and ids) bit for bit against the oracle's
 penalised row, and the tokens against the oracle's tokens (src/sampler.c:136-234 on whole rows).
-With two GPUs the same runs through NCCL in two processes.
+With two GPUs the same runs through NCCL in two processes.  Every test runs on both candidate
+kernels (the per-row streaming kernel and the per-chunk kernels).
 """
 from __future__ import annotations
 
@@ -23,6 +24,17 @@ from util import csr, ids_match, pack_mask, u24
 pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(autouse=True, params=["stream", "chunked"])
+def shard_path(request, monkeypatch):
+    """both candidate kernels: one streaming CTA per row (the default when k + the history bound
+    fits its exact select) and the per-chunk kernels with the row merge (DLLM_SHARD_CHUNKED)"""
+    if request.param == "chunked":
+        monkeypatch.setenv("DLLM_SHARD_CHUNKED", "1")
+    else:
+        monkeypatch.delenv("DLLM_SHARD_CHUNKED", raising=False)
+    return request.param
 
 
 def _shard_np(pen, s, e, k):
