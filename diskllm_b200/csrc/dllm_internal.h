@@ -55,6 +55,7 @@ struct KernelArgs {
     unsigned long long *dbg;        // diagnostic counters or null
     unsigned char  *ws;             // workspace (row headers, warp records, stash)
     int             nrec;           // warp records per row (4 * warps * cluster)
+    int             dbg_rank;       // cluster rank whose phases the diagnostic counters time
 };
 
 // Launch configuration chosen by the host for one (vocab, dtype, history bound, top-k bound).

@@ -54,6 +54,10 @@
 
 #include "dllm_internal.h"
 
+#ifndef DLLM_TMA_PIECE
+#define DLLM_TMA_PIECE (1 << 20)  // one bulk copy per slice (the mbarrier transaction count allows < 2^20 bytes)
+#endif
+
 namespace cg = cooperative_groups;
 
 namespace dllm {
@@ -81,7 +85,7 @@ namespace {
 constexpr int MAXW = 16;          // warps per CTA (blockDim <= 512)
 constexpr int MAXC = 16;          // CTAs per cluster
 constexpr int CAND_CAP = 2048;    // top-k survivors gathered in CTA 0
-constexpr int TMA_PIECE = 32768;  // bytes per bulk copy instruction
+constexpr int TMA_PIECE = DLLM_TMA_PIECE;  // bytes per bulk copy instruction
 constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
 constexpr int WALK_WARPS = 4;     // rows per CTA of the walk kernel
 constexpr int HLIST = 256;        // per-warp history ids kept for a recomputed region
@@ -1072,7 +1076,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         return ok;
     };
 
-    const bool timing = a.dbg != nullptr && rank == 0 && tid == 0;
+    const bool timing = a.dbg != nullptr && rank == a.dbg_rank && tid == 0;
     long long tmark = clock64();
     auto mark = [&](int k) {
         if (timing) {
@@ -2001,6 +2005,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         b1[q] = sin ? c1[q] : 0u;
                     }
                 }
+                mark(DBG_P3);  // (index-order path: record classification)
                 // stash / wide slots for the four quarters: one claim per warp on CTA 0's counter
                 bool need_st[4], need_wd[4];
                 int n_st = 0, n_wd = 0;
@@ -2058,6 +2063,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         }
                     }
                 }
+                mark(DBG_W3);  // (slot claims and copies)
                 // the slice is no longer read: the next row's bulk copy starts here
                 if (use_tma && !dbuf) {
                     fence_proxy_async();
@@ -2065,8 +2071,10 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     if (tid == 0 && row + ncl < a.rows) issue_row_copy(row + ncl, 0);
                     copy_issued = true;
                 }
+                mark(DBG_P3L);  // (barrier and bulk-copy issue)
                 compose_scan4(a0, a1);
                 if (any_nonconf) compose_scan4(b0, b1);
+                mark(DBG_P3S);  // (compositions)
                 if (lane == 31) {
 #pragma unroll
                     for (int q = 0; q < 4; q++) {

@@ -203,6 +203,9 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     lc.numAttrs = 1;
     KernelArgs args = a;
     args.dbg = g_host_dbg;
+    args.dbg_rank = 0;
+    if (g_host_dbg)
+        if (const char *e = getenv("DLLM_DBG_RANK")) args.dbg_rank = atoi(e);
     if (g_ev_before) cudaEventRecord(g_ev_before, stream);
     e = cudaLaunchKernelEx(&lc, fn, args);
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
