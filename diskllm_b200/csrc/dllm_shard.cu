@@ -60,6 +60,7 @@ struct SelScratch {
     int bin, above, ncand;
     uint32_t thr;
     int nsurv;
+    int ntie;
 };
 
 // Appends to s.ck / s.cid (from s.ncand) the `need` entries equal to `target` with the lowest ids.
@@ -70,6 +71,33 @@ __device__ void select_ties(const uint32_t *keys, const int *ids, int id0, int n
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
     if (need <= 0) return;
     if (ids) {
+        // the tied entries' ids in a short list (s.hist is free once the radix passes are done),
+        // then each ranked among the tied ones only
+        if (tid == 0) s.ntie = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += NT)
+            if (keys[i] == target) {
+                const int at = atomicAdd(&s.ntie, 1);
+                if (at < 256) s.hist[at] = (unsigned)ids[i];
+            }
+        __syncthreads();
+        const int nt = s.ntie;
+        if (nt <= 256) {
+            for (int j = tid; j < nt; j += NT) {
+                const int idj = (int)s.hist[j];
+                int r = 0;
+                for (int q = 0; q < nt; q++) r += (int)s.hist[q] < idj;
+                if (r < need) {
+                    const int pos = atomicAdd(&s.ncand, 1);
+                    if (pos < cap) {
+                        s.ck[pos] = target;
+                        s.cid[pos] = idj;
+                    }
+                }
+            }
+            __syncthreads();
+            return;
+        }
         for (int i = tid; i < n; i += NT) {
             if (keys[i] != target) continue;
             int r = 0;
@@ -367,8 +395,8 @@ __global__ void __launch_bounds__(SH_T) shard_rowmerge_kernel(const ShardArgs a)
 // penalised value), because at most H of the K' best raw entries are history ids.  The union is
 // selected by (key desc, id asc) once more.  Used when k + the history bound <= SH_KMAX.
 constexpr int ST_T = 256;          // threads per row CTA
-constexpr int ST_U = 2;            // 16-byte vectors per thread per tile
-constexpr int ST_PD = 6;           // tiles pulled into L2 ahead of the loads
+constexpr int ST_U = 1;            // 16-byte vectors per thread per tile
+constexpr int ST_PD = 12;          // tiles pulled into L2 ahead of the loads
 constexpr int ST_CAP = 4608;       // candidate buffer entries
 constexpr int ST_FIN = 2 * SH_KMAX;  // final union entries
 
