@@ -348,18 +348,25 @@ def params_array(rows_params, device):
     return torch.from_numpy(raw).to(device)
 
 
-def shard_candidates(logits, vocab_offset, vocab_total, k, params=None, *, stream=None, check=True, **kw):
+def shard_candidates(logits, vocab_offset, vocab_total, k, params=None, *, stream=None, check=True, out=None,
+                     **kw):
     """Step 1 of vocabulary-sharded sampling on this GPU's columns: returns (values float32
     [rows][k], global ids int32 [rows][k]) of each row's k best entries after mask and penalties.
     `logits` holds columns [vocab_offset, vocab_offset + logits.shape[1]); `mask` (if given) the
-    words of those columns; history ids are global."""
+    words of those columns; history ids are global.  `out` = (vals, ids): contiguous [rows][k]
+    tensors to write into (views of one buffer, for a single all-gather)."""
     import torch
 
     rows = logits.shape[0]
     dummy_u = torch.empty(max(rows, 1), dtype=torch.float32, device=logits.device)
     d, _ = fill_desc(logits, dummy_u, params, **kw)
-    vals = torch.empty(rows, k, dtype=torch.float32, device=logits.device)
-    ids = torch.empty(rows, k, dtype=torch.int32, device=logits.device)
+    if out is not None:
+        vals, ids = out
+        assert vals.is_contiguous() and ids.is_contiguous() and vals.shape == (rows, k) and ids.shape == (rows, k)
+        assert vals.dtype == torch.float32 and ids.dtype == torch.int32
+    else:
+        vals = torch.empty(rows, k, dtype=torch.float32, device=logits.device)
+        ids = torch.empty(rows, k, dtype=torch.int32, device=logits.device)
     s = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
     rc = load_library().dllm_cuda_shard_candidates(C.byref(d), int(vocab_offset), int(vocab_total), int(k),
                                                    vals.data_ptr(), ids.data_ptr(), s)

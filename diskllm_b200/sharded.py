@@ -47,10 +47,22 @@ def sample_vocab_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab_to
     k = int(k if k is not None else params.get("top_k", 0))
     if not (0 < int(params.get("top_k", 0)) <= k):
         raise ValueError("vocabulary-sharded sampling needs 0 < top_k <= k")
+    rows = logits_shard.shape[0]
+    distributed = group is not None or (dist.is_available() and dist.is_initialized())
+    if distributed:
+        # values and ids in one buffer ([2][rows][k] int32 words), so one all-gather moves both
+        buf = torch.empty(2 * rows * k, dtype=torch.int32, device=logits_shard.device)
+        vals = buf[:rows * k].view(torch.float32).view(rows, k)
+        ids = buf[rows * k:].view(rows, k)
+        capi.shard_candidates(logits_shard, vocab_offset, vocab_total, k, params, mask=mask_shard,
+                              hist_ids=hist_ids, hist_off=hist_off, hist_max=hist_max, out=(vals, ids))
+        world = dist.get_world_size(group)
+        allb = torch.empty(world * 2 * rows * k, dtype=torch.int32, device=logits_shard.device)
+        dist.all_gather_into_tensor(allb, buf, group=group)
+        allb = allb.view(world, 2, rows, k)
+        all_v = allb[:, 0].contiguous().view(torch.float32)
+        all_i = allb[:, 1].contiguous()
+        return capi.merge_sample(all_v, all_i, uniforms, params)
     vals, ids = capi.shard_candidates(logits_shard, vocab_offset, vocab_total, k, params, mask=mask_shard,
                                       hist_ids=hist_ids, hist_off=hist_off, hist_max=hist_max)
-    if group is not None or (dist.is_available() and dist.is_initialized()):
-        all_v, all_i = gather_candidates(vals, ids, group)
-    else:
-        all_v, all_i = vals.unsqueeze(0), ids.unsqueeze(0)
-    return capi.merge_sample(all_v, all_i, uniforms, params)
+    return capi.merge_sample(vals.unsqueeze(0), ids.unsqueeze(0), uniforms, params)
