@@ -29,6 +29,23 @@ def gather_candidates(vals: torch.Tensor, ids: torch.Tensor, group=None) -> tupl
     return out_v.view(world, rows, k), out_i.view(world, rows, k)
 
 
+def candidate_buffer(rows: int, k: int, device) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """One int32 buffer [2][rows][k] holding a rank's candidate values (float32 bits) then ids, so
+    one all-gather moves both.  Returns (buffer, values view, ids view)."""
+    buf = torch.empty(2 * rows * k, dtype=torch.int32, device=device)
+    return buf, buf[:rows * k].view(torch.float32).view(rows, k), buf[rows * k:].view(rows, k)
+
+
+def gather_packed(buf: torch.Tensor, rows: int, k: int, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """All-gathers every rank's candidate_buffer with one collective and returns the values
+    [world][rows][k] float32 and ids [world][rows][k] int32, contiguous, in rank order."""
+    world = dist.get_world_size(group)
+    allb = torch.empty(world * 2 * rows * k, dtype=torch.int32, device=buf.device)
+    dist.all_gather_into_tensor(allb, buf, group=group)
+    allb = allb.view(world, 2, rows, k)
+    return allb[:, 0].contiguous().view(torch.float32), allb[:, 1].contiguous()
+
+
 def shard_range(vocab_total: int, rank: int, world: int) -> tuple[int, int]:
     """Columns [start, end) of `rank` when vocab_total is split into `world` equal shards whose
     boundaries fall on mask words (multiples of 32)."""
@@ -50,18 +67,10 @@ def sample_vocab_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab_to
     rows = logits_shard.shape[0]
     distributed = group is not None or (dist.is_available() and dist.is_initialized())
     if distributed:
-        # values and ids in one buffer ([2][rows][k] int32 words), so one all-gather moves both
-        buf = torch.empty(2 * rows * k, dtype=torch.int32, device=logits_shard.device)
-        vals = buf[:rows * k].view(torch.float32).view(rows, k)
-        ids = buf[rows * k:].view(rows, k)
+        buf, vals, ids = candidate_buffer(rows, k, logits_shard.device)
         capi.shard_candidates(logits_shard, vocab_offset, vocab_total, k, params, mask=mask_shard,
                               hist_ids=hist_ids, hist_off=hist_off, hist_max=hist_max, out=(vals, ids))
-        world = dist.get_world_size(group)
-        allb = torch.empty(world * 2 * rows * k, dtype=torch.int32, device=logits_shard.device)
-        dist.all_gather_into_tensor(allb, buf, group=group)
-        allb = allb.view(world, 2, rows, k)
-        all_v = allb[:, 0].contiguous().view(torch.float32)
-        all_i = allb[:, 1].contiguous()
+        all_v, all_i = gather_packed(buf, rows, k, group)
         return capi.merge_sample(all_v, all_i, uniforms, params)
     vals, ids = capi.shard_candidates(logits_shard, vocab_offset, vocab_total, k, params, mask=mask_shard,
                                       hist_ids=hist_ids, hist_off=hist_off, hist_max=hist_max)

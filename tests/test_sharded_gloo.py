@@ -76,7 +76,14 @@ def _worker(rank, world, port, result):
         s, e = sharded.shard_range(V, rank, world)
         v, i = _shard_candidates_np(ora.pen_logits, s, e, k)
         all_v, all_i = sharded.gather_candidates(torch.from_numpy(v), torch.from_numpy(i))
+        # the single-collective layout sample_vocab_sharded uses: values and ids in one buffer
+        buf, bv, bi = sharded.candidate_buffer(rows, k, "cpu")
+        bv.copy_(torch.from_numpy(v))
+        bi.copy_(torch.from_numpy(i))
+        pv, pi = sharded.gather_packed(buf, rows, k)
         if rank == 0:
+            result["packed_equal"] = bool(torch.equal(pv.view(torch.int32), all_v.view(torch.int32)) and
+                                          torch.equal(pi, all_i))
             merged = _merge_np(all_v.numpy(), all_i.numpy(), params["temperature"], k)
             result["ok"] = bool(np.array_equal(merged, ora.topk_idx))
             result["shapes"] = tuple(all_v.shape)
@@ -100,3 +107,4 @@ def test_two_gloo_ranks_merge_to_the_whole_row_topk():
         mp.spawn(_worker, args=(2, port, result), nprocs=2, join=True)
         assert result.get("shapes") == (2, 6, 16)
         assert result.get("ok"), "merged shard candidates differ from the whole-row top-k"
+        assert result.get("packed_equal"), "one-buffer all-gather differs from the two-tensor gather"
