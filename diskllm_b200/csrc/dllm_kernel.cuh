@@ -20,7 +20,7 @@
 //       and softmax / min-p / top-p / draw run on that short list (a 4-pass radix select is
 //       the fallback when too many elements survive the threshold)
 //   otherwise (top-k off: the reference's index-order list):
-//   P2  t = (x - M) * (1/T), e = exp(t - max_t) in place, compensated sum -> cluster sum
+//   P2  t = (x - M) * (1/T), e = exp(t - max_t) in place, fp32 sub-chunk sums -> cluster sum
 //   P2b min-p (absolute threshold) kept count / renormalisation sum      -> cluster sums
 //   P3  sub-chunk sums of the list probabilities, exclusive scan over the cluster; the one warp
 //       holding the sub-chunk where (float)cumsum first reaches top_p finds the cut element
@@ -885,8 +885,8 @@ __device__ __forceinline__ T pick4(const T (&v)[4], int q) {
     return q == 0 ? v[0] : q == 1 ? v[1] : q == 2 ? v[2] : v[3];
 }
 
-// P2 body: exponentials of this thread's four sub-chunks, written back in place, and their
-// compensated sums.  Sub-chunks past the slice (the shared zero sub-chunk) are skipped.
+// P2 body: exponentials of this thread's four sub-chunks, written back in place, and their fp32
+// sums.  Sub-chunks past the slice (the shared zero sub-chunk) are skipped.
 template <int NV4>
 __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, float M, float inv_temp, float mv,
                                         double (&sube)[4]) {
@@ -894,7 +894,8 @@ __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, 
     bool real[4];
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-        sub[q] = csum_zero();
+        // a plain sum from 0 in .s; .c holds the base so that csum_val returns .s exactly
+        sub[q] = CSum{0.0f, CSUM_BASE};
         real[q] = kb[q] < S;
     }
     // temperature 1 (and no shift): ((x - M) * 1) - 0 == x - M exactly, so skip the two no-ops
@@ -918,10 +919,11 @@ __device__ __forceinline__ void p2_scan(float *vals, const int (&kb)[4], int S, 
                 t23 = fmul2(t23, L2E2);
                 x = make_float4(ex2(t01.x), ex2(t01.y), ex2(t23.x), ex2(t23.y));
                 *p = x;
-                // the four summed plainly (error ~2^-24 of a 4-element sum), the group sum
-                // compensated
+                // plain fp32 sums: a sub-chunk of SUB elements carries a relative error of about
+                // SUB/4 * 2^-24, which moves the row sum by ~1e-9 relative (random signs), far
+                // below the one-ulp spread of (float)(1/sum) that the probability tolerance covers
                 const float2 s2 = fadd2(make_float2(x.x, x.y), make_float2(x.z, x.w));
-                csum_add(sub[q], __fadd_rn(s2.x, s2.y));
+                sub[q].s = __fadd_rn(sub[q].s, __fadd_rn(s2.x, s2.y));
             }
         }
     }
@@ -1610,7 +1612,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 if (lane < C) tv = remote_xs(lane)->mt;
                 mv = warp_allreduce(tv, [](float x, float y) { return fmaxf(x, y); });
             }
-            // P2: exponentials (in place) and compensated sums per sub-chunk, scanned in
+            // P2: exponentials (in place) and fp32 sums per sub-chunk, scanned (in double) in
             // sub-chunk order; the prefix sums of e place the top-p cut
             double sube[4];
             p2_scan<NV4>(vals, kb, S, M, inv_temp, mv, sube);
