@@ -17,6 +17,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdiskllm_cuda.so")
 
 DLLM_OK = 0
+DLLM_ERR_INVALID_ARG = 1
+DLLM_ERR_OOM = 2
+DLLM_ERR_UNSUPPORTED = 6
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "NCCL", 5: "TIMEOUT",
                 6: "UNSUPPORTED"}
 DTYPE_F32 = 0
@@ -29,6 +32,7 @@ ROW_ERR_NONFINITE = 2
 ROW_ERR_TOPK_LARGE = 4
 ROW_ERR_WALK = 8
 ROW_ERR_TIMEOUT = 16
+ROW_TOPP_EDGE = 32  # information: the index-order top-p cut lies near the threshold
 
 # every symbol the public headers declare
 EXPORTS = [
@@ -126,7 +130,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_merge_sample.restype = C.c_int
     lib.dllm_cuda_merge_sample.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
                                            C.POINTER(SamplerParams), C.c_void_p, C.c_void_p, C.c_void_p,
-                                           C.c_void_p]
+                                           C.c_void_p, C.c_void_p]
     lib.dllm_cuda_lmhead_logits.restype = C.c_int
     lib.dllm_cuda_lmhead_logits.argtypes = [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_float, C.c_int,
                                             C.c_void_p, C.c_int, C.c_float, C.c_void_p, C.c_void_p]
@@ -375,8 +379,11 @@ def shard_candidates(logits, vocab_offset, vocab_total, k, params=None, *, strea
     return vals, ids
 
 
-def merge_sample(vals, ids, uniforms, params=None, *, row_params=None, token=None, stream=None, check=True):
-    """Step 3: tokens from all-gathered candidates vals / ids [nshards][rows][k]."""
+def merge_sample(vals, ids, uniforms, params=None, *, row_params=None, token=None, status=None, stream=None,
+                 check=True):
+    """Step 3: tokens from all-gathered candidates vals / ids [nshards][rows][k].  `status` (int32
+    [rows], optional) receives DLLM_ROW_ERR_TOPK_LARGE for per-row params the candidates cannot
+    serve (temperature > 0 with top_k outside 1..k); those rows get the greedy token."""
     import torch
 
     nsh, rows, k = vals.shape
@@ -389,8 +396,9 @@ def merge_sample(vals, ids, uniforms, params=None, *, row_params=None, token=Non
         token = torch.empty(rows, dtype=torch.int32, device=vals.device)
     s = stream if stream is not None else torch.cuda.current_stream(vals.device).cuda_stream
     rp = row_params.data_ptr() if row_params is not None else None
+    st = status.data_ptr() if status is not None else None
     rc = load_library().dllm_cuda_merge_sample(rows, nsh, k, vals.data_ptr(), ids.data_ptr(), C.byref(params), rp,
-                                               uniforms.data_ptr(), token.data_ptr(), s)
+                                               uniforms.data_ptr(), token.data_ptr(), st, s)
     if check and rc != DLLM_OK:
         raise DllmError(f"dllm_cuda_merge_sample: {STATUS_NAMES.get(rc, rc)} ({load_library().dllm_cuda_last_error().decode()})")
     return token

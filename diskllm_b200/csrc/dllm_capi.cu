@@ -224,12 +224,13 @@ extern "C" dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *d, int6
 extern "C" dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const float *cand_val,
                                               const int32_t *cand_id, const dllm_sampler_params *params,
                                               const dllm_sampler_params *row_params, const float *uniforms,
-                                              int32_t *token, void *stream) {
+                                              int32_t *token, int32_t *status, void *stream) {
     if (rows < 0 || nshards < 1 || k < 1 || !params) return DLLM_ERR_INVALID_ARG;
     if (rows > 0 && (!cand_val || !cand_id || !uniforms || !token)) return DLLM_ERR_INVALID_ARG;
-    if (!row_params && (params->top_k < 1 || params->top_k > k)) return DLLM_ERR_UNSUPPORTED;
+    if (!row_params && params->temperature != 0.0f && (params->top_k < 1 || params->top_k > k))
+        return DLLM_ERR_UNSUPPORTED;
     const dllm_status st = launch_merge_sample(rows, nshards, k, cand_val, cand_id, params, row_params, uniforms,
-                                               token, (cudaStream_t)stream);
+                                               token, status, (cudaStream_t)stream);
     if (st == DLLM_ERR_CUDA) set_error("merge kernel launch", cudaGetLastError());
     return st;
 }

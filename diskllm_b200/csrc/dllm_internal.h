@@ -102,7 +102,7 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
                                     int32_t *cand_id, void *part, cudaStream_t stream);
 dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, const int32_t *ids,
                                 const dllm_sampler_params *params, const dllm_sampler_params *row_params,
-                                const float *uniforms, int32_t *token, cudaStream_t stream);
+                                const float *uniforms, int32_t *token, int32_t *status, cudaStream_t stream);
 dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream);
 int nrec_for(const LaunchCfg &cfg);
 

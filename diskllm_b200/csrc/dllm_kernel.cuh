@@ -1336,15 +1336,13 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             if (lane < C) gv = remote_xs(lane)->gidx;
             token = warp_allreduce(gv, [](int x, int y) { return min(x, y); });
             if (token == INT_MAX) token = 0;
-        } else if (M == -INFINITY) {
-            // fully masked row: every t is NaN, comparisons fail, the reference's list stays in
-            // id order and it returns the last entry
+        } else if (M == -INFINITY || M == INFINITY) {
+            // fully masked row (M = -inf) or a row holding +inf: every t is -inf or NaN
+            // ((x - M) * inv_temp), comparisons fail, so the reference's list stays in id order
+            // and, with its sum NaN, its draw returns the last entry (src/sampler.c:153-233)
             token = topk ? p.top_k - 1 : a.vocab_total - 1;
             if (topk && a.topk_ids && rank == 0)
                 for (int i = tid; i < p.top_k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = i + a.vocab_offset;
-        } else if (!(M < INFINITY) || M != M) {
-            rowflags |= ROW_ERR_NONFINITE;
-            token = 0;
         } else if (topk) {
             // ---------------- top-k ----------------------------------------------------------
             const int k = p.top_k;
@@ -1591,6 +1589,9 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     for (int i = tid; i < k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = il[i] + a.vocab_offset;
                 if (wid == 0) {
                     float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride : nullptr;
+                    // a NaN logit sorts first (its key is the largest); the reference's order of
+                    // NaNs in its insertion sort is not defined by its -ffast-math build
+                    if (isnan(tl[0])) rowflags |= ROW_ERR_NONFINITE;
                     token = sample_sorted_list(tl, il, k, p, r, pr, (a.flags & DLLM_MODE_MINP_RELATIVE) != 0);
                 }
             }
@@ -1642,6 +1643,14 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     if (rr == rank) offE = sum;
                     sum = sum + __shfl_sync(0xffffffffu, xd, rr);
                 }
+            }
+            if (isnan(sum)) {
+                // a NaN logit (the maximum ignores it) makes the reference's sum, and so every
+                // probability, NaN: no cut is reached and its draw returns the list's last
+                // entry (src/sampler.c:176-233).  Every CTA of the cluster sees the same sum.
+                token = a.vocab_total - 1;
+                done = true;
+                goto row_done;
             }
 
             Chain ch;

@@ -738,6 +738,7 @@ struct MergeArgs {
     const dllm_sampler_params *rparams;
     const float *uniforms;
     int32_t *token;
+    int32_t *status;       // [rows] or null
 };
 
 constexpr int MG_THREADS = 256;
@@ -754,7 +755,12 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
     __shared__ int red_i[MG_THREADS / 32];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x;
     const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
-    const int k = min(p.top_k, a.k);
+    // Sampling rows need 1 <= top_k <= k: the gathered lists hold each shard's k best, so a
+    // larger top_k (or top-k off) cannot be served from them.  Such a row gets the greedy token
+    // (always correct to take from the candidates) and DLLM_ROW_ERR_TOPK_LARGE.
+    const bool bad_k = p.temperature != 0.0f && (p.top_k < 1 || p.top_k > a.k);
+    const int k = bad_k ? 1 : p.top_k;
+    if (a.status && tid == 0) a.status[row] = bad_k ? ROW_ERR_TOPK_LARGE : 0;
     for (int i = tid; i < n; i += NT) {
         const int s = i / a.k, j = i % a.k;
         v[i] = a.vals[((int64_t)s * a.rows + row) * a.k + j];
@@ -769,7 +775,7 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
     __syncthreads();
     float M = -INFINITY;
     for (int w = 0; w < NT / 32; w++) M = fmaxf(M, red_f[w]);
-    if (p.temperature == 0.0f) {
+    if (p.temperature == 0.0f || bad_k) {
         int best = INT_MAX;
         for (int i = tid; i < n; i += NT)
             if (v[i] == M) best = min(best, id[i]);
@@ -783,8 +789,8 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
         }
         return;
     }
-    if (M == -INFINITY) {
-        // every t is NaN: the reference's list keeps id order and returns its last entry
+    if (M == -INFINITY || M == INFINITY) {
+        // every t is -inf or NaN: the reference's list keeps id order and returns its last entry
         if (tid == 0) a.token[row] = k - 1;
         return;
     }
@@ -886,7 +892,7 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
 
 dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, const int32_t *ids,
                                 const dllm_sampler_params *params, const dllm_sampler_params *row_params,
-                                const float *uniforms, int32_t *token, cudaStream_t stream) {
+                                const float *uniforms, int32_t *token, int32_t *status, cudaStream_t stream) {
     if (nsh < 1 || k < 1 || k > SH_KMAX || nsh * k > MG_MAX) return DLLM_ERR_UNSUPPORTED;
     MergeArgs a = {};
     a.rows = rows;
@@ -898,6 +904,7 @@ dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, con
     a.rparams = row_params;
     a.uniforms = uniforms;
     a.token = token;
+    a.status = status;
     if (rows == 0) return DLLM_OK;
     const size_t smem = (size_t)nsh * k * 8 + (size_t)k * 8;
     if (cudaFuncSetAttribute((const void *)merge_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -168,14 +168,18 @@ DLLM_API dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_cou
  * the penalised logits (fp32), ids global.  k <= 256.
  * Step 2, the caller: all-gather the two arrays over the N GPUs into [N][rows][k].
  * Step 3, on any GPU: one token per row from the gathered candidates (per-row or broadcast
- * params; top_k <= k; uniforms and token device arrays [rows]). */
+ * params; uniforms, token and the optional status are device arrays [rows]).  A sampling row
+ * (temperature > 0) needs 1 <= top_k <= k: broadcast params outside that range are rejected
+ * with DLLM_ERR_UNSUPPORTED; a per-row top_k outside it gets the greedy token and status bit
+ * DLLM_ROW_ERR_TOPK_LARGE. */
 DLLM_API dllm_status dllm_cuda_shard_candidates(const dllm_batch_desc *desc, int64_t vocab_offset,
                                                 int64_t vocab_total, int k, float *cand_val,
                                                 int32_t *cand_id, void *stream);
 DLLM_API dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const float *cand_val,
                                             const int32_t *cand_id, const dllm_sampler_params *params,
                                             const dllm_sampler_params *row_params,
-                                            const float *uniforms, int32_t *token, void *stream);
+                                            const float *uniforms, int32_t *token, int32_t *status,
+                                            void *stream);
 
 /* The step before the sampler (src/core/context.c:854-876): the final RMSNorm of `rows` hidden
  * states h [rows][hidden] (fp32; src/rmsnorm.c:4-27, norm_w may be NULL, add_one for Gemma's

@@ -1,4 +1,4 @@
-"""Two-GPU run of vocabulary-sharded sampling through NCCL (launched by test_gpu_sharded.py with
+"""Multi-GPU run (2, 4 or 8 ranks) of vocabulary-sharded sampling through NCCL (launched by test_gpu_sharded.py with
 torch.distributed.run).  Every rank builds the same seeded rows, samples from its own columns
 with sharded.sample_vocab_sharded, and checks that all ranks drew the same tokens; rank 0 checks
 them against the whole-row oracle."""

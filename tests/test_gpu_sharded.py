@@ -4,7 +4,7 @@ On one GPU the N shards run one after another (dllm_cuda_shard_candidates per co
 their candidates are stacked as the all-gather would stack them, and dllm_cuda_merge_sample
 draws.  Checked: every shard's candidates (values and ids) bit for bit against the oracle's
 penalised row, and the tokens against the oracle's tokens (src/sampler.c:136-234 on whole rows).
-With two GPUs the same runs through NCCL in two processes.  Every test runs on both candidate
+With 2, 4 or 8 GPUs the same runs through NCCL, one process per GPU.  Every test runs on both candidate
 kernels (the per-row streaming kernel and the per-chunk kernels).
 """
 from __future__ import annotations
@@ -135,13 +135,53 @@ def test_greedy():
     _run(x, None, hist, params, 4, 8)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpus_nccl():
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_nccl_ranks(world):
+    """world ranks, one per GPU, each sampling from its own columns; candidates all-gathered by NCCL"""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     script = os.path.join(ROOT, "tests", "sharded_nccl_worker.py")
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "tests"),
                                                       os.path.join(ROOT, "oracle")]))
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29613", script]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr=127.0.0.1", f"--master-port={29613 + world}", script]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
     assert "SHARDED_NCCL_OK" in res.stdout
+
+
+def test_merge_rejects_rows_the_candidates_cannot_serve():
+    """per-row top_k above the gathered k, or top-k off, at temperature > 0: greedy token plus
+    DLLM_ROW_ERR_TOPK_LARGE; the other rows sample normally"""
+    rng = np.random.default_rng(15)
+    rows, V, k = 6, 4096, 16
+    x = (rng.standard_normal((rows, V)) * 2.0).astype(np.float32)
+    uni = u24(rng, rows)
+    good = dict(temperature=0.8, top_k=12, top_p=0.9)
+    per_row = [good, dict(good, top_k=k + 1), dict(good, top_k=0), good, dict(good, top_k=-3),
+               dict(good, top_k=k)]
+    dev = torch.device("cuda", 0)
+    xt = torch.from_numpy(x).to(dev)
+    vs, is_ = [], []
+    for r in range(2):
+        s, e = sharded.shard_range(V, r, 2)
+        v, i = capi.shard_candidates(xt[:, s:e], s, V, k, good)
+        vs.append(v)
+        is_.append(i)
+    rp = capi.params_array(per_row, dev)
+    status = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+    tok = capi.merge_sample(torch.stack(vs).contiguous(), torch.stack(is_).contiguous(),
+                            torch.from_numpy(uni).to(dev), good, row_params=rp, status=status)
+    torch.cuda.synchronize()
+    tok, status = tok.cpu().numpy(), status.cpu().numpy()
+    for r, p in enumerate(per_row):
+        if 1 <= p["top_k"] <= k:
+            assert status[r] == 0
+            ora = O.sample_restated(x[r:r + 1], p, uni[r:r + 1], kept_cap=k)
+            assert ids_match(int(tok[r]), ora, uni[r:r + 1], 0)
+        else:
+            assert status[r] == capi.ROW_ERR_TOPK_LARGE
+            assert tok[r] == int(np.argmax(x[r]))
+    with pytest.raises(capi.DllmError):
+        capi.merge_sample(torch.stack(vs).contiguous(), torch.stack(is_).contiguous(),
+                          torch.from_numpy(uni).to(dev), dict(good, top_k=k + 1))
