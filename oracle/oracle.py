@@ -275,6 +275,51 @@ def reference_cdf(logits_row, params, mask_row=None, hist_row=None, n_boundaries
     return np.array(ids, dtype=np.int64), np.array(cdf, dtype=np.float64)
 
 
+def reference_cdf_around(logits_row, params, r, mask_row=None, hist_row=None):
+    """The reference's fp32 CDF boundaries that enclose the uniform r: returns (lo, hi, id) with
+    lo <= r < hi, where the reference returns `id` for every uniform in [lo, hi) (lo = the
+    running sum before id's entry, hi = the one after it; hi = inf when id is the list's last
+    entry and r reaches the total).  Found by bisection on the uniform's bit pattern."""
+    row = np.ascontiguousarray(logits_row, dtype=np.float32)[None, :]
+    mask = None if mask_row is None else np.asarray(mask_row, dtype=np.uint32)[None, :]
+    hist = None if hist_row is None else [hist_row]
+
+    def draw(bits):
+        x = np.array([np.uint32(bits)], dtype=np.uint32).view(np.float32)
+        res, _ = sample_reference(row, params, x, mask=mask, hist=hist, threads=1)
+        return int(res.token[0])
+
+    f2b = lambda x: int(np.array([x], dtype=np.float32).view(np.uint32)[0])
+    b2f = lambda b: float(np.array([np.uint32(b)], dtype=np.uint32).view(np.float32)[0])
+    rb = f2b(r)
+    tid = draw(rb)
+    # rand_f32 can emit every float in [2^-30, 1) and nothing smaller but 0
+    lo_lim, hi_lim = f2b(2.0 ** -30), f2b(1.0) - 1
+    if draw(hi_lim) == tid:
+        hi = np.inf
+    else:
+        a, z = rb, hi_lim
+        while z - a > 1:
+            m = (a + z) // 2
+            if draw(m) == tid:
+                a = m
+            else:
+                z = m
+        hi = b2f(z)
+    if draw(lo_lim) == tid:
+        lo = 0.0
+    else:
+        a, z = lo_lim, rb  # draw(a) != tid, draw(z) == tid
+        while z - a > 1:
+            m = (a + z) // 2
+            if draw(m) == tid:
+                z = m
+            else:
+                a = m
+        lo = b2f(z)
+    return lo, hi, tid
+
+
 # ---- LM-head tail (the step before the sampler) ----------------------------------------------
 
 RMSNORM_SO = os.path.join(HERE, "_ref", "librmsnorm_asbuilt.so")

@@ -8,7 +8,8 @@ rows.  Stored outputs, all from the reference:
   * tokens for eight injected uniforms per row (the harness seeds the reference's xorshift so
     that rand_f32 returns the wanted value);
   * SHA-256 of the penalised, masked logits (mask -> presence -> repetition, bit for bit);
-  * for the small rows, the first fp32 CDF boundaries recovered by bisection on the uniform.
+  * for the small rows, the first fp32 CDF boundaries recovered by bisection on the uniform;
+  * for the full-vocabulary rows, the two CDF boundaries that enclose row 1's first uniform.
 
     python tests/golden/make_golden.py      # needs oracle/_ref (make -C oracle ref)
 """
@@ -41,19 +42,29 @@ CASES = [
     ("top_k_3", 110, 4, 300, 2.0, False, 8, dict(temperature=0.5, top_k=3, top_p=1.0)),
     ("top_k_ge_V", 111, 4, 257, 2.0, True, 8, dict(temperature=2.0, top_k=999999, top_p=0.5)),
     ("tiny_vocab", 112, 4, 5, 2.0, False, 3, dict(temperature=1.0, top_k=0, top_p=0.9)),
+    # the benchmark configurations' full vocabularies, where the
+    # reference's sequential fp32 running sum drifts furthest from the exact prefix
+    ("cfg1_V128256", 121, 2, 128256, 2.5, False, 64, dict(temperature=0.8, top_k=40, top_p=0.95, repetition=1.1)),
+    ("cfg2_V151936", 122, 2, 151936, 3.0, False, 512, dict(temperature=0.7, top_k=50, top_p=0.9, repetition=1.1,
+                                                            presence=0.2)),
+    ("cfg3_V151936_mask", 123, 2, 151936, 2.0, 0.02, 0, dict(temperature=1.0, top_k=0, top_p=0.95)),
+    ("cfg4_V256000", 124, 2, 256000, 0.5, False, 256, dict(temperature=1.0, top_k=0, top_p=0.99, repetition=1.05)),
+    ("cfg5_V262144_mask", 125, 2, 262144, 2.0, 0.10, 128, dict(temperature=0.9, top_k=64, top_p=0.9,
+                                                                 repetition=1.1)),
 ]
 UNIFORMS_PER_ROW = 8
 CDF_BOUNDARIES = 24
 
 
 def case_inputs(seed, rows, V, sigma, with_mask, hlen):
-    """(logits, mask or None, history lists, uniforms [rows][UNIFORMS_PER_ROW]) of one case."""
+    """(logits, mask or None, history lists, uniforms [rows][UNIFORMS_PER_ROW]) of one case.
+    with_mask: False, True (30 % of ids allowed) or the allowed fraction."""
     rng = np.random.default_rng(seed)
     lg = (rng.standard_normal((rows, V)) * sigma).astype(np.float32)
     lg[0, V // 3] = lg[0].max()  # a tie for the maximum in the first row
     mask = None
     if with_mask:
-        allow = rng.random((rows, V)) < 0.3
+        allow = rng.random((rows, V)) < (0.3 if with_mask is True else float(with_mask))
         allow[:, 0] = True
         W = (V + 31) // 32
         pad = np.zeros((rows, W * 32), dtype=bool)
@@ -100,6 +111,13 @@ def main():
         case = {"name": name, "seed": seed, "rows": rows, "vocab": V, "sigma": sigma, "mask": with_mask,
                 "history": hlen, "params": params, "inputs_sha256": inputs_digest(lg, mask, hist, u),
                 "tokens": tokens.tolist(), "pen_logits_sha256": hashlib.sha256(pen.tobytes()).hexdigest()}
+        if V >= 100000 and params.get("temperature", 1.0) > 0:
+            # the reference's CDF boundaries on both sides of row 1's first uniform
+            lo, hi, tid = O.reference_cdf_around(lg[1], params, float(u[1, 0]), None if mask is None else mask[1],
+                                                 hist[1])
+            case["around_row"] = 1
+            case["around_id"] = tid
+            case["around_bits"] = [int(np.float32(lo).view(np.uint32)), int(np.float32(hi).view(np.uint32))]
         if V <= 1500 and params.get("temperature", 1.0) > 0:
             ids, cdf = O.reference_cdf(lg[1], params, None if mask is None else mask[1], hist[1],
                                        n_boundaries=CDF_BOUNDARIES)

@@ -63,6 +63,26 @@ def test_oracle_reproduces_reference_cdf(name):
             assert int(ocdf[i].view(np.uint32)) == bits[i], f"{name} boundary {i}"
 
 
+@pytest.mark.parametrize("name", [n for n, c in CASES.items() if "around_id" in c])
+def test_oracle_reproduces_reference_cdf_at_full_vocabulary(name):
+    """at the benchmark vocabularies (up to 262144 entries of sequential fp32 drift) the oracle's
+    running sum equals the reference's on both boundaries around the drawn entry, bit for bit"""
+    c = CASES[name]
+    lg, mask, hist, u = _inputs(c)
+    r = c["around_row"]
+    o = O.sample_restated(lg[r:r + 1], c["params"], u[r:r + 1, 0].copy(),
+                          mask=None if mask is None else mask[r:r + 1], hist=[hist[r]], kept_cap=c["vocab"])
+    assert int(o.token[0]) == c["around_id"]
+    n = int(o.kept_n[0])
+    ids = o.kept_idx[0, :n]
+    j = int(np.nonzero(ids == c["around_id"])[0][0])
+    lo_bits, hi_bits = c["around_bits"]
+    assert int(o.kept_cdf[0, j].view(np.uint32)) == hi_bits
+    if j > 0:
+        # the reference's lowest uniform drawing this id is the running sum before its entry
+        assert int(o.kept_cdf[0, j - 1].view(np.uint32)) == lo_bits
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("name", list(CASES))
 def test_cuda_path_on_golden_rows(name):
