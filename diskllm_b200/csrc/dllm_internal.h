@@ -12,10 +12,11 @@ namespace dllm {
 // Per-row status bits written to dllm_batch_desc::status (0 = OK).
 enum : int32_t {
     ROW_ERR_HIST_TABLE = 1,   // more distinct in-slice history ids than the table holds
-    ROW_ERR_NONFINITE  = 2,   // +inf / NaN row maximum (unsupported input)
+    ROW_ERR_NONFINITE  = 2,   // a NaN among a top-k row's candidates (order undefined in the reference)
     ROW_ERR_TOPK_LARGE = 4,   // top_k above the kernel's candidate capacity
     ROW_ERR_WALK       = 8,   // internal consistency check of the draw walk failed
     ROW_ERR_TIMEOUT    = 16,  // a bounded wait on a bulk copy expired
+    ROW_TOPP_EDGE      = 32,  // information, not an error: see DLLM_ROW_TOPP_EDGE
 };
 
 // Largest top-k list the fused kernel handles.

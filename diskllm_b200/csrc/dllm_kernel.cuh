@@ -89,7 +89,16 @@ constexpr int TMA_PIECE = DLLM_TMA_PIECE;  // bytes per bulk copy instruction
 constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
 constexpr int WALK_WARPS = 4;     // rows per CTA of the walk kernel
 constexpr int HLIST = 256;        // per-warp history ids kept for a recomputed region
-constexpr float DRAW_WINDOW = 1.0f / 16384.0f;  // bound assumed on |fp32 running sum - exact prefix|
+constexpr float DRAW_WINDOW = 1.0f / 16384.0f;
+// Relative difference of this kernel's exponential sums from the reference's (glibc's scalar and
+// 4-wide vector expf), measured on B200 at most 4e-8 over the benchmark row distributions; with
+// margin.  Used to flag top-p cuts the reference may place one entry away (ROW_TOPP_EDGE).
+constexpr double TOPP_EXP_DIFF = 6e-8;
+// one ulp of x relative to x (x a positive normal float)
+__device__ __forceinline__ double ulp_rel(float x) {
+    const uint32_t m = __float_as_uint(x) & 0x7fffffu;
+    return 1.0 / (double)(0x800000u + m);
+}  // bound assumed on |fp32 running sum - exact prefix|
 
 enum : int { REC_IDENT = 0, REC_CLEAN = 1, REC_MIXED = 2, REC_PBS = 3 };
 
@@ -144,6 +153,7 @@ struct Xch {
     float first_e;    // exponential of the slice's first element
     int last_member;
     int cut_idx;
+    int cut_flags;
     double cut_s3;
     int gidx;
     int flags;
@@ -167,7 +177,7 @@ struct __align__(16) Push2 {
 };
 struct __align__(16) Push4 {
     int cut_idx;
-    int pad;
+    int cut_flags;  // ROW_TOPP_EDGE when the prefix at the cut lies near the threshold
     double cut_s3;
 };
 
@@ -1160,6 +1170,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             if (rank == 0) sh.slots[(it + 1) & 1] = 0;
             sh.bcast_i[2] = 0;  // the CTA's row status bits
             sh.xs.cut_idx = -1;
+            sh.xs.cut_flags = 0;
         }
         for (int i = tid; i < a.htab; i += NT) {
             hkeys[i] = -1;
@@ -1819,34 +1830,49 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                             const double ex = __shfl_up_sync(0xffffffffu, x, 1);
                             double cum = lane == 0 ? base : base + ex;
                             int hitk = -1, lastm = -1;
-                            double hitc = 0.0;
+                            double hitc = 0.0, hitb = 0.0;
 #pragma unroll
                             for (int k = 0; k < SL; k++) {
                                 if (mem[k] && hitk < 0) {
+                                    const double before = cum;
                                     cum = cum + (double)wv[k];
                                     lastm = k;
                                     if (__double2float_rn(cum) >= tp) {
                                         hitk = k;
                                         hitc = cum;
+                                        hitb = before;
                                     }
                                 }
                             }
                             const unsigned hm = __ballot_sync(0xffffffffu, hitk >= 0);
                             int ci;
                             double cs3;
+                            int cfl = 0;
                             if (hm) {
                                 const int hl = __ffs(hm) - 1;
                                 ci = __shfl_sync(0xffffffffu, cb0 + j0 + hitk, hl);
                                 cs3 = __shfl_sync(0xffffffffu, hitc, hl);
+                                const double cb4 = __shfl_sync(0xffffffffu, hitb, hl);
+                                // (float)x >= tp exactly when x >= thr, the midpoint below tp.  The
+                                // reference's prefixes can sit up to thr * w from these: its
+                                // (float)(1/sum) may be one ulp away, and its exponentials add a
+                                // few 1e-8 relative (TOPP_EXP_DIFF) on their own
+                                const double thr = 0.5 * ((double)nextafterf(tp, 0.0f) + (double)tp);
+                                double w = ulp_rel(ch.inv_sum) + TOPP_EXP_DIFF;
+                                if (ch.minp) w += ulp_rel(ch.inv_s2);
+                                w *= thr;
+                                if (fabs(cs3 - thr) <= w || fabs(cb4 - thr) <= w) cfl = ROW_TOPP_EDGE;
                             } else {
                                 // rounding disagreed with the sub-chunk sum: cut at its last member
                                 const unsigned lm2 = __ballot_sync(0xffffffffu, lastm >= 0);
                                 const int ll = lm2 ? 31 - __clz(lm2) : 0;
                                 ci = __shfl_sync(0xffffffffu, cb0 + j0 + lastm, ll);
                                 cs3 = base + __shfl_sync(0xffffffffu, x, 31);
+                                cfl = ROW_TOPP_EDGE;  // the sub-chunk sums and the elements disagree on the crossing
                             }
                             if (lane == 0) {
                                 sh.xs.cut_idx = slice0 + ci;
+                                sh.xs.cut_flags = cfl;
                                 sh.xs.cut_s3 = cs3;
                             }
                         }
@@ -1855,7 +1881,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     if (tid == 0) mbar_arrive_expect_tx(&sh.xbar[2][par], (uint32_t)(C * sizeof(Push4)));
                     if (tid < C) {
                         const unsigned long long sb = (unsigned long long)__double_as_longlong(sh.xs.cut_s3);
-                        push16(&sh.in4[par][rank], &sh.xbar[2][par], tid, (uint32_t)sh.xs.cut_idx, 0u, (uint32_t)sb,
+                        push16(&sh.in4[par][rank], &sh.xbar[2][par], tid, (uint32_t)sh.xs.cut_idx,
+                               (uint32_t)sh.xs.cut_flags, (uint32_t)sb,
                                (uint32_t)(sb >> 32));
                     }
                     if (!xwait(2, par)) rowflags |= ROW_ERR_TIMEOUT;  // ---- #4
@@ -1863,10 +1890,12 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         const int xc = lane < C ? sh.in4[par][lane].cut_idx : -1;
                         const double xs3 = lane < C ? sh.in4[par][lane].cut_s3 : 0.0;
                         const unsigned hm = __ballot_sync(0xffffffffu, xc >= 0);
+                        const int xf = lane < C ? sh.in4[par][lane].cut_flags : 0;
                         if (hm) {
                             const int src = __ffs(hm) - 1;
                             cut = __shfl_sync(0xffffffffu, xc, src);
                             s3 = __shfl_sync(0xffffffffu, xs3, src);
+                            rowflags |= __shfl_sync(0xffffffffu, xf, src);
                         }
                     }
                 }

@@ -120,10 +120,22 @@ typedef struct {
 
 /* per-row status bits */
 #define DLLM_ROW_ERR_HIST_TABLE 1   /* more distinct history ids than the table holds */
-#define DLLM_ROW_ERR_NONFINITE  2   /* +inf / NaN row maximum (unsupported input) */
+#define DLLM_ROW_ERR_NONFINITE  2   /* a NaN among a top-k row's candidates: the reference's
+                                       -ffast-math build leaves its order undefined.  (Rows with
+                                       +inf, all-NaN rows and NaN rows with top-k off get the
+                                       reference's id: its list's last entry) */
 #define DLLM_ROW_ERR_TOPK_LARGE 4   /* top_k above the kernel's candidate capacity */
 #define DLLM_ROW_ERR_WALK       8   /* internal consistency check of the draw failed */
 #define DLLM_ROW_ERR_TIMEOUT   16   /* a bounded wait on a bulk copy expired */
+#define DLLM_ROW_TOPP_EDGE     32   /* information, not an error: the index-order top-p prefix
+                                       at the cut, or just before it, lies within
+                                       top_p * (one ulp of (float)(1/sum) + 6e-8) of the
+                                       threshold.  The reference's exponentials (glibc's scalar
+                                       and vector expf) differ from this library's by a few ulp,
+                                       so its (float)(1/sum) can be one ulp away and, on such a
+                                       row only, its cut one entry earlier or later
+                                       (src/sampler.c:204-222); its probabilities and id follow
+                                       that cut */
 
 /* Samples every row of the batch on `stream` (stream-ordered; returns after the launch).
  * Replaces, per row, the sequence of src/core/sampler_api.c:48-63:

@@ -13,7 +13,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from util import TOL_PROB, csr, dense_probs, ids_match, knife_edge_rescue, pack_mask, u24
+from util import TOL_PROB, csr, dense_probs, ids_match, pack_mask, u24
 
 pytestmark = pytest.mark.gpu
 
@@ -55,34 +55,71 @@ def _any_allowed(mrow, V):
     return bits.any()
 
 
-def check(lg, params, u, mask=None, hist=None, flags=0, dtype="f32", check_probs=True):
+def check(lg, params, u, mask=None, hist=None, flags=0, dtype="f32", check_probs=True, stats=None):
+    """GPU against the oracle on every row (see compare)."""
+    out = gpu_run(lg, params, u, mask, hist, flags, dtype)
+    return compare(lg, params, u, *out, mask=mask, hist=hist, flags=flags, dtype=dtype,
+                   check_probs=check_probs, stats=stats)
+
+
+def compare(lg, params, u, tok, probs, pen, status, tk, mask=None, hist=None, flags=0, dtype="f32",
+            check_probs=True, stats=None):
+    """GPU outputs against the oracle on every row.  A row the GPU flags ROW_TOPP_EDGE (its
+    index-order top-p prefix lies within the reference's rounding reach of the threshold) is held
+    to the same bars against the oracle as it stands or with its cut moved one entry earlier or
+    later, whichever the GPU's id and probabilities follow; every other row against the oracle as
+    it stands.  `stats` (a dict) accumulates rows, flagged rows and rows whose cut moved."""
+    from diskllm_b200 import capi
+
     rows, V = lg.shape
     ref_lg = lg
     if dtype == "bf16":
         ref_lg = torch.from_numpy(lg).to(torch.bfloat16).float().numpy()
-    tok, probs, pen, status, tk = gpu_run(lg, params, u, mask, hist, flags, dtype)
     k = params.get("top_k", 0)
     ora = O.sample_restated(ref_lg, params, u, mask=mask, hist=hist, flags=flags, want_pen=True,
                             kept_cap=V, topk_cap=k if 0 < k < V else 1)
-    assert np.all(status == 0), status
+    assert np.all((status & ~capi.ROW_TOPP_EDGE) == 0), status
+    edge = (status & capi.ROW_TOPP_EDGE) != 0
     assert np.array_equal(pen.view(np.uint32), ora.pen_logits.view(np.uint32))
-    bad = [i for i in range(rows) if not ids_match(int(tok[i]), ora, u, i)]
-    if dtype == "f32":
-        bad = knife_edge_rescue(bad, tok, lg, params, u, mask=mask, hist=hist, flags=flags)
-    assert not bad, f"id mismatch rows {bad[:8]}: gpu {tok[bad[:8]]} oracle {ora.token[bad[:8]]}"
-    if params.get("temperature", 1.0) == 0.0:
-        return tok, ora
-    if tk is not None:
+    variants = [ora]
+    if edge.any():
+        variants += [O.sample_restated(ref_lg, params, u, mask=mask, hist=hist, flags=flags | f, kept_cap=V,
+                                       topk_cap=k if 0 < k < V else 1) for f in (O.CUT_EARLIER, O.CUT_LATER)]
+
+    def probs_close(i, o):
+        g, d = probs[i].astype(np.float64), dense_probs(o, i, V).astype(np.float64)
+        if not np.array_equal(np.isnan(g), np.isnan(d)):
+            return False, np.inf
+        diff = np.abs(np.nan_to_num(g) - np.nan_to_num(d))
+        return diff.max() <= TOL_PROB, diff.max()
+
+    sampling = params.get("temperature", 1.0) != 0.0
+    moved = 0
+    for i in range(rows):
+        cands = variants if edge[i] else variants[:1]
+        skip_probs = (not check_probs or not sampling or ref_lg[i].max() == -np.inf
+                      or (mask is not None and not _any_allowed(mask[i], V)))
+        ok, worst = False, None
+        for j, o in enumerate(cands):
+            if not ids_match(int(tok[i]), o, u, i):
+                continue
+            if not skip_probs:
+                good, d = probs_close(i, o)
+                worst = d if worst is None else min(worst, d)
+                if not good:
+                    continue
+            ok = True
+            moved += j > 0
+            break
+        assert ok, (f"row {i} (edge flag {bool(edge[i])}): gpu id {tok[i]} oracle id {ora.token[i]}, "
+                    f"closest probability distance {worst}")
+    if stats is not None:
+        stats["rows"] = stats.get("rows", 0) + rows
+        stats["flagged"] = stats.get("flagged", 0) + int(edge.sum())
+        stats["cut_moved"] = stats.get("cut_moved", 0) + moved
+    if sampling and tk is not None:
         for i in range(rows):
             assert np.array_equal(tk[i], ora.topk_idx[i, :k]), i
-    if check_probs:
-        for i in range(rows):
-            if ref_lg[i].max() == -np.inf or (mask is not None and not _any_allowed(mask[i], V)):
-                continue
-            g, o = probs[i].astype(np.float64), dense_probs(ora, i, V).astype(np.float64)
-            assert np.array_equal(np.isnan(g), np.isnan(o)), i
-            d = np.abs(np.nan_to_num(g) - np.nan_to_num(o))
-            assert d.max() <= TOL_PROB, (i, d.max(), int(d.argmax()))
     return tok, ora
 
 
@@ -134,9 +171,12 @@ def test_parity_random_rows(V, name, with_mask):
         assert tok[1] == V // 3
 
 
-@pytest.mark.parametrize("name", ["cfg3", "cfg4", "plain", "server", "cfg1"])
-def test_parity_degenerate_rows(name):
-    V = 5003
+@pytest.mark.parametrize("V,name", [(5003, n) for n in ("cfg3", "cfg4", "plain", "server", "cfg1")] +
+                         [(256000, n) for n in ("cfg4", "cfg3", "minp_topp", "cfg1")])
+def test_parity_degenerate_rows(V, name):
+    """all-equal rows (the largest linear fp32 drift: at V = 256000 far beyond the draw window,
+    so the walk recomputes unslotted ranges), a dominant spike, a ramp, pairwise ties, very
+    peaked and tiny values"""
     rng = np.random.default_rng(5)
     rows = [np.zeros(V, np.float32)]                                       # all ties (linear drift)
     r = np.full(V, -5.0, np.float32); r[300] = 40.0; rows.append(r)        # p ~ 1 spike
@@ -145,7 +185,7 @@ def test_parity_degenerate_rows(name):
     rows.append((rng.standard_normal(V) * 30).astype(np.float32))          # very peaked
     rows.append(np.full(V, 1e-30, np.float32))                              # tiny values
     lg = np.stack(rows)
-    for seed in range(4):
+    for seed in range(4 if V < 100000 else 2):
         u = u24(np.random.default_rng(seed), len(rows))
         check(lg, PARAM_SETS[name], u)
 
@@ -210,7 +250,7 @@ def test_full_config4_batch_properties():
                            hist_off=w.hist_off, hist_max=w.hist_max)
     torch.cuda.synchronize()
     assert torch.equal(t1, t2)
-    assert int(st.abs().sum()) == 0
+    assert int((st & ~capi.ROW_TOPP_EDGE).abs().sum()) == 0
     sel = list(range(0, w.rows, 64))
     lg = w.logits[sel].cpu().numpy()
     hist = [W.hist_lists(w)[i] for i in sel]
@@ -268,4 +308,88 @@ def test_parity_config4_shape_256_rows():
     lg = (rng.standard_normal((rows, V)) * 0.5).astype(np.float32)
     hist = [rng.integers(0, V, 256) for _ in range(rows)]
     u = u24(rng, rows)
-    check(lg, PARAM_SETS["cfg4"], u, hist=hist, check_probs=False)
+    stats = {}
+    check(lg, PARAM_SETS["cfg4"], u, hist=hist, stats=stats)
+    print(f"config-4 shape, 256 rows: {stats}")
+
+
+def _full_batch(cfg):
+    """one launch over a whole benchmark batch, every output on"""
+    from diskllm_b200 import capi
+    from diskllm_b200 import workloads as W
+
+    w = W.CONFIGS[cfg](device="cuda")
+    V = w.vocab
+    probs = torch.full((w.rows, V), -1.0, device="cuda")
+    pen = torch.empty((w.rows, V), device="cuda")
+    status = torch.full((w.rows,), -1, dtype=torch.int32, device="cuda")
+    k = w.params.get("top_k", 0)
+    tk = torch.full((w.rows, k), -1, dtype=torch.int32, device="cuda") if 0 < k < V else None
+    kw = dict(probs=probs, pen_logits=pen, status=status, topk_ids=tk)
+    if w.hist_ids is not None:
+        kw.update(hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=w.hist_max)
+    if w.mask is not None:
+        kw["mask"] = w.mask
+    tok = capi.sample_batch(w.logits, w.uniforms, w.params, **kw)
+    torch.cuda.synchronize()
+    out = dict(tok=tok.cpu().numpy(), probs=probs.cpu().numpy(), pen=pen.cpu().numpy(),
+               status=status.cpu().numpy(), tk=None if tk is None else tk.cpu().numpy())
+    del probs, pen
+    return w, out
+
+
+@pytest.mark.parametrize("cfg", [2, 3, 4])
+def test_every_row_of_benchmark_batch(cfg):
+    """configs 2, 3 and 4 at full size (64 x 151936, 256 x 151936 with its JSON mask, 1024 x
+    256000): every row against the oracle, probabilities included, in blocks of rows"""
+    from diskllm_b200 import workloads as W
+
+    w, out = _full_batch(cfg)
+    lg = w.logits.float().cpu().numpy()
+    w.logits = None
+    torch.cuda.empty_cache()
+    mask = None if w.mask is None else w.mask.cpu().numpy().view(np.uint32)
+    hist = W.hist_lists(w)
+    u = w.uniforms.cpu().numpy()
+    stats = {}
+    blk = 128
+    for r0 in range(0, w.rows, blk):
+        sl = slice(r0, min(w.rows, r0 + blk))
+        sub = lambda a: None if a is None else a[sl]
+        compare(lg[sl], w.params, u[sl], out["tok"][sl], out["probs"][sl], out["pen"][sl], out["status"][sl],
+                sub(out["tk"]), mask=sub(mask), hist=None if hist is None else hist[sl], stats=stats)
+    if cfg == 3:
+        for r in w.notes["single_allowed_rows"]:
+            bits = np.unpackbits(mask[r].view(np.uint8), bitorder="little")[:w.vocab]
+            assert out["tok"][r] == int(np.nonzero(bits)[0][0]), r
+    print(f"config {cfg} full batch: {stats}")
+
+
+@pytest.mark.parametrize("k", [0, 40])
+def test_nonfinite_rows_follow_the_reference(k):
+    """+inf logits (one or several, or alone among -inf), all-NaN rows and NaN rows with top-k
+    off: the reference's sums turn NaN and its draw returns its list's last entry (the oracle is
+    pinned to that on CPU)"""
+    from diskllm_b200 import capi
+
+    rng = np.random.default_rng(33)
+    rows, V = 6, 6000
+    lg = (rng.standard_normal((rows, V))).astype(np.float32)
+    lg[0, 17] = np.inf
+    lg[1, [5, 4000]] = np.inf
+    lg[2, 123] = np.nan
+    lg[3, :] = -np.inf
+    lg[3, 9] = np.inf
+    lg[5, :] = np.nan
+    u = u24(rng, rows)
+    p = dict(temperature=0.8, top_k=k, top_p=0.9)
+    tok, _, _, st, _ = gpu_run(lg, p, u)
+    ora = O.sample_restated(lg, p, u)
+    for i in range(rows):
+        if i == 2 and k:
+            # a NaN among top-k candidates: the reference's insertion-sort order of NaNs is not
+            # defined by its -ffast-math build; the row is flagged instead
+            assert st[i] & capi.ROW_ERR_NONFINITE, st
+            continue
+        assert tok[i] == ora.token[i], (i, tok[i], ora.token[i])
+        assert st[i] & ~capi.ROW_TOPP_EDGE == 0, (i, st[i])
