@@ -40,6 +40,7 @@ EXPORTS = [
     "dllm_cuda_set_debug_counters", "dllm_cuda_workspace_bytes", "dllm_cuda_sample_batch_static",
     "dllm_cuda_set_timing_events", "dllm_cuda_shard_candidates", "dllm_cuda_merge_sample",
     "dllm_cuda_append_history", "dllm_cuda_lmhead_logits",
+    "dllm_cuda_debug_inject_wait_timeout", "dllm_cuda_debug_fail_allocations",
     "diskllm_grammar_init_from_file", "diskllm_grammar_init_from_str", "diskllm_grammar_init_json",
     "diskllm_grammar_free", "diskllm_grammar_reset", "diskllm_grammar_accept_str", "diskllm_grammar_advance",
     "diskllm_grammar_is_finished", "diskllm_grammar_apply_mask", "dllm_grammar_build_bitmask",
@@ -140,6 +141,10 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_set_timing_events.argtypes = [C.c_void_p, C.c_void_p]
     lib.dllm_cuda_sample_batch_static.restype = C.c_int
     lib.dllm_cuda_sample_batch_static.argtypes = [C.POINTER(BatchDesc), C.c_void_p]
+    lib.dllm_cuda_debug_inject_wait_timeout.restype = C.c_int
+    lib.dllm_cuda_debug_inject_wait_timeout.argtypes = [C.c_int, C.c_longlong]
+    lib.dllm_cuda_debug_fail_allocations.restype = C.c_int
+    lib.dllm_cuda_debug_fail_allocations.argtypes = [C.c_int]
     lib.dllm_cuda_workspace_bytes.restype = C.c_size_t
     lib.dllm_cuda_workspace_bytes.argtypes = [C.POINTER(BatchDesc)]
     lib.dllm_cuda_version.restype = C.c_char_p
@@ -172,6 +177,24 @@ def set_timing_events(before=None, after=None):
     rc = load_library().dllm_cuda_set_timing_events(b, a)
     if rc != DLLM_OK:
         raise DllmError(f"dllm_cuda_set_timing_events: {STATUS_NAMES.get(rc, rc)}")
+
+
+FAULT_NONE, FAULT_COPY_WAIT, FAULT_EXCHANGE_WAIT = 0, 1, 2
+
+
+def inject_wait_timeout(site: int, polls: int = 1) -> None:
+    """Test hook: later sampling launches make one bounded wait run out (FAULT_COPY_WAIT or
+    FAULT_EXCHANGE_WAIT) after `polls` polls; FAULT_NONE switches it off."""
+    rc = load_library().dllm_cuda_debug_inject_wait_timeout(int(site), int(polls))
+    if rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_debug_inject_wait_timeout: {STATUS_NAMES.get(rc, rc)}")
+
+
+def fail_allocations(count: int) -> None:
+    """Test hook: the library's next `count` device allocations fail as out of memory."""
+    rc = load_library().dllm_cuda_debug_fail_allocations(int(count))
+    if rc != DLLM_OK:
+        raise DllmError(f"dllm_cuda_debug_fail_allocations: {STATUS_NAMES.get(rc, rc)}")
 
 
 def set_debug_counters(tensor_or_none):

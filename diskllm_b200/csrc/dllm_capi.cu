@@ -10,6 +10,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <new>
 #include <vector>
@@ -36,6 +37,9 @@ extern "C" dllm_status dllm_cuda_set_timing_events(void *before, void *after) {
 }
 extern "C" dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters) {
     return set_debug_counters(device_counters);
+}
+extern "C" dllm_status dllm_cuda_debug_inject_wait_timeout(int site, long long polls) {
+    return set_fault_injection(site, polls);
 }
 
 extern "C" const char *dllm_cuda_version(void) { return "diskllm_cuda 0.1.0 sm_100a"; }
@@ -98,6 +102,23 @@ std::mutex g_ws_mu;
 std::vector<WsEntry> g_ws;
 }  // namespace
 
+// Test hook: this many of the next library allocations fail as if cudaMalloc had run out of
+// memory (dllm_cuda_debug_fail_allocations).
+static std::atomic<int> g_fail_allocs{0};
+
+static cudaError_t lib_malloc(void **p, size_t bytes) {
+    int n = g_fail_allocs.load();
+    while (n > 0)
+        if (g_fail_allocs.compare_exchange_weak(n, n - 1)) return cudaErrorMemoryAllocation;
+    return cudaMalloc(p, bytes);
+}
+
+extern "C" dllm_status dllm_cuda_debug_fail_allocations(int count) {
+    if (count < 0) return DLLM_ERR_INVALID_ARG;
+    g_fail_allocs.store(count);
+    return DLLM_OK;
+}
+
 static void *internal_workspace(void *stream, size_t bytes) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
@@ -108,12 +129,15 @@ static void *internal_workspace(void *stream, size_t bytes) {
         cudaFree(w.ptr);  // waits for kernels still using the old buffer
         w.ptr = nullptr;
         w.bytes = 0;
-        if (cudaMalloc(&w.ptr, bytes) != cudaSuccess) return nullptr;
+        if (lib_malloc(&w.ptr, bytes) != cudaSuccess) {
+            w.ptr = nullptr;
+            return nullptr;
+        }
         w.bytes = bytes;
         return w.ptr;
     }
     void *p = nullptr;
-    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    if (lib_malloc(&p, bytes) != cudaSuccess) return nullptr;
     g_ws.push_back({dev, stream, p, bytes});
     return p;
 }

@@ -57,6 +57,19 @@ struct KernelArgs {
     unsigned char  *ws;             // workspace (row headers, warp records, stash)
     int             nrec;           // warp records per row (4 * warps * cluster)
     int             dbg_rank;       // cluster rank whose phases the diagnostic counters time
+    long long       wait_limit;     // polls before a bounded wait on an mbarrier gives up
+    int             fault_site;     // test hook: FAULT_* wait made to run out, 0 = none
+};
+
+// Bounded waits: polls of an mbarrier before the wait gives up and the row is marked
+// ROW_ERR_TIMEOUT (about a second on B200).
+constexpr long long WAIT_LIMIT = 1ll << 26;
+// Test hook sites (dllm_cuda_debug_inject_wait_timeout): the cluster kernel adds one wait that
+// nothing completes, on the cluster's first row, with no copy or store in flight to it.
+enum : int {
+    FAULT_NONE = 0,
+    FAULT_COPY_WAIT = 1,      // CTA 0, after its slice's bulk copy landed
+    FAULT_EXCHANGE_WAIT = 2,  // the last CTA, after exchange #1 completed
 };
 
 // Launch configuration chosen by the host for one (vocab, dtype, history bound, top-k bound).
@@ -92,6 +105,7 @@ __host__ __device__ inline size_t walk_smem_per_warp(int nrec) {
 dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
 dllm_status set_debug_counters(unsigned long long *dev_counters);
 dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
+dllm_status set_fault_injection(int site, long long polls);
 size_t shard_part_bytes(int rows, int vlocal, int k);
 size_t sorted_ws_bytes(int rows, int vocab);
 dllm_status launch_sorted(const dllm_batch_desc *d, bool after_fused, void *ws, cudaStream_t stream);

@@ -64,12 +64,15 @@ namespace dllm {
 
 typedef void (*KernelFn)(const KernelArgs);
 
+constexpr int MAXC_HDR = 16;  // = MAXC, the most CTAs per cluster
 // Row scalars kept in the workspace for the walk kernel (128 bytes).
 struct RowHdr {
     float M, inv_temp, mv, inv_sum, min_p, inv_s2, inv_s3, r;
     int cut_idx, last_idx, flags, done, minp, nokept, topp;
-    int pad[17];
+    int rank_flags[MAXC_HDR];  // status bits each CTA of the row's cluster saw (timeouts after #1)
+    int pad[1];
 };
+static_assert(sizeof(RowHdr) == 128, "row_ws_bytes assumes a 128-byte row header");
 // Warp-level draw record (24 bytes).  meta: type (bits 0-1), boundary sub-chunk (2-7, 63 =
 // none), first suffix sub-chunk (8-13), prefix binade (16-23), suffix binade (24-31).
 struct WRec {
@@ -86,7 +89,6 @@ constexpr int MAXW = 16;          // warps per CTA (blockDim <= 512)
 constexpr int MAXC = 16;          // CTAs per cluster
 constexpr int CAND_CAP = 2048;    // top-k survivors gathered in CTA 0
 constexpr int TMA_PIECE = DLLM_TMA_PIECE;  // bytes per bulk copy instruction
-constexpr long long WAIT_LIMIT = 1ll << 26;  // bounded waits on the bulk-copy barrier
 constexpr int WALK_WARPS = 4;     // rows per CTA of the walk kernel
 constexpr int HLIST = 256;        // per-warp history ids kept for a recomputed region
 constexpr float DRAW_WINDOW = 1.0f / 16384.0f;
@@ -288,6 +290,11 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long *bar, uint32_t 
         : "memory");
     return ok != 0;
 }
+// Bounded wait for the phase of `bar` with the given parity: true when it completed within
+// `limit` polls, false when the wait gave up (the caller records ROW_ERR_TIMEOUT and goes on).
+template <bool CLUSTER>
+__device__ __noinline__ bool bounded_wait_slow(unsigned long long *bar, uint32_t parity, long long limit);
+
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, unsigned long long *bar) {
     asm volatile(
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -329,6 +336,20 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(unsigned long long *bar, u
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+template <bool CLUSTER>
+__device__ __noinline__ bool bounded_wait_slow(unsigned long long *bar, uint32_t parity, long long limit) {
+    for (long long it = 0;;) {
+        if (CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+        if (++it > limit) return false;
+    }
+}
+// the first poll inline (the common case: the phase is already complete), the loop out of line
+template <bool CLUSTER>
+__device__ __forceinline__ bool bounded_wait(unsigned long long *bar, uint32_t parity, long long limit) {
+    if (CLUSTER ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    return bounded_wait_slow<CLUSTER>(bar, parity, limit);
 }
 
 // Cluster barrier without release/acquire semantics: execution ordering only, so it does not wait
@@ -1076,14 +1097,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
     // tid, then every thread waits (bounded) for the C payloads addressed to this CTA.
     auto xwait = [&](int k, int par) -> bool {
         const uint32_t bit = 1u << (2 * k + par);
-        long long it2 = 0;
-        bool ok = true;
-        while (!mbar_try_wait_cluster(&sh.xbar[k][par], (xph & bit) ? 1u : 0u)) {
-            if (++it2 > WAIT_LIMIT) {
-                ok = false;
-                break;
-            }
-        }
+        const bool ok = bounded_wait<true>(&sh.xbar[k][par], (xph & bit) ? 1u : 0u, a.wait_limit);
         xph ^= bit;
         return ok;
     };
@@ -1224,13 +1238,13 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
         for (int i = slen + tid; i < S; i += NT) vals[i] = -INFINITY;
         if (use_tma) {
-            long long it = 0;
-            while (!mbar_try_wait(&sh.tma_bar[buf], phase)) {
-                if (++it > WAIT_LIMIT) {
-                    flags |= ROW_ERR_TIMEOUT;
-                    break;
-                }
-            }
+            if (!bounded_wait<false>(&sh.tma_bar[buf], phase, a.wait_limit)) flags |= ROW_ERR_TIMEOUT;
+            // test hook (off unless a test asks): on the cluster's first row, CTA 0 also waits for
+            // the barrier's next phase, which nothing completes, so the wait runs out with no
+            // copy in flight
+            if (a.fault_site == FAULT_COPY_WAIT && it == 0 && rank == 0 &&
+                !bounded_wait<false>(&sh.tma_bar[buf], phase ^ 1u, a.wait_limit))
+                flags |= ROW_ERR_TIMEOUT;
         }
         if (flags) atomicOr(&sh.bcast_i[2], flags);
         __syncthreads();
@@ -1309,7 +1323,12 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
         if (tid < C) push8(&sh.in1[par][rank], &sh.xbar[0][par], tid, __float_as_uint(lm), (uint32_t)flags);
         mark(DBG_P1);
-        const bool to1 = !xwait(0, par);  // ---- #1
+        bool to1 = !xwait(0, par);  // ---- #1
+        // test hook (off unless a test asks): on the cluster's first row, the last CTA also waits
+        // for exchange #1's next phase, which nothing completes before this CTA moves on
+        if (a.fault_site == FAULT_EXCHANGE_WAIT && it == 0 && rank == C - 1 &&
+            !bounded_wait<true>(&sh.xbar[0][par], (xph & (1u << par)) ? 1u : 0u, a.wait_limit))
+            to1 = true;
         mark(DBG_W1);
         float M = -INFINITY;
         int rowflags = 0;
@@ -1356,6 +1375,14 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 for (int i = tid; i < p.top_k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = i + a.vocab_offset;
         } else if (topk) {
             // ---------------- top-k ----------------------------------------------------------
+            {
+                // a NaN logit: the reference's -ffast-math build leaves its place in the sorted
+                // list undefined, so the row is flagged (each CTA for its slice; the walk kernel
+                // ORs the CTAs' bits into the status)
+                bool nanf = false;
+                for (int i = tid; i < slen; i += NT) nanf |= isnan(vals[i]);
+                if (__syncthreads_or(nanf)) rowflags |= ROW_ERR_NONFINITE;
+            }
             const int k = p.top_k;
             int kp2 = 1;
             while (kp2 < k) kp2 <<= 1;
@@ -1600,9 +1627,6 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                     for (int i = tid; i < k; i += NT) a.topk_ids[(int64_t)row * a.topk_stride + i] = il[i] + a.vocab_offset;
                 if (wid == 0) {
                     float *pr = a.probs ? a.probs + (int64_t)row * a.probs_stride : nullptr;
-                    // a NaN logit sorts first (its key is the largest); the reference's order of
-                    // NaNs in its insertion sort is not defined by its -ffast-math build
-                    if (isnan(tl[0])) rowflags |= ROW_ERR_NONFINITE;
                     token = sample_sorted_list(tl, il, k, p, r, pr, (a.flags & DLLM_MODE_MINP_RELATIVE) != 0);
                 }
             }
@@ -2151,6 +2175,8 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             hdr->done = 1;
         }
         mark(DBG_TOPK);
+        // the status bits this CTA saw; the walk kernel ORs every CTA's into the row's status
+        if (tid == 0) hdr->rank_flags[rank] = rowflags;
         fence_proxy_async();    // order this row's generic accesses of the slice before the next bulk copy
         cluster_sync_relaxed();  // ---- end of row: peers may reuse their shared memory
         if (dbuf && tid == 0 && use_tma && row + 2 * ncl < a.rows) issue_row_copy(row + 2 * ncl, buf);
@@ -2172,7 +2198,12 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
     __syncthreads();
     if (row >= a.rows) return;
     const RowHdr h = *row_hdr(a, row);
-    if (h.done) return;
+    int cl_flags = 0;  // status bits of the row's other CTAs (a bounded wait that ran out)
+    for (int c = 0; c < a.cluster; c++) cl_flags |= h.rank_flags[c];
+    if (h.done) {
+        if (lane == 0 && a.status && cl_flags) a.status[row] |= cl_flags;
+        return;
+    }
     const long long t_start = clock64();
     // the row's warp records and used stash slots -> shared memory, all copies in flight at once
     const size_t recb = ((size_t)a.nrec * sizeof(WRec) + 127) & ~(size_t)127;
@@ -2405,7 +2436,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
         res = walk_records(n, tyw, ep, wl.p0, wl.p1, cb, r, 1 << 12, expandA0);
     }
     if (lane == 0) {
-        int flags = h.flags;
+        int flags = h.flags | cl_flags;
         if (res == -2) flags |= ROW_ERR_WALK;
         a.token[row] = (res >= 0 ? res : h.last_idx) + a.vocab_offset;
         if (a.status) a.status[row] = flags;

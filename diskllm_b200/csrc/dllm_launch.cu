@@ -3,6 +3,10 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <mutex>
+#include <utility>
+#include <vector>
+
 #include "dllm_kernel.cuh"
 
 namespace dllm {
@@ -40,10 +44,59 @@ static size_t union_bytes(int htab, int cand_entries) {
 
 int nrec_for(const LaunchCfg &cfg) { return 4 * (cfg.threads / 32) * cfg.cluster; }
 
-static cudaError_t set_attrs(KernelFn fn, size_t smem) {
-    cudaError_t e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+// Function attributes, set once per (device, kernel): the largest dynamic shared memory the
+// device allows the kernel (a launch still asks only for what it uses) and cluster sizes above 8.
+namespace {
+std::mutex g_attr_mu;
+std::vector<std::pair<int, const void *>> g_attr_done;
+}  // namespace
+
+static cudaError_t set_attrs(KernelFn fn, size_t smem, bool cluster = true) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    return cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    for (auto &d : g_attr_done)
+        if (d.first == dev && d.second == (const void *)fn) return cudaSuccess;
+    int optin = 0;
+    e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, (const void *)fn);
+    if (e != cudaSuccess) return e;
+    // the dynamic part may use what the kernel's static shared memory leaves of the block limit
+    const int dyn_max = optin - (int)fa.sharedSizeBytes;
+    if (dyn_max < 0 || (size_t)dyn_max < smem) return cudaErrorInvalidValue;
+    e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn_max);
+    if (e != cudaSuccess) return e;
+    if (cluster) {
+        e = cudaFuncSetAttribute((const void *)fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+    }
+    g_attr_done.push_back({dev, (const void *)fn});
+    return cudaSuccess;
+}
+
+// Environment switches, read once per process.
+static bool no_idx_variant() {
+    static const bool v = getenv("DLLM_NO_IDX_VARIANT") != nullptr;
+    return v;
+}
+static int dbg_rank_env() {
+    static const int v = getenv("DLLM_DBG_RANK") ? atoi(getenv("DLLM_DBG_RANK")) : 0;
+    return v;
+}
+
+// Test hook: the bounded wait that the next launches make run out (FAULT_NONE = none).
+static int g_fault_site = FAULT_NONE;
+static long long g_fault_limit = WAIT_LIMIT;
+
+dllm_status set_fault_injection(int site, long long polls) {
+    if (site < FAULT_NONE || site > FAULT_EXCHANGE_WAIT || (site != FAULT_NONE && polls < 1))
+        return DLLM_ERR_INVALID_ARG;
+    g_fault_site = site;
+    g_fault_limit = site == FAULT_NONE ? WAIT_LIMIT : polls;
+    return DLLM_OK;
 }
 
 static int active_clusters(KernelFn fn, int C, int NT, size_t smem) {
@@ -179,8 +232,7 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     // min-p): the variant without the other paths' code
     const dllm_sampler_params &bp = a.bparams;
     const bool idx_only = !a.rparams && a.dtype == DLLM_DTYPE_F32 && bp.temperature > 0.0f &&
-                          !(bp.top_k > 0 && bp.top_k < a.vocab_total) && !(bp.min_p > 0.0f) &&
-                          !getenv("DLLM_NO_IDX_VARIANT");
+                          !(bp.top_k > 0 && bp.top_k < a.vocab_total) && !(bp.min_p > 0.0f) && !no_idx_variant();
     if (idx_only) {
         KernelFn fi = kernel_for(a.dtype, cfg.SUB, 2);
         if (fi) fn = fi;
@@ -203,9 +255,9 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     lc.numAttrs = 1;
     KernelArgs args = a;
     args.dbg = g_host_dbg;
-    args.dbg_rank = 0;
-    if (g_host_dbg)
-        if (const char *e = getenv("DLLM_DBG_RANK")) args.dbg_rank = atoi(e);
+    args.dbg_rank = g_host_dbg ? dbg_rank_env() : 0;
+    args.fault_site = g_fault_site;
+    args.wait_limit = g_fault_limit;
     if (g_ev_before) cudaEventRecord(g_ev_before, stream);
     e = cudaLaunchKernelEx(&lc, fn, args);
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
@@ -213,7 +265,7 @@ dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_
     // the walk kernel: one warp per row, after the cluster kernel on the same stream
     const int wb = (a.rows + WALK_WARPS - 1) / WALK_WARPS;
     const size_t wsmem = (size_t)WALK_WARPS * walk_smem_per_warp(a.nrec);
-    e = cudaFuncSetAttribute((const void *)fnb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsmem);
+    e = set_attrs(fnb, wsmem, false);
     if (e != cudaSuccess) return DLLM_ERR_CUDA;
     fnb<<<wb, WALK_WARPS * 32, wsmem, stream>>>(args);
     e = cudaGetLastError();

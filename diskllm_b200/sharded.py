@@ -17,6 +17,15 @@ import torch.distributed as dist
 from . import capi
 
 
+def _all_gather(out: torch.Tensor, inp: torch.Tensor, group) -> None:
+    """all_gather_into_tensor that reports a failed exchange (a rank that died, a timed-out or
+    aborted communicator) as a DllmError instead of the backend's exception type."""
+    try:
+        dist.all_gather_into_tensor(out, inp, group=group)
+    except Exception as e:  # the backends raise RuntimeError / DistBackendError subclasses
+        raise capi.DllmError(f"all-gather of shard candidates failed: {e}") from e
+
+
 def gather_candidates(vals: torch.Tensor, ids: torch.Tensor, group=None) -> tuple[torch.Tensor, torch.Tensor]:
     """All-gathers this rank's [rows][k] candidates into [world][rows][k] (rank order)."""
     world = dist.get_world_size(group)
@@ -24,8 +33,8 @@ def gather_candidates(vals: torch.Tensor, ids: torch.Tensor, group=None) -> tupl
     # concatenated along rows (the layout every backend accepts), viewed as [world][rows][k]
     out_v = torch.empty((world * rows, k), dtype=vals.dtype, device=vals.device)
     out_i = torch.empty((world * rows, k), dtype=ids.dtype, device=ids.device)
-    dist.all_gather_into_tensor(out_v, vals.contiguous(), group=group)
-    dist.all_gather_into_tensor(out_i, ids.contiguous(), group=group)
+    _all_gather(out_v, vals.contiguous(), group)
+    _all_gather(out_i, ids.contiguous(), group)
     return out_v.view(world, rows, k), out_i.view(world, rows, k)
 
 
@@ -41,7 +50,7 @@ def gather_packed(buf: torch.Tensor, rows: int, k: int, group=None) -> tuple[tor
     [world][rows][k] float32 and ids [world][rows][k] int32, contiguous, in rank order."""
     world = dist.get_world_size(group)
     allb = torch.empty(world * 2 * rows * k, dtype=torch.int32, device=buf.device)
-    dist.all_gather_into_tensor(allb, buf, group=group)
+    _all_gather(allb, buf, group)
     allb = allb.view(world, 2, rows, k)
     return allb[:, 0].contiguous().view(torch.float32), allb[:, 1].contiguous()
 

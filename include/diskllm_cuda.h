@@ -168,6 +168,21 @@ DLLM_API dllm_status dllm_cuda_sample_batch_static(const dllm_batch_desc *desc, 
  * statistics into it; NULL switches it off.  No effect on results. */
 DLLM_API dllm_status dllm_cuda_set_debug_counters(unsigned long long *device_counters);
 
+/* Test hooks for failure detection (no counterpart in the reference).  Both are off by default
+ * and change nothing while off.
+ *   dllm_cuda_debug_inject_wait_timeout(site, polls): from the next sampling launch on, the
+ *     cluster kernel adds, on each cluster's first row, one bounded wait that nothing completes
+ *     (site 1: CTA 0 waits for its slice barrier's next phase after the bulk copy landed; site 2:
+ *     the last CTA waits for exchange #1's next phase after the exchange completed), giving up
+ *     after `polls` polls instead of about a second.  No copy or store is in flight to the waited
+ *     barrier, so the kernel goes on and the row's status gets DLLM_ROW_ERR_TIMEOUT.  Site 0
+ *     switches it off.
+ *   dllm_cuda_debug_fail_allocations(count): the next `count` device allocations the library
+ *     makes for its own buffers fail as if cudaMalloc had run out of memory, so the calls that
+ *     needed them return DLLM_ERR_OOM. */
+DLLM_API dllm_status dllm_cuda_debug_inject_wait_timeout(int site, long long polls);
+DLLM_API dllm_status dllm_cuda_debug_fail_allocations(int count);
+
 /* Vocabulary-sharded sampling (a row's logits split over N GPUs, as a tensor-parallel LM head
  * leaves them).  No counterpart in the reference, whose sampler sees whole rows; together the
  * two calls and one all-gather give the tokens sampler_sample would (src/sampler.c:136-234)
