@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdiskllm_cuda.so")
 
 SUB_LENGTHS = [4, 12, 20, 28, 36, 44, 52, 60]
-UNITS = [("dllm_launch.cu", []), ("dllm_capi.cu", []), ("dllm_noalloc.cu", []), ("dllm_shard.cu", []), ("dllm_grammar.cu", []), ("dllm_lmhead.cu", []), ("dllm_sorted.cu", [])] + [
+UNITS = [("dllm_launch.cu", []), ("dllm_capi.cu", []), ("dllm_noalloc.cu", []), ("dllm_shard.cu", []), ("dllm_grammar.cu", []), ("dllm_lmhead.cu", []), ("dllm_sorted.cu", []), ("dllm_largek.cu", [])] + [
     ("dllm_kernel_inst.cu", [f"-DDLLM_SUB={s}"]) for s in SUB_LENGTHS
 ]
 SOURCES = sorted({u[0] for u in UNITS})

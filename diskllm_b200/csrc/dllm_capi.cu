@@ -262,61 +262,81 @@ extern "C" dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, cons
 static int topk_bound(const dllm_batch_desc *d) {
     int topk_max = d->row_params ? d->topk_max : d->params.top_k;
     if (topk_max >= d->vocab || topk_max < 0) topk_max = 0;
+    if (!d->row_params && d->params.temperature == 0.0f) topk_max = 0;  // greedy ignores top-k
     return topk_max;
 }
 
-// Which kernels a descriptor runs: the fused sampler, the sorted-nucleus passes, or both (per-row
-// parameters under the sorted flag: the fused kernel samples every row, then the sorted passes
-// resample the rows with top-k off and temperature > 0).
-static void plan(const dllm_batch_desc *d, bool *fused, bool *sorted) {
-    *sorted = (d->flags & DLLM_MODE_TOPP_SORTED) != 0;
-    *fused = true;
-    if (*sorted && !d->row_params) {
+// Which kernels a descriptor runs: the fused sampler, the sorted-nucleus passes, the large-k pass,
+// or a combination.  Per-row parameters under the sorted flag: the fused kernel samples every
+// row, then the sorted passes resample the rows with top-k off and temperature > 0.  Top-k above
+// the fused kernel's list capacity (KMAX): the large-k pass samples those rows (all of them for
+// broadcast parameters; after the fused kernel, the rows whose own top_k exceeds KMAX, for
+// per-row parameters).
+struct Plan {
+    bool fused, sorted, large;
+    int fused_topk;  // top-k bound the fused kernel is configured for
+};
+
+static Plan plan(const dllm_batch_desc *d) {
+    Plan pl;
+    pl.sorted = (d->flags & DLLM_MODE_TOPP_SORTED) != 0;
+    pl.fused = true;
+    if (pl.sorted && !d->row_params) {
         const dllm_sampler_params &p = d->params;
         const bool eligible = p.temperature > 0.0f && !(p.top_k > 0 && p.top_k < d->vocab);
-        *fused = !eligible;
-        *sorted = eligible;
+        pl.fused = !eligible;
+        pl.sorted = eligible;
     }
+    const int tk = topk_bound(d);
+    pl.large = tk > KMAX;
+    if (pl.large && !d->row_params) pl.fused = false;
+    pl.fused_topk = tk > KMAX ? KMAX : tk;
+    return pl;
 }
 
-static size_t sorted_offset(size_t fused_bytes) { return (fused_bytes + 255) & ~(size_t)255; }
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Workspace layout: [fused kernel rows][sorted-nucleus passes][large-k pass], each 256-aligned.
+struct WsLayout {
+    size_t fused, sorted_off, large_off, total;
+};
+
+static dllm_status ws_layout(const dllm_batch_desc *d, const Plan &pl, LaunchCfg *cfg, WsLayout *out) {
+    WsLayout L = {};
+    if (pl.fused) {
+        const dllm_status st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, pl.fused_topk, cfg);
+        if (st != DLLM_OK) return st;
+        L.fused = (size_t)d->rows * row_ws_bytes(nrec_for(*cfg), cfg->SUB);
+    }
+    L.sorted_off = al256(L.fused);
+    L.large_off = al256(L.sorted_off + (pl.sorted ? sorted_ws_bytes(d->rows, d->vocab) : 0));
+    L.total = L.large_off + (pl.large ? largek_ws_bytes(d->rows, d->vocab) : 0);
+    *out = L;
+    return DLLM_OK;
+}
 
 extern "C" size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *d) {
     if (validate(d) != DLLM_OK || d->rows == 0) return 0;
-    bool fused, sorted;
-    plan(d, &fused, &sorted);
-    size_t bytes = 0;
-    if (fused) {
-        const int tk = topk_bound(d);
-        if (tk > KMAX) return 0;
-        LaunchCfg cfg;
-        if (get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, tk, &cfg) != DLLM_OK) return 0;
-        bytes = (size_t)d->rows * row_ws_bytes(nrec_for(cfg), cfg.SUB);
-    }
-    if (sorted) bytes = sorted_offset(bytes) + sorted_ws_bytes(d->rows, d->vocab);
-    return bytes;
+    const Plan pl = plan(d);
+    LaunchCfg cfg;
+    WsLayout L;
+    if (ws_layout(d, pl, &cfg, &L) != DLLM_OK) return 0;
+    return L.total;
 }
 
 extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *stream) {
     dllm_status st = validate(d);
     if (st != DLLM_OK) return st;
     if (d->rows == 0) return DLLM_OK;
-    bool fused, sorted;
-    plan(d, &fused, &sorted);
-    const int topk_max = topk_bound(d);
-    if (fused && topk_max > KMAX) return DLLM_ERR_UNSUPPORTED;
+    const Plan pl = plan(d);
+    const bool fused = pl.fused, sorted = pl.sorted;
 
     LaunchCfg cfg = {};
-    int nrec = 0;
-    size_t ws_need = 0;
-    if (fused) {
-        st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, topk_max, &cfg);
-        if (st != DLLM_OK) return st;
-        nrec = nrec_for(cfg);
-        ws_need = (size_t)d->rows * row_ws_bytes(nrec, cfg.SUB);
-    }
-    const size_t fused_bytes = ws_need;
-    if (sorted) ws_need = sorted_offset(fused_bytes) + sorted_ws_bytes(d->rows, d->vocab);
+    WsLayout L;
+    st = ws_layout(d, pl, &cfg, &L);
+    if (st != DLLM_OK) return st;
+    const int nrec = fused ? nrec_for(cfg) : 0;
+    const size_t ws_need = L.total;
     void *ws = d->workspace;
     if (ws) {
         if (d->workspace_bytes < ws_need) return DLLM_ERR_INVALID_ARG;
@@ -370,8 +390,13 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
         }
     }
     if (sorted) {
-        st = launch_sorted(d, fused, (unsigned char *)ws + sorted_offset(fused_bytes), (cudaStream_t)stream);
+        st = launch_sorted(d, fused, (unsigned char *)ws + L.sorted_off, (cudaStream_t)stream);
         if (st == DLLM_ERR_CUDA) set_error("sorted-nucleus kernel launch", cudaGetLastError());
+        if (st != DLLM_OK) return st;
+    }
+    if (pl.large) {
+        st = launch_largek(d, fused, (unsigned char *)ws + L.large_off, (cudaStream_t)stream);
+        if (st == DLLM_ERR_CUDA) set_error("large top-k pass launch", cudaGetLastError());
     }
     return st;
 }

@@ -13,7 +13,7 @@ namespace dllm {
 enum : int32_t {
     ROW_ERR_HIST_TABLE = 1,   // more distinct in-slice history ids than the table holds
     ROW_ERR_NONFINITE  = 2,   // a NaN among a top-k row's candidates (order undefined in the reference)
-    ROW_ERR_TOPK_LARGE = 4,   // top_k above the kernel's candidate capacity
+    ROW_ERR_TOPK_LARGE = 4,   // top_k above the list capacity (fused kernel: the large-k pass takes the row over)
     ROW_ERR_WALK       = 8,   // internal consistency check of the draw walk failed
     ROW_ERR_TIMEOUT    = 16,  // a bounded wait on a bulk copy expired
     ROW_TOPP_EDGE      = 32,  // information, not an error: see DLLM_ROW_TOPP_EDGE
@@ -108,6 +108,8 @@ dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
 dllm_status set_fault_injection(int site, long long polls);
 size_t shard_part_bytes(int rows, int vlocal, int k);
 size_t sorted_ws_bytes(int rows, int vocab);
+size_t largek_ws_bytes(int rows, int vocab);
+dllm_status launch_largek(const dllm_batch_desc *d, bool after_fused, void *ws, cudaStream_t stream);
 dllm_status launch_sorted(const dllm_batch_desc *d, bool after_fused, void *ws, cudaStream_t stream);
 int lmh_max_rows(int hidden);
 dllm_status launch_lmhead(int rows, int hidden, int vocab, const float *h, const float *norm_w, float eps, int add_one,

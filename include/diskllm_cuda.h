@@ -96,7 +96,9 @@ typedef struct {
 
     dllm_sampler_params params;            /* host value, used for every row ... */
     const dllm_sampler_params *row_params; /* ... unless this device array is given */
-    int topk_max;             /* upper bound on top_k over rows when row_params is given */
+    int topk_max;             /* upper bound on top_k over rows when row_params is given.
+                                 Any top_k works (as in the reference, src/sampler.c:165-170);
+                                 rows with top_k above 1024 take a slower sort-based pass */
 
     unsigned flags;           /* DLLM_MODE_* */
 
@@ -124,7 +126,8 @@ typedef struct {
                                        -ffast-math build leaves its order undefined.  (Rows with
                                        +inf, all-NaN rows and NaN rows with top-k off get the
                                        reference's id: its list's last entry) */
-#define DLLM_ROW_ERR_TOPK_LARGE 4   /* top_k above the kernel's candidate capacity */
+#define DLLM_ROW_ERR_TOPK_LARGE 4   /* a top_k dllm_cuda_merge_sample cannot serve (above its
+                                       gathered k); whole-row calls serve every top_k */
 #define DLLM_ROW_ERR_WALK       8   /* internal consistency check of the draw failed */
 #define DLLM_ROW_ERR_TIMEOUT   16   /* a bounded wait on a bulk copy expired */
 #define DLLM_ROW_TOPP_EDGE     32   /* information, not an error: the index-order top-p prefix
@@ -144,8 +147,10 @@ typedef struct {
  * Row i draws with uniforms[i] where the reference draws rand_f32 (src/sampler.c:225). */
 DLLM_API dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *desc, void *stream);
 
-/* Scratch the sampler needs for this descriptor (per-row headers, warp-level draw
- * records and stashed probabilities; about 16 KB per row).  0 on invalid descriptors. */
+/* Scratch the sampler needs for this descriptor: per-row headers, warp-level draw records and
+ * stashed probabilities (the size depends on the vocabulary's launch configuration: about 30 KB
+ * per row at vocab 256000), plus the sorted-nucleus passes' and the large-top-k pass's buffers
+ * when the descriptor uses them.  0 on invalid descriptors. */
 DLLM_API size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *desc);
 
 /* Allocation-free variant of dllm_cuda_sample_batch; it has no counterpart in the reference.
@@ -157,7 +162,8 @@ DLLM_API size_t dllm_cuda_workspace_bytes(const dllm_batch_desc *desc);
  * dllm_cuda_workspace_bytes() exceeds 16 MiB (about 550 rows of vocab 256000) are rejected
  * with DLLM_ERR_UNSUPPORTED and a message in dllm_cuda_last_error().  The first call on a
  * device looks up the array's device address and picks the launch configuration, so make it
- * before any stream capture.  Every call shares the one array: calls whose work overlaps on the
+ * before any stream capture.  The address is kept for the life of the process: after a
+ * cudaDeviceReset of a device this entry point must not be called on it again.  Every call shares the one array: calls whose work overlaps on the
  * GPU (other streams, other host threads) race and must be serialised by the caller.  The
  * kernels write every scratch field before reading it, so leftover contents from an earlier
  * call need no clearing. */

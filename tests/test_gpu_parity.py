@@ -138,6 +138,7 @@ PARAM_SETS = {
     "topp_zero": dict(temperature=1.0, top_k=0, top_p=0.0),
     "k3": dict(temperature=0.5, top_k=3, top_p=1.0),
     "k_big": dict(temperature=1.1, top_k=700, top_p=0.97),
+    "k_huge": dict(temperature=0.9, top_k=3000, top_p=0.95, min_p=1e-5),  # above the fused list
     "k_ge_V": dict(temperature=2.0, top_k=10 ** 7, top_p=0.5),
     "hot": dict(temperature=3.0, top_k=0, top_p=0.999, presence=0.4, frequency=0.1),
 }
@@ -365,7 +366,7 @@ def test_every_row_of_benchmark_batch(cfg):
     print(f"config {cfg} full batch: {stats}")
 
 
-@pytest.mark.parametrize("k", [0, 40])
+@pytest.mark.parametrize("k", [0, 40, 2000])
 def test_nonfinite_rows_follow_the_reference(k):
     """+inf logits (one or several, or alone among -inf), all-NaN rows and NaN rows with top-k
     off: the reference's sums turn NaN and its draw returns its list's last entry (the oracle is
@@ -393,3 +394,49 @@ def test_nonfinite_rows_follow_the_reference(k):
             continue
         assert tok[i] == ora.token[i], (i, tok[i], ora.token[i])
         assert st[i] & ~capi.ROW_TOPP_EDGE == 0, (i, st[i])
+
+
+def test_per_row_top_k_above_and_below_the_fused_list():
+    """per-row parameters mixing top-k off, small k, and k above the fused kernel's list
+    capacity (those rows take the large-k pass after the fused kernel)"""
+    from diskllm_b200 import capi
+
+    rng = np.random.default_rng(31)
+    rows, V = 8, 9000
+    lg = (rng.standard_normal((rows, V)) * 1.5).astype(np.float32)
+    hist = [rng.integers(0, V, 50) for _ in range(rows)]
+    u = u24(rng, rows)
+    ks = [3, 1500, 0, 40, 5000, 8999, 1025, 0]
+    per_row = [dict(temperature=0.8 + 0.05 * i, top_k=k, top_p=0.93, repetition=1.1) for i, k in enumerate(ks)]
+    dev = "cuda"
+    ids, off = csr(hist)
+    st = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+    probs = torch.full((rows, V), -1.0, device=dev)
+    tok = capi.sample_batch(torch.from_numpy(lg).to(dev), torch.from_numpy(u).to(dev), per_row[0],
+                            row_params=capi.params_array(per_row, dev), topk_max=max(ks),
+                            hist_ids=torch.from_numpy(ids).to(dev), hist_off=torch.from_numpy(off).to(dev),
+                            status=st, probs=probs)
+    torch.cuda.synchronize()
+    tok, st, probs = tok.cpu().numpy(), st.cpu().numpy(), probs.cpu().numpy()
+    assert np.all((st & ~capi.ROW_TOPP_EDGE) == 0), st
+    for i in range(rows):
+        ora = O.sample_restated(lg[i:i + 1], per_row[i], u[i:i + 1], hist=[hist[i]], kept_cap=V)
+        assert ids_match(int(tok[i]), ora, u[i:i + 1], 0), (i, ks[i], tok[i], ora.token[0])
+        if ks[i] > 0:
+            d = np.abs(probs[i].astype(np.float64) - dense_probs(ora, 0, V))
+            assert d.max() <= TOL_PROB, (i, d.max())
+
+
+def test_drop_in_sampler_with_top_k_above_the_fused_list():
+    """the reference accepts any 0 < top_k < vocab (src/sampler.c:165-170); so does the drop-in"""
+    from diskllm_b200 import capi
+
+    rng = np.random.default_rng(32)
+    V = 20000
+    s = capi.Sampler(temperature=0.9, top_k=4000, top_p=0.9, seed=77)
+    us = O.xorshift_uniforms(77, 4)
+    for i in range(4):
+        row = (rng.standard_normal(V) * 1.2).astype(np.float32)
+        tok = s.sample(row)
+        ora = O.sample_restated(row[None], dict(temperature=0.9, top_k=4000, top_p=0.9), us[i:i + 1], kept_cap=V)
+        assert ids_match(tok, ora, us[i:i + 1], 0)
