@@ -402,30 +402,27 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
 }
 
 // ----------------------------------------------------------------------------------------
-// history penalty kernel for the host-pointer drop-ins (src/sampler.c:21-52): one CTA,
-// thread i owns history entry i; the first occurrence of each id applies the penalty.
+// history penalty kernel for the host-pointer drop-ins (src/sampler.c:21-52).  Sparse: the host
+// gathers the logits of the n history entries, the kernel computes each entry's penalised value
+// (every occurrence of an id gets the same value: its logit after the penalty, applied once per
+// id for presence and once per occurrence for repetition), and the host writes them back.  Only
+// 8 bytes per history entry cross PCIe each way, not the row.
 
-__global__ void penalty_kernel(float *logits, int vocab, const int *seen, int n, float value, int mode) {
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+__global__ void penalty_kernel(const float *vals, float *out, const int *seen, int n, int vocab, float value,
+                               int mode) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
         const int id = seen[i];
         if (id < 0 || id >= vocab) continue;
-        bool first = true;
-        int count = 1;
-        for (int j = 0; j < i; j++)
-            if (seen[j] == id) {
-                first = false;
-                break;
-            }
-        if (!first) continue;
-        for (int j = i + 1; j < n; j++) count += seen[j] == id;
-        float v = logits[id];
+        int count = 0;
+        for (int j = 0; j < n; j++) count += seen[j] == id;
+        float v = vals[i];
         if (mode == 0) {  // repetition, once per occurrence
             const float inv = __fdiv_rn(1.0f, value);
             for (int k = 0; k < count; k++) v = v < 0.0f ? __fmul_rn(v, value) : __fmul_rn(v, inv);
         } else {          // presence, once per id
             v = __fsub_rn(v, value);
         }
-        logits[id] = v;
+        out[i] = v;
     }
 }
 
@@ -567,13 +564,18 @@ extern "C" int greedy_sample(const float *logits, int vocab_size) {
 
 static void apply_penalty(float *logits, int vocab, const int *seen, int n, float value, int mode) {
     DevBuf &b = t_free_buf;
-    buf_reserve(b, vocab, n);
-    DLLM_CHECK(cudaMemcpyAsync(b.row, logits, sizeof(float) * (size_t)vocab, cudaMemcpyHostToDevice, b.stream));
+    buf_reserve(b, 2 * n, n);
+    std::vector<float> vals((size_t)n, 0.0f);
+    for (int i = 0; i < n; i++)
+        if (seen[i] >= 0 && seen[i] < vocab) vals[i] = logits[seen[i]];
+    DLLM_CHECK(cudaMemcpyAsync(b.row, vals.data(), sizeof(float) * (size_t)n, cudaMemcpyHostToDevice, b.stream));
     DLLM_CHECK(cudaMemcpyAsync(b.ids, seen, sizeof(int) * (size_t)n, cudaMemcpyHostToDevice, b.stream));
-    penalty_kernel<<<1, 1024, 0, b.stream>>>(b.row, vocab, b.ids, n, value, mode);
+    penalty_kernel<<<(n + 255) / 256, 256, 0, b.stream>>>(b.row, b.row + n, b.ids, n, vocab, value, mode);
     DLLM_CHECK(cudaGetLastError());
-    DLLM_CHECK(cudaMemcpyAsync(logits, b.row, sizeof(float) * (size_t)vocab, cudaMemcpyDeviceToHost, b.stream));
+    DLLM_CHECK(cudaMemcpyAsync(vals.data(), b.row + n, sizeof(float) * (size_t)n, cudaMemcpyDeviceToHost, b.stream));
     DLLM_CHECK(cudaStreamSynchronize(b.stream));
+    for (int i = 0; i < n; i++)
+        if (seen[i] >= 0 && seen[i] < vocab) logits[seen[i]] = vals[i];
 }
 
 extern "C" void sampler_apply_repetition_penalty(float *logits, int vocab_size, const int *seen_tokens,
