@@ -9,8 +9,16 @@ of the fused kernel.  Inputs are 1.05 GB per GPU, larger than the 126 MB L2, so 
 needed between steps.  Multi-GPU: one process per GPU, rows sharded (each rank samples its
 own 1024-row batch; no collective on the data path) -> weak scaling.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-    python bench.py --workload cfg5 [--gpus N] ...   # vocabulary-sharded config 5 (strong scaling)
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extra]
+    python bench.py --workload cfg1|cfg2|cfg3|cfg5 [--gpus N] ...   # one configuration alone
+
+After the headline, the same run measures the other BASELINE configurations and adds them to the
+line under "configs": 1 (one sequence, 1000 dependent decode steps in a CUDA graph), 2 (64 x
+151936 with penalties, top-k 50), 3 (256 x 151936 JSON mask, index-order top-p), each with its
+roofline fraction and, at N = 1, the reference's own sampler timed on the host cores; and 5,
+vocabulary-sharded over the N ranks with the NCCL all-gather (strong scaling), with its step
+split into candidates, all-gather and merge.  Inputs that would fit twice in L2 are preceded by
+a 256 MB L2 flush outside each step's events.
 
 Config 5 (--workload cfg5): 512 rows x vocab 262144 bf16 N(0, 2^2), 10 % of ids allowed by the
 mask, repetition 1.1 over 128 ids, temperature 0.9, top-k 64, top-p 0.9; every GPU holds 1/N of
@@ -144,6 +152,74 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------------------
+# timing helpers for the per-configuration legs
+
+L2_FLUSH_BYTES = 256 << 20  # twice the 126 MB L2
+
+
+class L2Flush:
+    """Writes a buffer twice the size of L2 between timed steps whose inputs would fit in it."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.v = 0
+
+    def __call__(self):
+        self.v ^= 1
+        self.buf.fill_(self.v)
+
+
+def max_over_ranks(x, dev, world):
+    if world == 1:
+        return x
+    import torch
+
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def timed_steps(step, steps, dev, world, flush=None, kernel=False):
+    """CUDA events around each step (an L2 flush, when given, runs before the step and outside its
+    events).  Returns (mean ms per step, mean ms of the library's cluster kernel or None), each the
+    max over ranks."""
+    import torch
+
+    from diskllm_b200 import capi
+
+    stream = torch.cuda.current_stream(dev)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in ev + kev:
+        a.record(stream)
+        b.record(stream)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(steps):
+        if flush is not None:
+            flush()
+        if kernel:
+            capi.set_timing_events(*kev[i])
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    if kernel:
+        capi.set_timing_events(None, None)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    kms = sum(a.elapsed_time(b) for a, b in kev) / steps if kernel else None
+    ms = max_over_ranks(ms, dev, world)
+    if kernel:
+        kms = max_over_ranks(kms, dev, world)
+    return ms, kms
+
+
+# ----------------------------------------------------------------------------------------------
 # CPU baseline: DiskLLM's own sampler.c (oracle/_ref, as built) or the restated port
 
 def host_rows(n, seed=404):
@@ -184,11 +260,12 @@ def cpu_baseline(seconds=10.0):
 
 
 def run_reference(args, rank, world):
+    """DiskLLM's own sampler.c (oracle/_ref, as built) on the host cores, over the same
+    1024-row config-4 batch the GPU arm samples per step, one reference sampler per thread."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    per_step = max(64, 2 * threads)
-    lg, hist = host_rows(per_step)
+    lg, hist = host_rows(ROWS)
     kind = "port"
     for _ in range(args.warmup):
         cpu_run(lg, hist, threads)
@@ -196,7 +273,7 @@ def run_reference(args, rank, world):
     for _ in range(args.steps):
         s, kind = cpu_run(lg, hist, threads)
         tot += s
-    value = per_step * args.steps / tot
+    value = ROWS * args.steps / tot
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "rows/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
@@ -204,13 +281,26 @@ def run_reference(args, rank, world):
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,0.5^2) rows)",
         "config": config_block(args.gpus),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": kind,
-                         "sample": f"{per_step} rows of config 4 per step, {threads} threads"},
+                         "sample": f"the full {ROWS}-row config-4 batch per step, {threads} threads"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def run_ours(args, rank, world, dev):
+    line = headline_result(args, rank, world, dev)
+    if not args.no_extra:
+        import torch
+
+        torch.cuda.empty_cache()
+        extra = extra_configs(args, rank, world, dev)
+        if rank == 0:
+            line["configs"] = extra
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def headline_result(args, rank, world, dev):
     import torch
 
     from diskllm_b200 import capi
@@ -301,8 +391,10 @@ def run_ours(args, rank, world, dev):
         ms_e2e = float(t.item())
     e2e_rows_s = ROWS * world / (ms_e2e / e2e_steps / 1e3)
 
+    del d_logits, h_logits
+    w.logits = None
     if rank != 0:
-        return
+        return None
     value = ROWS * world / (ms_step / 1e3)
     peak, peak_kind = measured_peak()
     achieved = ROWS * algo_bytes_per_row() / (ms_kernel / 1e3) / 1e9
@@ -327,15 +419,22 @@ def run_ours(args, rank, world, dev):
     }
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(seconds=args.cpu_seconds)
-    print(json.dumps(line), flush=True)
+    return line
 
 
 CFG1_VOCAB, CFG1_STEPS, CFG1_RING = 128256, 1000, 8
 
 
 def run_cfg1(args, rank, world, dev):
+    line = cfg1_result(args, rank, world, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cfg1_result(args, rank, world, dev):
     """Config 1: one sequence, 1000 dependent steps (sample, append the id to the history the
-    next step penalises), replayed as one CUDA graph.  Reported as steps (rows) per second."""
+    next step penalises), replayed as one CUDA graph.  Reported as steps (rows) per second,
+    aggregated over the ranks (each rank decodes its own sequence)."""
     import numpy as np
     import torch
 
@@ -364,7 +463,7 @@ def run_cfg1(args, rank, world, dev):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     clocks.stop()
-    us_step = e0.elapsed_time(e1) * 1e3 / (reps * CFG1_STEPS)
+    us_step = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (reps * CFG1_STEPS), dev, world)
     # the same steps launched one by one from the host
     e0.record(stream)
     loop.run_eager()
@@ -383,13 +482,14 @@ def run_cfg1(args, rank, world, dev):
         h_tok.copy_(loop.tokens[i:i + 1], non_blocking=True)
     e1.record(stream)
     torch.cuda.synchronize(dev)
-    us_e2e = e0.elapsed_time(e1) * 1e3 / n_e2e
+    us_e2e = max_over_ranks(e0.elapsed_time(e1) * 1e3 / n_e2e, dev, world)
     if rank != 0:
-        return
+        return None
     bytes_step = CFG1_VOCAB * 4 + 64 * 4
     peak, peak_kind = measured_peak()
     line = {
-        "metric": METRIC, "value": 1e6 / us_step, "unit": "rows/s", "n_gpus": world, "steps": reps * CFG1_STEPS,
+        "metric": METRIC, "value": world * 1e6 / us_step, "unit": "rows/s", "n_gpus": world,
+        "steps": reps * CFG1_STEPS,
         "warmup": args.warmup, "ms_per_step": us_step / 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,2.5^2) row + 20 boosted ids, ring of 8 perturbed rows, Philox uniforms)",
@@ -402,12 +502,12 @@ def run_cfg1(args, rank, world, dev):
                      "unit": "GB/s", "frac": bytes_step / (us_step * 1e-6) / 1e9 / peak,
                      "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s", "traffic": None, "kernel": "one decode step (graph replay)"},
-        "e2e": {"value": 1e6 / us_e2e, "unit": "rows/s", "h2d_bytes_per_step": CFG1_VOCAB * 4,
+        "e2e": {"value": world * 1e6 / us_e2e, "unit": "rows/s", "h2d_bytes_per_step": CFG1_VOCAB * 4,
                 "d2h_bytes_per_step": 4},
         "gpu_launches": reps * CFG1_STEPS * 3,
         "clocks": clocks.summary(),
     }
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:
         # the reference's step on one host core, the same row and history
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         import oracle as O
@@ -415,7 +515,7 @@ def run_cfg1(args, rank, world, dev):
         lg = w.logits.cpu().numpy()
         hist = [w.hist_ids.cpu().numpy()]
         reps_cpu, tot, kind = 0, 0.0, "port"
-        while tot < args.cpu_seconds:
+        while tot < args.cpu_seconds / 3:
             if O.have_reference():
                 _, secs = O.sample_reference(lg, dict(w.params), hist=hist, threads=1, stream=True)
                 kind = "reference"
@@ -427,13 +527,22 @@ def run_cfg1(args, rank, world, dev):
             reps_cpu += 1
         line["cpu_baseline"] = {"value": reps_cpu / tot, "unit": "rows/s", "cores": 1, "kind": kind,
                                 "sample": f"{reps_cpu} single-row config 1 steps on one core"}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 CFG5_ROWS, CFG5_VOCAB, CFG5_HIST, CFG5_K = 512, 262144, 128, 64
 
 
 def run_cfg5(args, rank, world, dev):
+    line = cfg5_result(args, rank, world, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def cfg5_result(args, rank, world, dev):
+    """Config 5, vocabulary-sharded over the ranks: every GPU holds 1/N of the columns of all 512
+    rows; a step is the shard candidate kernel, the NCCL all-gather of the candidates and the
+    merge kernel (sharded.sample_vocab_sharded).  Strong scaling."""
     import torch
 
     from diskllm_b200 import capi, sharded
@@ -453,30 +562,39 @@ def run_cfg5(args, rank, world, dev):
 
     for _ in range(args.warmup):
         step()
+    shard_bytes = x.numel() * 2 + m.numel() * 4
+    flush = L2Flush(dev) if shard_bytes < 2 * 126e6 else None
+    steps = min(args.steps, 50)
+    clocks = ClockSampler(dev.index)
+    clocks.start()
+    ms_step, _ = timed_steps(step, steps, dev, world, flush)
+    clocks.stop()
 
-    def barrier():
+    # the three parts of a step, each timed with its own events (candidates, all-gather, merge)
+    stream = torch.cuda.current_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    parts = [0.0, 0.0, 0.0]
+    buf, vals, ids = sharded.candidate_buffer(CFG5_ROWS, CFG5_K, dev)
+    for _ in range(steps):
+        if flush is not None:
+            flush()
         if world > 1:
             torch.distributed.barrier()
+        ev[0].record(stream)
+        capi.shard_candidates(x, s, CFG5_VOCAB, CFG5_K, params, mask=m, hist_ids=w.hist_ids,
+                              hist_off=w.hist_off, hist_max=CFG5_HIST, out=(vals, ids))
+        ev[1].record(stream)
+        if world > 1:
+            all_v, all_i = sharded.gather_packed(buf, CFG5_ROWS, CFG5_K)
+        else:
+            all_v, all_i = vals.unsqueeze(0), ids.unsqueeze(0)
+        ev[2].record(stream)
+        capi.merge_sample(all_v, all_i, w.uniforms, params)
+        ev[3].record(stream)
         torch.cuda.synchronize(dev)
-
-    stream = torch.cuda.current_stream(dev)
-    clocks = ClockSampler(dev.index)
-    barrier()
-    clocks.start()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    barrier()
-    clocks.stop()
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
+        for j in range(3):
+            parts[j] += ev[j].elapsed_time(ev[j + 1]) / steps
+    parts = [max_over_ranks(v, dev, world) for v in parts]
 
     # end to end: this GPU's shard of the logits from pinned host memory, tokens back to the host
     h_x = x.cpu().pin_memory()
@@ -492,32 +610,35 @@ def run_cfg5(args, rank, world, dev):
     e2e_steps = max(3, min(args.steps, 20))
     for _ in range(2):
         e2e_step()
-    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
     e0.record(stream)
     for _ in range(e2e_steps):
         e2e_step()
     e1.record(stream)
-    barrier()
-    ms_e2e = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms_e2e], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_e2e = float(t.item())
+    torch.cuda.synchronize(dev)
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1), dev, world)
     if rank != 0:
-        return
+        return None
     cols = e - s
     bytes_per_gpu = CFG5_ROWS * (2 * cols + (cols + 7) // 8 + CFG5_HIST * 4)
     peak, peak_kind = measured_peak()
     achieved = bytes_per_gpu / (ms_step / 1e3) / 1e9
-    line = {
+    return {
         "metric": METRIC, "value": CFG5_ROWS / (ms_step / 1e3), "unit": "rows/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16 in, f32 arithmetic",
         "data": "synthetic (seeded N(0,2^2) bf16 rows, 10% mask, uniform histories, Philox uniforms)",
         "config": {"workload": "cfg5_vocab_parallel_b512_v262144_bf16 (BASELINE config 5)",
                    "global_batch": CFG5_ROWS, "vocab": CFG5_VOCAB, "columns_per_gpu": cols, "top_k_per_shard": CFG5_K,
                    "params": params, "parallelism": f"vocab-sharded x{world} (NCCL all-gather of candidates)",
-                   "l2_policy": "per-GPU shard may fit in L2 at N >= 2; no flush (step time includes the exchange)"},
+                   "l2_policy": ("L2 flushed (256 MB write) before each timed step: the shard is "
+                                 f"{shard_bytes / 1e6:.0f} MB") if flush is not None else
+                                f"shard ({shard_bytes / 1e6:.0f} MB) larger than twice the L2; no flush"},
+        "parts_ms": {"candidates": parts[0], "all_gather": parts[1], "merge": parts[2]},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
@@ -525,10 +646,101 @@ def run_cfg5(args, rank, world, dev):
                      "kernel": "shard_stream_kernel + all-gather + merge_sample_kernel (whole step)"},
         "e2e": {"value": CFG5_ROWS / (ms_e2e / e2e_steps / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": h_x.numel() * 2, "d2h_bytes_per_step": CFG5_ROWS * 4},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 2 * steps,
         "clocks": clocks.summary(),
     }
-    print(json.dumps(line), flush=True)
+
+
+BATCH_SEEDS = {2: 202, 3: 303}
+
+
+def batch_config_result(cfg, args, rank, world, dev):
+    """Configs 2 and 3: one batch per GPU (rows sharded, no collective), a step samples it."""
+    import numpy as np
+    import torch
+
+    from diskllm_b200 import capi
+    from diskllm_b200 import workloads as W
+
+    w = W.CONFIGS[cfg](device=dev, seed=BATCH_SEEDS[cfg] + rank)
+    kw = {}
+    if w.hist_ids is not None:
+        kw.update(hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=w.hist_max)
+    if w.mask is not None:
+        kw["mask"] = w.mask
+    tok = torch.empty(w.rows, dtype=torch.int32, device=dev)
+
+    def step():
+        capi.sample_batch(w.logits, w.uniforms, w.params, token=tok, **kw)
+
+    for _ in range(args.warmup):
+        step()
+    in_bytes = w.logits.numel() * w.logits.element_size() + (0 if w.mask is None else w.mask.numel() * 4)
+    flush = L2Flush(dev) if in_bytes < 2 * 126e6 else None
+    steps = min(args.steps, 50)
+    ms, kms = timed_steps(step, steps, dev, world, flush, kernel=True)
+    if rank != 0:
+        return None
+    algo = w.algo_bytes_per_row * w.rows
+    peak, peak_kind = measured_peak()
+    res = {"workload": f"{w.name} (BASELINE config {cfg})", "rows_per_gpu": w.rows, "vocab": w.vocab,
+           "params": dict(w.params), "steps": steps, "ms_per_step": ms, "value": w.rows * world / (ms / 1e3),
+           "unit": "rows/s", "scaling": "weak", "algorithmic_bytes_per_step": algo,
+           "achieved_gbs_step": algo / (ms / 1e3) / 1e9,
+           "roofline": {"bound": "hbm", "kernel": "sample_rows_kernel", "kernel_ms": kms,
+                        "achieved": algo / (kms / 1e3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": algo / (kms / 1e3) / 1e9 / peak,
+                        "peak_source": "measured" if peak_kind == "measured" else "fallback"},
+           "l2_policy": (f"inputs {in_bytes / 1e6:.0f} MB: L2 flushed (256 MB write) before each timed step"
+                         if flush is not None else f"inputs {in_bytes / 1e6:.0f} MB, over twice the L2; no flush")}
+    if world == 1 and not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        threads = os.cpu_count() or 1
+        lg = w.logits.float().cpu().numpy()
+        mask = None if w.mask is None else w.mask.cpu().numpy().view(np.uint32)
+        hist = W.hist_lists(w)
+        u = w.uniforms.cpu().numpy()
+        done, tot, kind = 0, 0.0, "port"
+        while tot < args.cpu_seconds / 3:
+            if O.have_reference():
+                _, secs = O.sample_reference(lg, dict(w.params), u, mask=mask, hist=hist, threads=threads)
+                kind = "reference"
+            else:
+                t0 = time.perf_counter()
+                O.sample_restated(lg, dict(w.params), u, mask=mask, hist=hist, threads=threads)
+                secs = time.perf_counter() - t0
+            done += w.rows
+            tot += secs
+        res["cpu_baseline"] = {
+            "value": done / tot, "unit": "rows/s", "cores": threads, "kind": kind,
+            "sample": f"the config {cfg} batch ({w.rows} rows) repeated for {tot:.1f} s on {threads} threads"
+                      + ("; the reference has no frequency penalty, so its rows skip that subtraction"
+                         if w.params.get("frequency", 0) else "")}
+    return res
+
+
+def extra_configs(args, rank, world, dev):
+    """The other BASELINE configurations, run after the headline: 1 (decode latency), 2 and 3
+    (row batches) and 5 (vocabulary-sharded over the ranks).  Every rank runs them in the same
+    order (config 5's all-gather needs all ranks)."""
+    import torch
+
+    out = {}
+    for name, fn in (("cfg1", lambda: cfg1_result(args, rank, world, dev)),
+                     ("cfg2", lambda: batch_config_result(2, args, rank, world, dev)),
+                     ("cfg3", lambda: batch_config_result(3, args, rank, world, dev)),
+                     ("cfg5", lambda: cfg5_result(args, rank, world, dev))):
+        r = fn()
+        torch.cuda.empty_cache()
+        if rank == 0:
+            if name in ("cfg1", "cfg5"):
+                keep = ("value", "unit", "ms_per_step", "scaling", "config", "roofline", "e2e", "cpu_baseline",
+                        "parts_ms", "n_gpus")
+                r = {k: r[k] for k in keep if k in r}
+            out[name] = r
+    return out
 
 
 def main():
@@ -539,7 +751,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["cfg4", "cfg5", "cfg1"], default="cfg4",
+    ap.add_argument("--no-extra", action="store_true",
+                    help="headline only: skip the configuration 1, 2, 3 and 5 legs")
+    ap.add_argument("--workload", choices=["cfg4", "cfg5", "cfg1", "cfg2", "cfg3"], default="cfg4",
                     help="cfg4: the headline row-sharded batch; cfg5: vocabulary-sharded config 5; "
                          "cfg1: one-sequence decode latency (CUDA graph)")
     ap.add_argument("--rows", type=int, default=ROWS,
@@ -565,6 +779,10 @@ def main():
             run_cfg5(args, rank, world, dev)
         elif args.workload == "cfg1":
             run_cfg1(args, rank, world, dev)
+        elif args.workload in ("cfg2", "cfg3"):
+            r = batch_config_result(int(args.workload[-1]), args, rank, world, dev)
+            if rank == 0:
+                print(json.dumps(r), flush=True)
         else:
             run_ours(args, rank, world, dev)
     finally:
