@@ -366,7 +366,6 @@ extern "C" dllm_status dllm_cuda_sample_batch(const dllm_batch_desc *d, void *st
     a.vocab_total = d->vocab;
     a.vocab_offset = 0;
     a.S = cfg.S;
-    a.S0 = cfg.S0;
     a.SUB = cfg.SUB;
     a.ws = (unsigned char *)ws;
     a.nrec = nrec;

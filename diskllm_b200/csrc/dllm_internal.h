@@ -38,8 +38,7 @@ struct KernelArgs {
     int             vocab;          // ids in this logits slice
     int             vocab_total;    // full vocabulary (history ids are checked against it)
     int             vocab_offset;   // global id of local index 0
-    int             S;              // slice length of ranks 1.. (the slice buffer; <= 4 * NT * SUB)
-    int             S0;             // slice length of rank 0 (<= S; shorter to balance its extra work)
+    int             S;              // slice length per CTA (= 4 * NT * SUB)
     int             SUB;            // elements per thread sub-chunk (SUB % 8 == 4)
     int             htab;           // history hash-table entries (power of 2)
     int             uni_bytes;      // bytes of the shared area after the slice buffers
@@ -79,18 +78,11 @@ struct LaunchCfg {
     int threads;     // NT
     int SUB;
     int S;
-    int S0;          // rank 0's slice (<= S)
     int htab;
     size_t smem;     // dynamic shared memory bytes
     int max_clusters;// co-resident clusters on the device
     int nbuf;        // slice buffers per CTA (1 or 2)
 };
-
-// Columns [slice_start, slice_start + slice_cap) of a row belong to cluster rank `rank`.  Rank 0
-// holds S0 <= S columns: its slice is the start of the row, where the draw's running sum is small
-// and crosses most binades, so its record and slot work is the heaviest of the cluster.
-__host__ __device__ inline int slice_start(int rank, int S, int S0) { return rank == 0 ? 0 : S0 + (rank - 1) * S; }
-__host__ __device__ inline int slice_cap(int rank, int S, int S0) { return rank == 0 ? S0 : S; }
 
 // Workspace layout per row: RowHdr, nrec warp records, STASH_SLOTS stash slots.
 constexpr int STASH_SLOTS = 32;

@@ -1053,18 +1053,15 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
     const int rank = (int)cluster.block_rank();
     const int cid = blockIdx.x / C, ncl = gridDim.x / C;
     const int S = a.S, V = a.vocab;
-    const int slice0 = slice_start(rank, S, a.S0);
-    const int cap = slice_cap(rank, S, a.S0);
-    const int slen = max(0, min(cap, V - slice0));
-    // the part of the slice buffer the passes read: whole sub-chunks covering the slice
-    const int S_used = min(S, (cap + SUBT - 1) / SUBT * SUBT);
+    const int slice0 = rank * S;
+    const int slen = max(0, min(S, V - slice0));
     int kb[4];  // slice-relative start of this thread's four sub-chunks
 #pragma unroll
     for (int q = 0; q < 4; q++) {
-        // sub-chunks past the slice (it need not fill 4 * NT sub-chunks) read a shared all-zero
-        // sub-chunk stored right after the buffer: they add nothing to sums or records
+        // sub-chunks past the slice (S need not fill 4 * NT sub-chunks) read a shared all-zero
+        // sub-chunk stored right after the slice: they add nothing to sums or records
         const int sc = q * NT + tid;
-        kb[q] = sc * SUBT < cap ? sc * SUBT : S;
+        kb[q] = sc * SUBT < S ? sc * SUBT : S;
     }
 
     // slice buffers: with nbuf == 2 the copy of this CTA's next row lands in the other buffer
@@ -1239,7 +1236,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         } else {
             load_slice_bf16(a, row, slice0, slen, vals);
         }
-        for (int i = slen + tid; i < S_used; i += NT) vals[i] = -INFINITY;
+        for (int i = slen + tid; i < S; i += NT) vals[i] = -INFINITY;
         if (use_tma) {
             if (!bounded_wait<false>(&sh.tma_bar[buf], phase, a.wait_limit)) flags |= ROW_ERR_TIMEOUT;
             // test hook (off unless a test asks): on the cluster's first row, CTA 0 also waits for
@@ -1282,7 +1279,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             float4 *v4 = reinterpret_cast<float4 *>(vals);
             const uint32_t *mrow = a.mask ? a.mask + (int64_t)row * a.mask_stride : nullptr;
             if (mrow) {
-                for (int i = tid; i < S_used / 4; i += NT) {
+                for (int i = tid; i < S / 4; i += NT) {
                     const int li = slice0 + 4 * i;
                     float4 x = v4[i];
                     const uint32_t w = li < V ? (mrow[li >> 5] >> (li & 31)) : 0u;
@@ -1297,14 +1294,14 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                 // four independent maxima, so four shared loads are in flight per thread
                 float m1 = -INFINITY, m2 = -INFINITY, m3 = -INFINITY;
                 int i = tid;
-                for (; i + 3 * NT < S_used / 4; i += 4 * NT) {
+                for (; i + 3 * NT < S / 4; i += 4 * NT) {
                     const float4 x0 = v4[i], x1 = v4[i + NT], x2 = v4[i + 2 * NT], x3 = v4[i + 3 * NT];
                     lmax = fmaxf(lmax, fmaxf(fmaxf(x0.x, x0.y), fmaxf(x0.z, x0.w)));
                     m1 = fmaxf(m1, fmaxf(fmaxf(x1.x, x1.y), fmaxf(x1.z, x1.w)));
                     m2 = fmaxf(m2, fmaxf(fmaxf(x2.x, x2.y), fmaxf(x2.z, x2.w)));
                     m3 = fmaxf(m3, fmaxf(fmaxf(x3.x, x3.y), fmaxf(x3.z, x3.w)));
                 }
-                for (; i < S_used / 4; i += NT) {
+                for (; i < S / 4; i += NT) {
                     const float4 x = v4[i];
                     lmax = fmaxf(lmax, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
                 }
@@ -1705,7 +1702,7 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             if (ch.minp) {
                 CSum s2c = csum_zero(), sac = csum_zero();
                 int nk = 0;
-                for (int i = tid; i < S_used; i += NT) {
+                for (int i = tid; i < S; i += NT) {
                     const float pp = __fmul_rn(vals[i], ch.inv_sum);
                     csum_add(sac, pp);
                     if (pp >= ch.min_p) {
@@ -2354,8 +2351,8 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
             if (lane == 0) dbg_add(DBG_EXPAND, 1);
             const int g = gw0 + j;
             const int rr = g / (4 * NW), kk = g % (4 * NW), q = kk / NW, w = kk % NW;
-            const int start = slice_start(rr, S, a.S0) + (q * NT + 32 * w) * SUBT;
-            const int rend = slice_start(rr, S, a.S0) + slice_cap(rr, S, a.S0);  // nothing past the slice
+            const int start = rr * S + (q * NT + 32 * w) * SUBT;
+            const int rend = rr * S + S;  // sub-chunks past the slice end hold nothing
             const int wslot = __shfl_sync(0xffffffffu, (int)wl.wslot, j);
             bool wide_in = false;
             // replays [st, st + n) of this warp range: from its wide slot when the cluster

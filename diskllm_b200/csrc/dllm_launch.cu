@@ -13,7 +13,6 @@ namespace dllm {
 
 static unsigned long long *g_host_dbg = nullptr;  // device counters for KernelArgs::dbg
 static int g_sm_count = 0;
-static const int RANK0_CUT_DEFAULT = 0;  // columns moved from rank 0's slice to each other rank's
 
 static const int kSUBs[] = {4, 12, 20, 28, 36, 44, 52, 60};
 
@@ -205,28 +204,9 @@ dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, 
         }
     }
     if (best >= 1e299) return DLLM_ERR_UNSUPPORTED;
-    bc.S0 = bc.S;
-    // Rank 0's slice is made shorter by (C - 1) * delta columns and every other slice longer by
-    // delta, when the larger slice buffer keeps the same number of co-resident clusters
-    // (DLLM_RANK0_CUT overrides delta; 0 switches it off).
-    int delta = RANK0_CUT_DEFAULT;
-    if (const char *e = getenv("DLLM_RANK0_CUT")) delta = atoi(e);
-    if (delta > 0 && bc.cluster > 1 && bc.nbuf == 1) {
-        const int L = bc.SUB, C = bc.cluster;
-        int S1 = (bc.S + delta + 2 * L - 1) / (2 * L) * (2 * L);  // whole sub-chunks, 8-aligned
-        if (S1 > 4 * bc.threads * L) S1 = 4 * bc.threads * L / (2 * L) * (2 * L);
-        const int S0 = ((vocab - (C - 1) * S1) + 7) & ~7;
-        const size_t smem1 = (size_t)(S1 + L) * 4 + (bc.smem - (size_t)(bc.S + L) * 4);
-        if (S1 > bc.S && S0 >= L && S0 < bc.S && smem1 <= 220 * 1024 &&
-            active_clusters(kernel_for(dtype, L), C, bc.threads, smem1) >= bc.max_clusters) {
-            bc.S = S1;
-            bc.S0 = S0;
-            bc.smem = smem1;
-        }
-    }
     if (getenv("DLLM_VERBOSE"))
-        fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d SUB %d S %d S0 %d htab %d smem %zu clusters %d nbuf %d\n",
-                vocab, dtype, bc.cluster, bc.threads, bc.SUB, bc.S, bc.S0, bc.htab, bc.smem, bc.max_clusters, bc.nbuf);
+        fprintf(stderr, "dllm config: vocab %d dtype %d -> cluster %d threads %d SUB %d S %d htab %d smem %zu clusters %d nbuf %d\n",
+                vocab, dtype, bc.cluster, bc.threads, bc.SUB, bc.S, bc.htab, bc.smem, bc.max_clusters, bc.nbuf);
     *cfg = bc;
     return DLLM_OK;
 }
