@@ -680,10 +680,88 @@ __device__ __noinline__ int replay_elems_impl(int n, int gbase, uint32_t &cb, fl
     return pos < 32 ? -2 : -1;
 }
 
-// replay_elems_impl, with its cycles counted in the diagnostic counters when they are on
+// replay_elems_impl with each lane's elements held in registers: they are loaded once (all loads
+// in flight together), and a lane's run for the running sum's binade is computed once per binade
+// instead of once per walk step.  Needs ceil(n / 32) <= SUBT.
+template <int SUBT>
+__device__ __noinline__ int replay_elems_reg(int n, int gbase, uint32_t &cb, float r, const float *src) {
+    const int lane = threadIdx.x & 31;
+    const int s = (n + 31) >> 5;
+    const int j0 = lane * s;
+    const int cnt = max(0, min(s, n - j0));
+    float v[SUBT];
+#pragma unroll
+    for (int k = 0; k < SUBT; k++) v[k] = k < cnt ? src[j0 + k] : 0.0f;
+    bool anyq = false;
+#pragma unroll
+    for (int k = 0; k < SUBT; k++) anyq |= v[k] != 0.0f;
+    if (lane == 0) dbg_add(DBG_REPLAY, 1);
+    // serial replay of one lane's sub-range on the exact running sum (the zeros past cnt leave
+    // a nonnegative sum unchanged)
+    auto serial = [&](int jl, uint32_t &cbx) -> int {
+        int found = -1;
+        uint32_t nb = 0;
+        if (lane == jl) {
+            float c = bitsf(cbx);
+#pragma unroll
+            for (int k = 0; k < SUBT; k++) {
+                c = __fadd_rn(c, v[k]);
+                if (found < 0 && k < cnt && r < c) found = gbase + j0 + k;
+            }
+            nb = fbits(c);
+        }
+        found = __shfl_sync(0xffffffffu, found, jl);
+        cbx = __shfl_sync(0xffffffffu, nb, jl);
+        return found;
+    };
+    int type = REC_IDENT;
+    uint32_t n0 = 0u, n1 = 0u, eb_c = 0xffffffffu;
+    int pos = 0;
+    for (int guard = 0; pos < 32 && guard < 96; guard++) {
+        if (lane == 0) dbg_add(DBG_REPLAY_IT, 1);
+        if (cb == 0u) {
+            const unsigned m = __ballot_sync(0xffffffffu, lane >= pos && anyq);
+            if (!m) return -1;
+            const int fl = __ffs(m) - 1;
+            const int found = serial(fl, cb);
+            pos = fl + 1;
+            if (found >= 0) return found;
+            continue;
+        }
+        const uint32_t eb = cb >> 23;  // the same in every lane
+        if (eb != eb_c) {
+            eb_c = eb;
+            const uint32_t gb = eb << 23, lim = (eb + 1u) << 23;
+            float g0 = bitsf(gb), g1 = bitsf(gb | 1u);
+#pragma unroll
+            for (int k = 0; k < SUBT; k++) {
+                g0 = __fadd_rn(g0, v[k]);
+                g1 = __fadd_rn(g1, v[k]);
+            }
+            type = !anyq ? REC_IDENT : ((fbits(g0) < lim && fbits(g1) < lim) ? REC_CLEAN : REC_MIXED);
+            n0 = fbits(g0) - gb;
+            n1 = fbits(g1) - (gb | 1u);
+        }
+        int xj = 0;
+        bool must_hit = false;
+        int res = walk_step(32, pos, type, (int)eb, n0, n1, cb, r, &xj, &must_hit);
+        if (res == WALK_EXPAND) {
+            res = serial(xj, cb);
+            if (must_hit) return res >= 0 ? res : -2;
+            pos = xj + 1;
+        }
+        if (res != -1) return res;
+    }
+    return pos < 32 ? -2 : -1;
+}
+
+// replay of n consecutive draw probabilities, with its cycles counted in the diagnostic counters
+// when they are on
+template <int SUBT>
 __device__ __forceinline__ int replay_elems(int n, int gbase, uint32_t &cb, float r, const float *src) {
     const long long t0 = g_dbg ? clock64() : 0;
-    const int res = replay_elems_impl(n, gbase, cb, r, src);
+    const int res = ((n + 31) >> 5) <= SUBT ? replay_elems_reg<SUBT>(n, gbase, cb, r, src)
+                                            : replay_elems_impl(n, gbase, cb, r, src);
     if (g_dbg && (threadIdx.x & 31) == 0) dbg_add(DBG_B_REPL, (unsigned long long)(clock64() - t0));
     return res;
 }
@@ -2330,7 +2408,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
             rv[i] = li < V ? qval(v, li) : 0.0f;
         }
         __syncwarp();
-        const int res = replay_elems(n, start, cbv, r, rv);
+        const int res = replay_elems<SUBT>(n, start, cbv, r, rv);
         __syncwarp();
         if (lane == 0) dbg_add(DBG_B_RECOMP, (unsigned long long)(clock64() - t0));
         return res;
@@ -2371,7 +2449,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                     __syncwarp();
                     wide_in = true;
                 }
-                const int res = replay_elems(n, st, cbv, r, rv + (st - start));
+                const int res = replay_elems<SUBT>(n, st, cbv, r, rv + (st - start));
                 __syncwarp();
                 return res;
             };
@@ -2398,7 +2476,7 @@ __global__ void __launch_bounds__(WALK_WARPS * 32, 4) walk_rows_kernel(const Ker
                         // the slot holds exponentials: probabilities into the region buffer
                         for (int k = lane; k < SUBT; k += 32) rv[k] = q_of(ch, qs[1 + k], sbase + k);
                         __syncwarp();
-                        const int found = replay_elems(SUBT, sbase, c, r, rv);
+                        const int found = replay_elems<SUBT>(SUBT, sbase, c, r, rv);
                         __syncwarp();
                         wide_in = false;  // the region buffer no longer holds the wide slot
                         if (found != -1) return found;
