@@ -104,6 +104,7 @@ __host__ __device__ inline size_t walk_smem_per_warp(int nrec) {
 
 dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
 dllm_status set_debug_counters(unsigned long long *dev_counters);
+unsigned long long *debug_counters();  // the device array set by set_debug_counters, or null
 dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
 dllm_status set_fault_injection(int site, long long polls);
 size_t shard_part_bytes(int rows, int vlocal, int k);

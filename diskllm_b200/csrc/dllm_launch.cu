@@ -223,6 +223,7 @@ dllm_status set_debug_counters(unsigned long long *dev_counters) {
     g_host_dbg = dev_counters;
     return DLLM_OK;
 }
+unsigned long long *debug_counters() { return g_host_dbg; }
 
 dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream) {
     if (a.rows == 0) return DLLM_OK;

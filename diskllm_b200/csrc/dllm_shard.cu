@@ -47,7 +47,11 @@ struct ShardArgs {
     uint32_t *part_key;    // per-chunk candidates [rows][nchunks][k] when nchunks > 1
     int32_t *part_id;
     int32_t *status;
+    unsigned long long *dbg;  // diagnostic counters (shard_stream_kernel phase cycles) or null
 };
+
+// diagnostic counter slots of shard_stream_kernel (thread 0 of each row CTA adds its cycles)
+enum : int { SDBG_ROWS = 0, SDBG_LOOP = 1, SDBG_CUT = 2, SDBG_NCUT = 3, SDBG_FINAL = 4, SDBG_UNION = 5 };
 
 constexpr int SH_SURV = 1024;    // survivors of the threshold pre-filter kept for the exact select
 
@@ -486,7 +490,9 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
             }
     };
     // cuts the buffer to its best kprime entries (sorted); later keys must beat the K'-th
+    long long t_cut = 0;
     auto cut = [&]() {
+        const long long tc0 = a.dbg ? clock64() : 0;
         const int nb = min(s_nb, ST_CAP);
         block_select(bk, bid, 0, nb, kprime, sel, okey_s, oid_s);
         const int kk = min(nb, kprime);
@@ -503,6 +509,10 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
             }
         }
         __syncthreads();
+        if (a.dbg && tid == 0) {
+            t_cut += clock64() - tc0;
+            atomicAdd(a.dbg + SDBG_NCUT, 1ull);
+        }
     };
 
     // Tiles of E columns, ST_U 16-byte vectors per thread.  Two register sets take turns (the loop
@@ -638,6 +648,7 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
         __syncthreads();
         if (s_nb > ST_CAP - E) cut();
     };
+    const long long t_start = a.dbg ? clock64() : 0;
     for (int d = 0; d < ST_PD; d++) prefetch_tile(d * E);
     {
         uint4 ra[ST_U], rb[ST_U];
@@ -673,7 +684,10 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
         if (s_nb > ST_CAP - NT) cut();
     }
     __syncthreads();
+    const long long t_loop = a.dbg ? clock64() : 0;
+    const long long t_cut_loop = t_cut;
     cut();
+    const long long t_fcut = a.dbg ? clock64() : 0;
     // the union: the K' best raw entries that are not history ids, and each history id of this
     // shard once, with its penalised value (src/sampler.c:21-52, after the mask)
     const int nraw = s_nb;
@@ -723,10 +737,19 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
         }
     }
     __syncthreads();
+    const long long t_union = a.dbg ? clock64() : 0;
     block_select(fk, fid, 0, nr + nh, a.k, sel, okey_s, oid_s);
     for (int i = tid; i < a.k; i += NT) {
         a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
         a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
+    }
+    if (a.dbg && tid == 0) {
+        const long long t_end = clock64();
+        atomicAdd(a.dbg + SDBG_ROWS, 1ull);
+        atomicAdd(a.dbg + SDBG_LOOP, (unsigned long long)(t_loop - t_start - t_cut_loop));
+        atomicAdd(a.dbg + SDBG_CUT, (unsigned long long)t_cut_loop);
+        atomicAdd(a.dbg + SDBG_UNION, (unsigned long long)(t_union - t_loop));  // final cut + union build
+        atomicAdd(a.dbg + SDBG_FINAL, (unsigned long long)(t_end - t_union));
     }
 }
 
@@ -848,6 +871,7 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     a.cand_val = cand_val;
     a.cand_id = cand_id;
     a.status = d->status;
+    a.dbg = debug_counters();
     if (a.rows == 0) return DLLM_OK;
     if (a.nchunks > 1) {
         if (!part) return DLLM_ERR_OOM;
