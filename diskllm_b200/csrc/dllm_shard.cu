@@ -145,13 +145,86 @@ __device__ void select_ties(const uint32_t *keys, const int *ids, int id0, int n
     __syncthreads();
 }
 
+// Order keys of bf16 values (exact fp32 upcasts) have their low 16 bits fixed by the sign: 0 for
+// a positive value, 0xffff for a negative one (the key of a negative float is its complement), so
+// a radix select over them needs only the two high bytes.  Completes a key from its high half.
+__device__ __forceinline__ uint32_t bf16_key_low(uint32_t hi_prefix) {
+    return hi_prefix | ((hi_prefix & 0x80000000u) ? 0u : 0xffffu);
+}
+
+// The K-th largest of the finite (above -inf) keys among n in shared memory, by four 8-bit radix
+// passes (the same passes block_select runs); 0 when fewer than K keys are finite.  Ends with a
+// barrier; every thread gets the result.
+__device__ uint32_t radix_kth(const uint32_t *keys, int n, int K, SelScratch &s, bool bf16_keys) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
+    const uint32_t KNEG = okey(-INFINITY);
+    int nf = 0;
+    for (int base = 0; base < n; base += NT) {
+        const int i = base + tid;
+        nf += __popc(__ballot_sync(0xffffffffu, i < n && keys[i] > KNEG));
+    }
+    if (lane == 0) s.wsum[wid] = nf;
+    __syncthreads();
+    nf = 0;
+    for (int w = 0; w < NW; w++) nf += s.wsum[w];
+    if (nf < K || K <= 0) {
+        __syncthreads();
+        return 0u;
+    }
+    uint32_t prefix = 0u, pmask = 0u;
+    int remaining = K;
+    for (int pass = 3; pass >= (bf16_keys ? 2 : 0); pass--) {
+        for (int i = tid; i < 256; i += NT) s.hist[i] = 0u;
+        __syncthreads();
+        const int sh = 8 * pass;
+        for (int i = tid; i < n; i += NT) {
+            const uint32_t key = keys[i];
+            if (key > KNEG && (key & pmask) == prefix) atomicAdd(&s.hist[(key >> sh) & 255u], 1u);
+        }
+        __syncthreads();
+        if (wid == 0) {
+            unsigned c[8], tot = 0u;
+#pragma unroll
+            for (int b = 0; b < 8; b++) {
+                c[b] = s.hist[255 - 8 * lane - b];
+                tot += c[b];
+            }
+            unsigned incl = tot;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const unsigned excl = incl - tot;
+            if (excl < (unsigned)remaining && incl >= (unsigned)remaining) {
+                unsigned acc = excl;
+#pragma unroll
+                for (int b = 0; b < 8; b++) {
+                    if (acc + c[b] >= (unsigned)remaining) {
+                        s.bin = 255 - 8 * lane - b;
+                        s.above = (int)acc;
+                        break;
+                    }
+                    acc += c[b];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= (uint32_t)s.bin << sh;
+        pmask |= 255u << sh;
+        remaining -= s.above;
+        __syncthreads();
+    }
+    return bf16_keys ? bf16_key_low(prefix) : prefix;
+}
+
 // The K best of n keys in shared memory by (key desc, id asc), written sorted to out_key / out_id
 // (K entries; positions past n, when n < K, get key 0 and id INT_MAX, which rank last).
 // Masked entries (-inf) are left out of the radix select of the K-th key (8 bits per pass from
 // the top) and taken, lowest ids first, only when fewer than K entries are finite.  Ids: ids[i],
 // or id0 + i when ids is null (then ids grow with position).
 __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int n, int K, SelScratch &s,
-                             uint32_t *out_key, int *out_id) {
+                             uint32_t *out_key, int *out_id, bool bf16_keys = false) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x, NW = NT >> 5;
     const uint32_t KNEG = okey(-INFINITY);
     const int Kn = min(K, n);
@@ -171,7 +244,7 @@ __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int 
     uint32_t prefix = 0u, pmask = 0u;
     int remaining = Kf;
     unsigned cnt_eq = 0u;
-    for (int pass = 3; pass >= 0 && Kf > 0; pass--) {
+    for (int pass = 3; pass >= (bf16_keys ? 2 : 0) && Kf > 0; pass--) {
         for (int i = tid; i < 256; i += NT) s.hist[i] = 0u;
         __syncthreads();
         const int sh = 8 * pass;
@@ -216,7 +289,7 @@ __device__ void block_select(const uint32_t *keys, const int *ids, int id0, int 
         __syncthreads();
     }
     if (Kf > 0) {
-        const uint32_t kstar = prefix;
+        const uint32_t kstar = bf16_keys ? bf16_key_low(prefix) : prefix;
         const bool all_eq = cnt_eq == (unsigned)remaining;
         for (int i = tid; i < n; i += NT) {
             const uint32_t key = keys[i];
@@ -494,7 +567,51 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
     auto cut = [&]() {
         const long long tc0 = a.dbg ? clock64() : 0;
         const int nb = min(s_nb, ST_CAP);
-        block_select(bk, bid, 0, nb, kprime, sel, okey_s, oid_s);
+        // Fast cut: the K'-th largest key kstar, and every entry with key >= kstar kept, in any
+        // order.  At least K' entries remain at or above kstar, so a later key equal to kstar
+        // (larger id) can no longer reach the K' best: later keys must beat kstar strictly.  The
+        // final union select orders what is kept.  The full select (below) handles buffers with
+        // fewer than K' finite keys, or more ties at kstar than the compaction area holds.
+        const uint32_t kstar = radix_kth(bk, nb, kprime, sel, DT == DLLM_DTYPE_BF16);
+        if (kstar != 0u) {
+            if (tid == 0) sel.ncand = 0;
+            __syncthreads();
+            for (int base = 0; base < nb; base += NT) {
+                const int i = base + tid;
+                const bool keep = i < nb && bk[i] >= kstar;
+                const unsigned m = __ballot_sync(0xffffffffu, keep);
+                int pos = 0;
+                if (lane == 0 && m) pos = atomicAdd(&sel.ncand, __popc(m));
+                pos = __shfl_sync(0xffffffffu, pos, 0) + __popc(m & ((1u << lane) - 1u));
+                if (keep && pos < ST_FIN) {
+                    fk[pos] = bk[i];
+                    fid[pos] = bid[i];
+                }
+            }
+            __syncthreads();
+            const int kept = sel.ncand;
+            // at most SH_KMAX kept, so that the final union (kept raw entries plus at most
+            // SH_KMAX - k history entries) fits the ST_FIN union area
+            if (kept <= ST_FIN - SH_KMAX) {
+                for (int i = tid; i < kept; i += NT) {
+                    bk[i] = fk[i];
+                    bid[i] = fid[i];
+                }
+                __syncthreads();
+                if (tid == 0) {
+                    s_nb = kept;
+                    s_thr = kstar;
+                    s_strict = 1;
+                }
+                __syncthreads();
+                if (a.dbg && tid == 0) {
+                    t_cut += clock64() - tc0;
+                    atomicAdd(a.dbg + SDBG_NCUT, 1ull);
+                }
+                return;
+            }
+        }
+        block_select(bk, bid, 0, nb, kprime, sel, okey_s, oid_s, DT == DLLM_DTYPE_BF16);
         const int kk = min(nb, kprime);
         for (int i = tid; i < kk; i += NT) {
             bk[i] = okey_s[i];
