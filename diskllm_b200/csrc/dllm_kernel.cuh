@@ -112,7 +112,8 @@ enum : int {
     DBG_P4 = 7, DBG_WEND = 10, DBG_TOPK = 11, DBG_LOADWAIT = 12,
     DBG_ROWS = 16, DBG_REPLAY = 17, DBG_EXPAND = 18, DBG_STEPS = 19, DBG_REPLAY_IT = 20,
     DBG_PBS = 21, DBG_STASH_MISS = 22, DBG_TOPK_FALLBACK = 23, DBG_RECOMP = 24, DBG_WALK_CYC = 25,
-    DBG_P2L = 13, DBG_P3L = 14, DBG_P3S = 15, DBG_P4L = 26, DBG_MAXP = 27,
+    DBG_P2L = 13, DBG_P3L = 14, DBG_P3S = 15, DBG_P4L = 26, DBG_MAXP = 27, DBG_HBUILD = 30,
+    DBG_COPY_EARLY = 31,
     DBG_B_PRE = 8, DBG_B_EXP = 9, DBG_B_REPL = 28, DBG_B_RECOMP = 29,
 };
 __device__ __forceinline__ void dbg_add(int k, unsigned long long v) {
@@ -1242,6 +1243,45 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             nxt_h1 = a.hist_off[cid + ncl + 1];
         }
     }
+    // History hash table of the row about to be sampled (ids cur_h0..cur_h1, the first HPF per
+    // thread already in cur_id): cleared, then every in-slice id inserted with its count.  No
+    // trailing barrier.  Returns ROW_ERR_HIST_TABLE when an id found no free entry.
+    auto build_table = [&](bool use_hist) -> int {
+        int fl = 0;
+        for (int i = tid; i < a.htab; i += NT) {
+            hkeys[i] = -1;
+            hcnt[i] = 0;
+        }
+        __syncthreads();
+        if (!use_hist) return 0;
+        const int64_t h0 = cur_h0, h1 = cur_h1;
+        const uint32_t hm = (uint32_t)a.htab - 1u;
+        int k = 0;
+        for (int64_t j = h0 + tid; j < h1; j += NT, k++) {
+            const int id = k == 0 ? cur_id[0] : (k == 1 ? cur_id[1] : a.hist_ids[j]);
+            if (id < 0 || id >= a.vocab_total) continue;
+            const int li = id - a.vocab_offset - slice0;
+            if (li < 0 || li >= slen) continue;
+            uint32_t h = hash_id((uint32_t)li) & hm;
+            bool placed = false;
+            for (int probe = 0; probe < a.htab; probe++) {
+                const int old = atomicCAS(&hkeys[h], -1, li);
+                if (old == -1 || old == li) {
+                    atomicAdd(&hcnt[h], 1);
+                    placed = true;
+                    break;
+                }
+                h = (h + 1u) & hm;
+            }
+            if (!placed) fl |= ROW_ERR_HIST_TABLE;
+        }
+        return fl;
+    };
+    // Index-order-only variant: the next row's table is built while this row waits for its
+    // top-p cut (exchange #4), after this row's penalties have been applied and the table is
+    // no longer read; the next row then skips the build.
+    bool prebuilt = false;
+    int pre_flags = 0;
     int it = 0;
     for (int row = cid; row < a.rows; row += ncl, it++) {
         if (timing) dbg_add(DBG_ROWS, 1);
@@ -1264,35 +1304,13 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
             sh.xs.cut_idx = -1;
             sh.xs.cut_flags = 0;
         }
-        for (int i = tid; i < a.htab; i += NT) {
-            hkeys[i] = -1;
-            hcnt[i] = 0;
-        }
-        __syncthreads();
         const bool use_hist = a.hist_ids && a.hist_off &&
                               (p.repetition > 1.0f || p.presence != 0.0f || p.frequency != 0.0f);
-        if (use_hist) {
-            const int64_t h0 = cur_h0, h1 = cur_h1;
-            const uint32_t hm = (uint32_t)a.htab - 1u;
-            int k = 0;
-            for (int64_t j = h0 + tid; j < h1; j += NT, k++) {
-                const int id = k == 0 ? cur_id[0] : (k == 1 ? cur_id[1] : a.hist_ids[j]);
-                if (id < 0 || id >= a.vocab_total) continue;
-                const int li = id - a.vocab_offset - slice0;
-                if (li < 0 || li >= slen) continue;
-                uint32_t h = hash_id((uint32_t)li) & hm;
-                bool placed = false;
-                for (int probe = 0; probe < a.htab; probe++) {
-                    const int old = atomicCAS(&hkeys[h], -1, li);
-                    if (old == -1 || old == li) {
-                        atomicAdd(&hcnt[h], 1);
-                        placed = true;
-                        break;
-                    }
-                    h = (h + 1u) & hm;
-                }
-                if (!placed) flags |= ROW_ERR_HIST_TABLE;
-            }
+        if (prebuilt) {
+            flags |= pre_flags;  // the table was built during the previous row
+            prebuilt = false;
+        } else {
+            flags |= build_table(use_hist);
         }
         if (have_hist && row + ncl < a.rows) {
             // this row's ids are in the table: load the next row's ids from its offsets (loaded a
@@ -1316,6 +1334,11 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
         }
         for (int i = slen + tid; i < S; i += NT) vals[i] = -INFINITY;
         if (use_tma) {
+            if (timing) {
+                // diagnostics: the part of P1 before the wait, and whether the copy had landed
+                mark(DBG_HBUILD);
+                if (mbar_try_wait(&sh.tma_bar[buf], phase)) dbg_add(DBG_COPY_EARLY, 1);
+            }
             if (!bounded_wait<false>(&sh.tma_bar[buf], phase, a.wait_limit)) flags |= ROW_ERR_TIMEOUT;
             // test hook (off unless a test asks): on the cluster's first row, CTA 0 also waits for
             // the barrier's next phase, which nothing completes, so the wait runs out with no
@@ -1986,6 +2009,14 @@ __global__ void __launch_bounds__(512, 1) sample_rows_kernel(const KernelArgs a)
                         push16(&sh.in4[par][rank], &sh.xbar[2][par], tid, (uint32_t)sh.xs.cut_idx,
                                (uint32_t)sh.xs.cut_flags, (uint32_t)sb,
                                (uint32_t)(sb >> 32));
+                    }
+                    if (IDX && row + ncl < a.rows) {
+                        // the next row's history table, while the cut comes in (its ids and
+                        // offsets were loaded during this row's P1)
+                        const dllm_sampler_params pn = a.bparams;
+                        pre_flags = build_table(a.hist_ids && a.hist_off &&
+                                                (pn.repetition > 1.0f || pn.presence != 0.0f || pn.frequency != 0.0f));
+                        prebuilt = true;
                     }
                     if (!xwait(2, par)) rowflags |= ROW_ERR_TIMEOUT;  // ---- #4
                     {
