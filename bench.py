@@ -535,7 +535,7 @@ CFG5_ROWS, CFG5_VOCAB, CFG5_HIST, CFG5_K = 512, 262144, 128, 64
 
 def run_cfg5(args, rank, world, dev):
     line = cfg5_result(args, rank, world, dev)
-    if rank == 0:
+    if rank == 0 and line is not None:
         print(json.dumps(line), flush=True)
 
 
@@ -550,7 +550,9 @@ def cfg5_result(args, rank, world, dev):
 
     capi.load_library()
     w = W.config5(device=dev, seed=505, rows=CFG5_ROWS)  # the same rows on every rank
-    s, e = sharded.shard_range(CFG5_VOCAB, rank, world)
+    # --emulate-shards N on one GPU: this GPU takes shard 0 of N (candidates and merge only)
+    nsh = world if world > 1 or args.emulate_shards <= 1 else args.emulate_shards
+    s, e = sharded.shard_range(CFG5_VOCAB, rank, nsh)
     x = w.logits[:, s:e].contiguous()
     m = w.mask[:, s // 32:(e + 31) // 32].contiguous()
     params = dict(w.params)
@@ -562,6 +564,11 @@ def cfg5_result(args, rank, world, dev):
 
     for _ in range(args.warmup):
         step()
+    if args.profile_only:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize(dev)
+        return None
     shard_bytes = x.numel() * 2 + m.numel() * 4
     flush = L2Flush(dev) if shard_bytes < 2 * 126e6 else None
     steps = min(args.steps, 50)
@@ -649,6 +656,44 @@ def cfg5_result(args, rank, world, dev):
         "gpu_launches": 2 * steps,
         "clocks": clocks.summary(),
     }
+
+
+def run_profile_workload(args, dev):
+    """Small launches of the kernels that have no bench leg of their own, for ncu captures:
+    --workload sorted: the sorted-nucleus passes (DLLM_MODE_TOPP_SORTED) on config 4's rows;
+    --workload lmhead: the LM-head tail, 8 rows x hidden 4096 x vocab 128256, bf16 weights.
+    Runs warm-up plus `steps` launches and prints the mean CUDA-event time per launch."""
+    import torch
+
+    from diskllm_b200 import capi
+    from diskllm_b200 import workloads as W
+
+    if args.workload == "sorted":
+        w = W.config4(device=dev, rows=args.rows)
+
+        def step():
+            capi.sample_batch(w.logits, w.uniforms, w.params, hist_ids=w.hist_ids, hist_off=w.hist_off,
+                              hist_max=HIST, flags=capi.MODE_TOPP_SORTED)
+
+        desc = f"sorted-nucleus passes, {args.rows} x {VOCAB} fp32 (config 4 rows)"
+    else:
+        g = torch.Generator(device=dev)
+        g.manual_seed(7)
+        rows, hidden, vocab = 8, 4096, 128256
+        h = torch.randn(rows, hidden, generator=g, device=dev)
+        wt = (torch.randn(vocab, hidden, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        nw = torch.rand(hidden, generator=g, device=dev) + 0.5
+        out = torch.empty(rows, vocab, device=dev)
+
+        def step():
+            capi.lmhead_logits(h, wt, norm_w=nw, logits=out)
+
+        desc = f"LM-head tail, {rows} x {hidden} x {vocab} bf16 weights"
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    ms, _ = timed_steps(step, args.steps, dev, 1)
+    print(json.dumps({"workload": desc, "ms_per_launch": ms, "steps": args.steps}), flush=True)
 
 
 BATCH_SEEDS = {2: 202, 3: 303}
@@ -753,7 +798,12 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-extra", action="store_true",
                     help="headline only: skip the configuration 1, 2, 3 and 5 legs")
-    ap.add_argument("--workload", choices=["cfg4", "cfg5", "cfg1", "cfg2", "cfg3"], default="cfg4",
+    ap.add_argument("--emulate-shards", type=int, default=1,
+                    help="cfg5 on one GPU: take 1 of N column shards (no all-gather)")
+    ap.add_argument("--profile-only", action="store_true",
+                    help="cfg5: only warm-up and `steps` plain steps, no timing legs (for ncu captures)")
+    ap.add_argument("--workload", choices=["cfg4", "cfg5", "cfg1", "cfg2", "cfg3", "sorted", "lmhead"],
+                    default="cfg4",
                     help="cfg4: the headline row-sharded batch; cfg5: vocabulary-sharded config 5; "
                          "cfg1: one-sequence decode latency (CUDA graph)")
     ap.add_argument("--rows", type=int, default=ROWS,
@@ -775,7 +825,9 @@ def main():
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
     try:
-        if args.workload == "cfg5":
+        if args.workload in ("sorted", "lmhead"):
+            run_profile_workload(args, dev)
+        elif args.workload == "cfg5":
             run_cfg5(args, rank, world, dev)
         elif args.workload == "cfg1":
             run_cfg1(args, rank, world, dev)
