@@ -50,9 +50,10 @@ extern "C" const char *dllm_cuda_version(void) { return "diskllm_cuda 0.1.0 sm_1
 namespace {
 struct CfgKey {
     int dev, vocab, dtype, hist_bound, topk_cap;
+    bool latency;
     bool operator==(const CfgKey &o) const {
         return dev == o.dev && vocab == o.vocab && dtype == o.dtype && hist_bound == o.hist_bound &&
-               topk_cap == o.topk_cap;
+               topk_cap == o.topk_cap && latency == o.latency;
     }
 };
 std::mutex g_cfg_mu;
@@ -66,14 +67,14 @@ int bucket(int x) {
 }
 }  // namespace
 
-static dllm_status get_config(int vocab, int dtype, int hist_max, int topk_max, LaunchCfg *out) {
+static dllm_status get_config(int rows, int vocab, int dtype, int hist_max, int topk_max, LaunchCfg *out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
         set_error("cudaGetDevice", e);
         return DLLM_ERR_CUDA;
     }
-    CfgKey key{dev, vocab, dtype, bucket(hist_max), topk_max > 0 ? bucket(topk_max) : 0};
+    CfgKey key{dev, vocab, dtype, bucket(hist_max), topk_max > 0 ? bucket(topk_max) : 0, rows <= LATENCY_ROWS};
     std::lock_guard<std::mutex> lk(g_cfg_mu);
     for (auto &kv : g_cfgs)
         if (kv.first == key) {
@@ -81,7 +82,7 @@ static dllm_status get_config(int vocab, int dtype, int hist_max, int topk_max, 
             return DLLM_OK;
         }
     LaunchCfg c;
-    dllm_status st = choose_config(vocab, dtype, key.hist_bound, key.topk_cap, &c);
+    dllm_status st = choose_config(vocab, dtype, key.hist_bound, key.topk_cap, key.latency, &c);
     if (st != DLLM_OK) return st;
     g_cfgs.push_back({key, c});
     *out = c;
@@ -304,7 +305,7 @@ struct WsLayout {
 static dllm_status ws_layout(const dllm_batch_desc *d, const Plan &pl, LaunchCfg *cfg, WsLayout *out) {
     WsLayout L = {};
     if (pl.fused) {
-        const dllm_status st = get_config(d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, pl.fused_topk, cfg);
+        const dllm_status st = get_config(d->rows, d->vocab, d->dtype, d->hist_ids ? d->hist_max : 0, pl.fused_topk, cfg);
         if (st != DLLM_OK) return st;
         L.fused = (size_t)d->rows * row_ws_bytes(nrec_for(*cfg), cfg->SUB);
     }

@@ -102,7 +102,10 @@ __host__ __device__ inline size_t walk_smem_per_warp(int nrec) {
     return (((size_t)nrec * 24 + 127) & ~(size_t)127) + (size_t)STASH_SLOTS * STASH_STRIDE * 4;
 }
 
-dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, LaunchCfg *cfg);
+// latency: a batch of a few rows (decode of one or several sequences), where one row's latency
+// matters, not the throughput of many co-resident rows
+dllm_status choose_config(int vocab, int dtype, int hist_bound, int topk_bound, bool latency, LaunchCfg *cfg);
+constexpr int LATENCY_ROWS = 4;  // batches of at most this many rows use the latency configuration
 dllm_status set_debug_counters(unsigned long long *dev_counters);
 unsigned long long *debug_counters();  // the device array set by set_debug_counters, or null
 dllm_status set_timing_events(cudaEvent_t before, cudaEvent_t after);
