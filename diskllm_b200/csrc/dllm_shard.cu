@@ -937,14 +937,49 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
     const float inv_temp = __fdiv_rn(1.0f, p.temperature);
     for (int i = tid; i < n; i += NT) v[i] = __fmul_rn(__fsub_rn(v[i], M), inv_temp);
     __syncthreads();
-    // the k best by (t desc, id asc)
+    // the k best by (t desc, id asc).  Each shard's list is sorted by (value desc, id asc), and t
+    // is a non-decreasing function of the value, so the list is in (t desc, id asc) order unless
+    // two distinct values round to the same t with their ids the wrong way round.  In order, a
+    // candidate's rank is its position in its own list plus, for every other list, the number of
+    // entries ahead of it (a binary search); otherwise every pair is compared.
+    __shared__ int s_unsorted;
+    if (tid == 0) s_unsorted = 0;
+    __syncthreads();
+    for (int i = tid; i < n; i += NT) {
+        const int j = i % a.k;
+        if (j + 1 < a.k) {
+            const uint32_t k0 = okey(v[i]), k1 = okey(v[i + 1]);
+            if (k0 < k1 || (k0 == k1 && id[i] > id[i + 1])) s_unsorted = 1;
+        }
+    }
+    __syncthreads();
+    const bool sorted_lists = s_unsorted == 0;
     for (int i = tid; i < n; i += NT) {
         const uint32_t ki = okey(v[i]);
         const int ii = id[i];
         int r = 0;
-        for (int j = 0; j < n; j++) {
-            const uint32_t kj = okey(v[j]);
-            r += kj > ki || (kj == ki && id[j] < ii);
+        if (sorted_lists) {
+            const int own = i / a.k;
+            r = i - own * a.k;
+            for (int sh = 0; sh < a.nsh; sh++) {
+                if (sh == own) continue;
+                // entries of list sh ahead of (ki, ii): the first position not ahead
+                const float *vl = v + sh * a.k;
+                const int *il2 = id + sh * a.k;
+                int lo = 0, hi = a.k;
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    const uint32_t km = okey(vl[mid]);
+                    if (km > ki || (km == ki && il2[mid] < ii)) lo = mid + 1;
+                    else hi = mid;
+                }
+                r += lo;
+            }
+        } else {
+            for (int j = 0; j < n; j++) {
+                const uint32_t kj = okey(v[j]);
+                r += kj > ki || (kj == ki && id[j] < ii);
+            }
         }
         if (r < k) {
             tl[r] = v[i];

@@ -185,3 +185,4 @@ def test_merge_rejects_rows_the_candidates_cannot_serve():
     with pytest.raises(capi.DllmError):
         capi.merge_sample(torch.stack(vs).contiguous(), torch.stack(is_).contiguous(),
                           torch.from_numpy(uni).to(dev), dict(good, top_k=k + 1))
+
