@@ -41,6 +41,8 @@ EXPORTS = [
     "dllm_cuda_set_timing_events", "dllm_cuda_shard_candidates", "dllm_cuda_merge_sample",
     "dllm_cuda_append_history", "dllm_cuda_lmhead_logits",
     "dllm_cuda_debug_inject_wait_timeout", "dllm_cuda_debug_fail_allocations",
+    "dllm_cuda_peer_exchange_create", "dllm_cuda_peer_exchange_open", "dllm_cuda_peer_exchange_close",
+    "dllm_cuda_peer_exchange_free", "dllm_cuda_shard_candidates_peer", "dllm_cuda_merge_sample_peer",
     "diskllm_grammar_init_from_file", "diskllm_grammar_init_from_str", "diskllm_grammar_init_json",
     "diskllm_grammar_free", "diskllm_grammar_reset", "diskllm_grammar_accept_str", "diskllm_grammar_advance",
     "diskllm_grammar_is_finished", "diskllm_grammar_apply_mask", "dllm_grammar_build_bitmask",
@@ -145,6 +147,18 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
     lib.dllm_cuda_debug_inject_wait_timeout.argtypes = [C.c_int, C.c_longlong]
     lib.dllm_cuda_debug_fail_allocations.restype = C.c_int
     lib.dllm_cuda_debug_fail_allocations.argtypes = [C.c_int]
+    for name, args in (("dllm_cuda_peer_exchange_create", [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+                       ("dllm_cuda_peer_exchange_open", [C.c_void_p, C.c_void_p]),
+                       ("dllm_cuda_peer_exchange_close", [C.c_void_p]),
+                       ("dllm_cuda_peer_exchange_free", [C.c_void_p]),
+                       ("dllm_cuda_shard_candidates_peer", [C.POINTER(BatchDesc), C.c_int64, C.c_int64, C.c_int,
+                                                            C.c_void_p, C.c_int, C.c_int, C.c_uint64, C.c_void_p]),
+                       ("dllm_cuda_merge_sample_peer", [C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_uint64,
+                                                        C.POINTER(SamplerParams), C.c_void_p, C.c_void_p, C.c_void_p,
+                                                        C.c_void_p, C.c_void_p])):
+        f = getattr(lib, name)
+        f.restype = C.c_int
+        f.argtypes = args
     lib.dllm_cuda_workspace_bytes.restype = C.c_size_t
     lib.dllm_cuda_workspace_bytes.argtypes = [C.POINTER(BatchDesc)]
     lib.dllm_cuda_version.restype = C.c_char_p
@@ -400,6 +414,61 @@ def shard_candidates(logits, vocab_offset, vocab_total, k, params=None, *, strea
     if check and rc != DLLM_OK:
         raise DllmError(f"dllm_cuda_shard_candidates: {STATUS_NAMES.get(rc, rc)} ({load_library().dllm_cuda_last_error().decode()})")
     return vals, ids
+
+
+def _check(rc, name):
+    if rc != DLLM_OK:
+        raise DllmError(f"{name}: {STATUS_NAMES.get(rc, rc)} ({load_library().dllm_cuda_last_error().decode()})")
+
+
+def peer_exchange_create(rows, k, world):
+    """This rank's peer exchange buffer: (device pointer, 64-byte IPC handle as bytes)."""
+    buf = C.c_void_p()
+    h = (C.c_ubyte * 64)()
+    _check(load_library().dllm_cuda_peer_exchange_create(int(rows), int(k), int(world), C.byref(buf), h),
+           "dllm_cuda_peer_exchange_create")
+    return buf.value, bytes(h)
+
+
+def peer_exchange_open(handle: bytes):
+    """Maps another rank's exchange buffer on this GPU; returns its device pointer here."""
+    h = (C.c_ubyte * 64).from_buffer_copy(handle)
+    p = C.c_void_p()
+    _check(load_library().dllm_cuda_peer_exchange_open(h, C.byref(p)), "dllm_cuda_peer_exchange_open")
+    return p.value
+
+
+def shard_candidates_peer(logits, vocab_offset, vocab_total, k, params, peers_dev, rank, world, epoch, *,
+                          stream=None, **kw):
+    """dllm_cuda_shard_candidates_peer: this GPU's candidates of step `epoch` into every rank's
+    exchange buffer (peers_dev: int64 CUDA tensor [world] of the buffers as mapped here)."""
+    import torch
+
+    rows = logits.shape[0]
+    dummy_u = torch.empty(max(rows, 1), dtype=torch.float32, device=logits.device)
+    d, _ = fill_desc(logits, dummy_u, params, **kw)
+    s = stream if stream is not None else torch.cuda.current_stream(logits.device).cuda_stream
+    _check(load_library().dllm_cuda_shard_candidates_peer(C.byref(d), int(vocab_offset), int(vocab_total), int(k),
+                                                          peers_dev.data_ptr(), int(rank), int(world), int(epoch), s),
+           "dllm_cuda_shard_candidates_peer")
+
+
+def merge_sample_peer(rows, world, k, local_buf, epoch, uniforms, params, *, row_params=None, token=None,
+                      status=None, stream=None):
+    """dllm_cuda_merge_sample_peer over this rank's exchange buffer for step `epoch`."""
+    import torch
+
+    if isinstance(params, dict):
+        params = make_params(**params)
+    if token is None:
+        token = torch.empty(rows, dtype=torch.int32, device=uniforms.device)
+    s = stream if stream is not None else torch.cuda.current_stream(uniforms.device).cuda_stream
+    rp = row_params.data_ptr() if row_params is not None else None
+    st = status.data_ptr() if status is not None else None
+    _check(load_library().dllm_cuda_merge_sample_peer(int(rows), int(world), int(k), local_buf, int(epoch),
+                                                      C.byref(params), rp, uniforms.data_ptr(), token.data_ptr(), st, s),
+           "dllm_cuda_merge_sample_peer")
+    return token
 
 
 def merge_sample(vals, ids, uniforms, params=None, *, row_params=None, token=None, status=None, stream=None,

@@ -260,6 +260,89 @@ extern "C" dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, cons
     return st;
 }
 
+// ----------------------------------------------------------------------------------------
+// peer exchange of vocabulary-sharded candidates (NVLink stores instead of a collective)
+
+extern "C" dllm_status dllm_cuda_peer_exchange_create(int rows, int k, int world, void **buf, void *ipc_handle) {
+    if (!buf || !ipc_handle) return DLLM_ERR_INVALID_ARG;
+    const size_t bytes = peer_exchange_bytes(rows, k, world);
+    if (!bytes) return DLLM_ERR_INVALID_ARG;
+    *buf = nullptr;
+    cudaError_t e = lib_malloc(buf, bytes);
+    if (e != cudaSuccess) {
+        set_error("peer exchange buffer", e);
+        *buf = nullptr;
+        return DLLM_ERR_OOM;
+    }
+    e = cudaMemset(*buf, 0, bytes);  // arrival counters start at zero
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(ipc_handle), *buf);
+    if (e != cudaSuccess) {
+        set_error("peer exchange buffer set-up", e);
+        cudaFree(*buf);
+        *buf = nullptr;
+        return DLLM_ERR_CUDA;
+    }
+    return DLLM_OK;
+}
+
+extern "C" dllm_status dllm_cuda_peer_exchange_open(const void *ipc_handle, void **peer_buf) {
+    if (!ipc_handle || !peer_buf) return DLLM_ERR_INVALID_ARG;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof h);
+    const cudaError_t e = cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+        set_error("cudaIpcOpenMemHandle", e);
+        return DLLM_ERR_CUDA;
+    }
+    return DLLM_OK;
+}
+
+extern "C" dllm_status dllm_cuda_peer_exchange_close(void *peer_buf) {
+    if (!peer_buf) return DLLM_ERR_INVALID_ARG;
+    return cudaIpcCloseMemHandle(peer_buf) == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
+}
+
+extern "C" dllm_status dllm_cuda_peer_exchange_free(void *buf) {
+    if (!buf) return DLLM_ERR_INVALID_ARG;
+    return cudaFree(buf) == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
+}
+
+extern "C" dllm_status dllm_cuda_shard_candidates_peer(const dllm_batch_desc *d, int64_t vocab_offset,
+                                                       int64_t vocab_total, int k, void *const *peer_bufs, int rank,
+                                                       int world, uint64_t epoch, void *stream) {
+    if (!d || d->rows < 0 || d->vocab <= 0 || (d->rows > 0 && !d->logits)) return DLLM_ERR_INVALID_ARG;
+    if (d->row_stride < d->vocab) return DLLM_ERR_INVALID_ARG;
+    if (d->dtype != DLLM_DTYPE_F32 && d->dtype != DLLM_DTYPE_BF16) return DLLM_ERR_INVALID_ARG;
+    if (d->mask && d->mask_stride < (d->vocab + 31) / 32) return DLLM_ERR_INVALID_ARG;
+    if ((d->hist_ids == nullptr) != (d->hist_off == nullptr)) return DLLM_ERR_INVALID_ARG;
+    if (vocab_offset < 0 || vocab_total <= 0 || vocab_offset + d->vocab > vocab_total) return DLLM_ERR_INVALID_ARG;
+    if (!peer_bufs || world < 1 || rank < 0 || rank >= world || epoch < 1 || k < 1) return DLLM_ERR_INVALID_ARG;
+    if (!peer_exchange_bytes(d->rows > 0 ? d->rows : 1, k, world)) return DLLM_ERR_INVALID_ARG;
+    if (d->flags & ~(unsigned)DLLM_MODE_PEN_TRUE_DIV) return DLLM_ERR_UNSUPPORTED;
+    PeerArgs px{peer_bufs, rank, world, (unsigned long long)epoch};
+    const dllm_status st = launch_shard_candidates(d, vocab_offset, vocab_total, k, nullptr, nullptr, nullptr,
+                                                   (cudaStream_t)stream, &px);
+    if (st == DLLM_ERR_CUDA) set_error("shard candidate kernel launch (peer exchange)", cudaGetLastError());
+    return st;
+}
+
+extern "C" dllm_status dllm_cuda_merge_sample_peer(int rows, int world, int k, const void *local_buf, uint64_t epoch,
+                                                   const dllm_sampler_params *params,
+                                                   const dllm_sampler_params *row_params, const float *uniforms,
+                                                   int32_t *token, int32_t *status, void *stream) {
+    if (rows < 0 || world < 1 || k < 1 || !params || !local_buf || epoch < 1) return DLLM_ERR_INVALID_ARG;
+    if (!peer_exchange_bytes(rows > 0 ? rows : 1, k, world)) return DLLM_ERR_INVALID_ARG;
+    if (rows > 0 && (!uniforms || !token)) return DLLM_ERR_INVALID_ARG;
+    if (!row_params && params->temperature != 0.0f && (params->top_k < 1 || params->top_k > k))
+        return DLLM_ERR_UNSUPPORTED;
+    const long long wait_ns = 2000000000ll;  // a rank that has not arrived after 2 s times the rows out
+    const dllm_status st = launch_merge_sample_peer(rows, world, k, local_buf, (unsigned long long)epoch, params,
+                                                    row_params, uniforms, token, status, wait_ns,
+                                                    (cudaStream_t)stream);
+    if (st == DLLM_ERR_CUDA) set_error("merge kernel launch (peer exchange)", cudaGetLastError());
+    return st;
+}
+
 static int topk_bound(const dllm_batch_desc *d) {
     int topk_max = d->row_params ? d->topk_max : d->params.top_k;
     if (topk_max >= d->vocab || topk_max < 0) topk_max = 0;

@@ -119,11 +119,24 @@ int lmh_max_rows(int hidden);
 dllm_status launch_lmhead(int rows, int hidden, int vocab, const float *h, const float *norm_w, float eps, int add_one,
                           const void *w, int w_dtype, float softcap, float *logits, float *scratch,
                           cudaStream_t stream);
+// Peer exchange of vocabulary-sharded candidates (see dllm_cuda_peer_exchange_create).
+struct PeerArgs {
+    void *const *peers;         // device array [world] of every rank's exchange buffer, mapped here
+    int rank, world;
+    unsigned long long epoch;   // step number, from 1
+};
+size_t peer_exchange_bytes(int rows, int k, int world);
 dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int64_t vtotal, int k, float *cand_val,
-                                    int32_t *cand_id, void *part, cudaStream_t stream);
+                                    int32_t *cand_id, void *part, cudaStream_t stream, const PeerArgs *px = nullptr);
+dllm_status launch_merge_sample_peer(int rows, int world, int k, const void *local_buf, unsigned long long epoch,
+                                     const dllm_sampler_params *params, const dllm_sampler_params *row_params,
+                                     const float *uniforms, int32_t *token, int32_t *status, long long wait_ns,
+                                     cudaStream_t stream);
 dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, const int32_t *ids,
                                 const dllm_sampler_params *params, const dllm_sampler_params *row_params,
-                                const float *uniforms, int32_t *token, int32_t *status, cudaStream_t stream);
+                                const float *uniforms, int32_t *token, int32_t *status, cudaStream_t stream,
+                                const unsigned long long *arrive = nullptr, unsigned long long target = 0,
+                                long long wait_ns = 0);
 dllm_status launch_sample(const KernelArgs &a, const LaunchCfg &cfg, cudaStream_t stream);
 int nrec_for(const LaunchCfg &cfg);
 

@@ -48,7 +48,25 @@ struct ShardArgs {
     int32_t *part_id;
     int32_t *status;
     unsigned long long *dbg;  // diagnostic counters (shard_stream_kernel phase cycles) or null
+    // peer exchange (null: write cand_val / cand_id): every rank's exchange buffer, mapped here
+    unsigned char *const *peers;
+    int p_rank, p_world, p_slot;
 };
+
+// Peer exchange buffer, one per rank (allocated by dllm_cuda_peer_exchange_create):
+//   [0, 256)            arrival counters, uint64 [world]: rank r's candidate CTAs add 1 per row
+//   then two slots      values float [world][rows][k], then ids int32 [world][rows][k]
+// Step e uses slot e & 1 and is complete on a rank when every counter reaches e * rows.
+constexpr size_t PX_HDR = 256;
+constexpr int PX_MAX_WORLD = 32;
+__host__ __device__ inline size_t px_slot_bytes(int world, int rows, int k) { return (size_t)world * rows * k * 8; }
+__host__ __device__ inline float *px_vals(unsigned char *base, int slot, int world, int rows, int k) {
+    return reinterpret_cast<float *>(base + PX_HDR + (size_t)slot * px_slot_bytes(world, rows, k));
+}
+__host__ __device__ inline int32_t *px_ids(unsigned char *base, int slot, int world, int rows, int k) {
+    return reinterpret_cast<int32_t *>(base + PX_HDR + (size_t)slot * px_slot_bytes(world, rows, k) +
+                                       (size_t)world * rows * k * 4);
+}
 
 // diagnostic counter slots of shard_stream_kernel (thread 0 of each row CTA adds its cycles)
 enum : int { SDBG_ROWS = 0, SDBG_LOOP = 1, SDBG_CUT = 2, SDBG_NCUT = 3, SDBG_FINAL = 4, SDBG_UNION = 5 };
@@ -856,9 +874,27 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
     __syncthreads();
     const long long t_union = a.dbg ? clock64() : 0;
     block_select(fk, fid, 0, nr + nh, a.k, sel, okey_s, oid_s);
-    for (int i = tid; i < a.k; i += NT) {
-        a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
-        a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
+    if (a.peers) {
+        // this row's candidates straight into every rank's exchange buffer (NVLink stores to the
+        // peers, no collective), then one arrival per rank, released after the stores
+        for (int i = tid; i < a.p_world * a.k; i += NT) {
+            const int pr = i / a.k, j = i - pr * a.k;
+            unsigned char *base = a.peers[pr];
+            const size_t o = ((size_t)a.p_rank * a.rows + row) * a.k + j;
+            px_vals(base, a.p_slot, a.p_world, a.rows, a.k)[o] = okey_inv(okey_s[j]);
+            px_ids(base, a.p_slot, a.p_world, a.rows, a.k)[o] = (int32_t)(oid_s[j] + a.voff);
+        }
+        __threadfence_system();
+        __syncthreads();
+        if (tid < a.p_world) {
+            unsigned long long *ctr = reinterpret_cast<unsigned long long *>(a.peers[tid]) + a.p_rank;
+            asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+        }
+    } else {
+        for (int i = tid; i < a.k; i += NT) {
+            a.cand_val[(int64_t)row * a.k + i] = okey_inv(okey_s[i]);
+            a.cand_id[(int64_t)row * a.k + i] = (int32_t)(oid_s[i] + a.voff);
+        }
     }
     if (a.dbg && tid == 0) {
         const long long t_end = clock64();
@@ -879,6 +915,10 @@ struct MergeArgs {
     const float *uniforms;
     int32_t *token;
     int32_t *status;       // [rows] or null
+    // peer exchange: wait until every rank's arrival counter here reaches `target` (bounded)
+    const unsigned long long *arrive;
+    unsigned long long target;
+    long long wait_ns;
 };
 
 constexpr int MG_THREADS = 256;
@@ -894,6 +934,40 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
     __shared__ float red_f[MG_THREADS / 32];
     __shared__ int red_i[MG_THREADS / 32];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x;
+    if (a.arrive) {
+        // every rank's candidates for this step have landed here once its counter reaches the
+        // target; the wait is bounded (a rank that never arrives makes the row DLLM_ROW_ERR_TIMEOUT)
+        __shared__ int s_late;
+        if (tid == 0) {
+            int late = 0;
+            unsigned long long t0;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+            for (int r = 0; r < a.nsh && !late; r++) {
+                for (;;) {
+                    unsigned long long c;
+                    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(c) : "l"(a.arrive + r) : "memory");
+                    if (c >= a.target) break;
+                    unsigned long long t;
+                    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+                    if ((long long)(t - t0) > a.wait_ns) {
+                        late = 1;
+                        break;
+                    }
+                    __nanosleep(200);
+                }
+            }
+            __threadfence();
+            s_late = late;
+        }
+        __syncthreads();
+        if (s_late) {
+            if (tid == 0) {
+                a.token[row] = 0;
+                if (a.status) a.status[row] = ROW_ERR_TIMEOUT;
+            }
+            return;
+        }
+    }
     const dllm_sampler_params p = a.rparams ? a.rparams[row] : a.bparams;
     // Sampling rows need 1 <= top_k <= k: the gathered lists hold each shard's k best, so a
     // larger top_k (or top-k off) cannot be served from them.  Such a row gets the greedy token
@@ -1001,7 +1075,7 @@ size_t shard_part_bytes(int rows, int vlocal, int k) {
 }
 
 dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int64_t vtotal, int k, float *cand_val,
-                                    int32_t *cand_id, void *part, cudaStream_t stream) {
+                                    int32_t *cand_id, void *part, cudaStream_t stream, const PeerArgs *px) {
     if (k < 1 || k > SH_KMAX || k > d->vocab) return DLLM_ERR_UNSUPPORTED;
     ShardArgs a = {};
     a.logits = d->logits;
@@ -1024,8 +1098,17 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     a.cand_id = cand_id;
     a.status = d->status;
     a.dbg = debug_counters();
+    if (px) {
+        a.peers = reinterpret_cast<unsigned char *const *>(px->peers);
+        a.p_rank = px->rank;
+        a.p_world = px->world;
+        a.p_slot = (int)(px->epoch & 1u);
+    }
     if (a.rows == 0) return DLLM_OK;
-    if (a.nchunks > 1) {
+    // the peer exchange is written by the streaming kernel only
+    const int hb0 = (d->hist_ids && d->hist_off) ? (d->hist_max > 0 ? d->hist_max : 0) : 0;
+    if (px && (k + hb0 > SH_KMAX || getenv("DLLM_SHARD_CHUNKED"))) return DLLM_ERR_UNSUPPORTED;
+    if (a.nchunks > 1 && !px) {
         if (!part) return DLLM_ERR_OOM;
         a.part_key = reinterpret_cast<uint32_t *>(part);
         a.part_id = reinterpret_cast<int32_t *>(a.part_key + (size_t)a.rows * a.nchunks * k);
@@ -1068,7 +1151,8 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
 
 dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, const int32_t *ids,
                                 const dllm_sampler_params *params, const dllm_sampler_params *row_params,
-                                const float *uniforms, int32_t *token, int32_t *status, cudaStream_t stream) {
+                                const float *uniforms, int32_t *token, int32_t *status, cudaStream_t stream,
+                                const unsigned long long *arrive, unsigned long long target, long long wait_ns) {
     if (nsh < 1 || k < 1 || k > SH_KMAX || nsh * k > MG_MAX) return DLLM_ERR_UNSUPPORTED;
     MergeArgs a = {};
     a.rows = rows;
@@ -1081,6 +1165,9 @@ dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, con
     a.uniforms = uniforms;
     a.token = token;
     a.status = status;
+    a.arrive = arrive;
+    a.target = target;
+    a.wait_ns = wait_ns;
     if (rows == 0) return DLLM_OK;
     const size_t smem = (size_t)nsh * k * 8 + (size_t)k * 8;
     if (cudaFuncSetAttribute((const void *)merge_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1088,6 +1175,23 @@ dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, con
         return DLLM_ERR_CUDA;
     merge_sample_kernel<<<rows, MG_THREADS, smem, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;
+}
+
+size_t peer_exchange_bytes(int rows, int k, int world) {
+    if (rows < 1 || k < 1 || world < 1 || world > PX_MAX_WORLD) return 0;
+    return PX_HDR + 2 * px_slot_bytes(world, rows, k);
+}
+
+dllm_status launch_merge_sample_peer(int rows, int world, int k, const void *local_buf, unsigned long long epoch,
+                                     const dllm_sampler_params *params, const dllm_sampler_params *row_params,
+                                     const float *uniforms, int32_t *token, int32_t *status, long long wait_ns,
+                                     cudaStream_t stream) {
+    unsigned char *base = reinterpret_cast<unsigned char *>(const_cast<void *>(local_buf));
+    const int slot = (int)(epoch & 1u);
+    return launch_merge_sample(rows, world, k, px_vals(base, slot, world, rows, k), px_ids(base, slot, world, rows, k),
+                               params, row_params, uniforms, token, status, stream,
+                               reinterpret_cast<const unsigned long long *>(base), epoch * (unsigned long long)rows,
+                               wait_ns);
 }
 
 }  // namespace dllm

@@ -84,3 +84,49 @@ def sample_vocab_sharded(logits_shard: torch.Tensor, vocab_offset: int, vocab_to
     vals, ids = capi.shard_candidates(logits_shard, vocab_offset, vocab_total, k, params, mask=mask_shard,
                                       hist_ids=hist_ids, hist_off=hist_off, hist_max=hist_max)
     return capi.merge_sample(vals.unsqueeze(0), ids.unsqueeze(0), uniforms, params)
+
+
+class PeerExchange:
+    """The NVLink peer exchange for vocabulary-sharded sampling, one per (rows, k) on every rank of
+    `group`: each rank's candidate kernel stores its rows' candidates straight into every rank's
+    buffer (CUDA IPC mappings exchanged once through the process group), so no collective runs on
+    the data path.  Steps must run on every rank, in the same order."""
+
+    def __init__(self, rows: int, k: int, device, group=None):
+        self.rows, self.k, self.group = int(rows), int(k), group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.local, handle = capi.peer_exchange_create(self.rows, self.k, self.world)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.mapped = []
+        ptrs = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self.local)
+            else:
+                p = capi.peer_exchange_open(h)
+                self.mapped.append(p)
+                ptrs.append(p)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self.epoch = 0
+        dist.barrier(group=group)  # every rank has mapped every buffer before any store
+
+    def sample(self, logits_shard, vocab_offset, vocab_total, uniforms, params, *, mask_shard=None, hist_ids=None,
+               hist_off=None, hist_max=None, token=None, status=None):
+        """One step: this rank's candidates into every buffer, then the merge on this rank."""
+        self.epoch += 1
+        capi.shard_candidates_peer(logits_shard, vocab_offset, vocab_total, self.k, params, self.peers, self.rank,
+                                   self.world, self.epoch, mask=mask_shard, hist_ids=hist_ids, hist_off=hist_off,
+                                   hist_max=hist_max)
+        return capi.merge_sample_peer(self.rows, self.world, self.k, self.local, self.epoch, uniforms, params,
+                                      token=token, status=status)
+
+    def close(self):
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no rank stores into a buffer being unmapped
+        lib = capi.load_library()
+        for p in self.mapped:
+            lib.dllm_cuda_peer_exchange_close(p)
+        lib.dllm_cuda_peer_exchange_free(self.local)
+        self.mapped = []

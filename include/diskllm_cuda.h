@@ -214,6 +214,37 @@ DLLM_API dllm_status dllm_cuda_merge_sample(int rows, int nshards, int k, const 
                                             const float *uniforms, int32_t *token, int32_t *status,
                                             void *stream);
 
+/* Peer exchange for vocabulary-sharded sampling (no counterpart in the reference): the candidate
+ * kernel stores each row's k candidates straight into every rank's exchange buffer over NVLink
+ * (plain peer stores, no multicast) and counts the row in that rank's arrival counter, so the
+ * exchange overlaps the candidate computation row by row instead of following it as a collective.
+ *   dllm_cuda_peer_exchange_create: on each rank, a zeroed device buffer for `rows` x `k`
+ *     candidates of `world` ranks (arrival counters, then two slots used by alternate steps) and
+ *     its cudaIpcMemHandle (64 bytes, written to ipc_handle) for the other ranks.
+ *   dllm_cuda_peer_exchange_open / _close: map / unmap another rank's buffer on this GPU.
+ *   dllm_cuda_peer_exchange_free: release this rank's buffer.
+ *   dllm_cuda_shard_candidates_peer: step `epoch` (1, 2, ...; the same on every rank) of
+ *     dllm_cuda_shard_candidates, writing into every rank's buffer; peer_bufs is a DEVICE array
+ *     [world] of the buffers as mapped on this GPU (this rank's own buffer at index rank).
+ *     Needs k + the history bound <= 256.
+ *   dllm_cuda_merge_sample_peer: dllm_cuda_merge_sample over this rank's buffer for step `epoch`;
+ *     each row's block waits until every rank's rows have arrived.  The wait is bounded: a rank
+ *     missing after 2 s makes the rows time out (token 0, status DLLM_ROW_ERR_TIMEOUT) and the
+ *     kernel returns.
+ * Every rank must run every step, in the same order, on one stream per rank: a rank's next step's
+ * stores reuse the slot of the step before last, which every rank has finished merging by then. */
+DLLM_API dllm_status dllm_cuda_peer_exchange_create(int rows, int k, int world, void **buf, void *ipc_handle);
+DLLM_API dllm_status dllm_cuda_peer_exchange_open(const void *ipc_handle, void **peer_buf);
+DLLM_API dllm_status dllm_cuda_peer_exchange_close(void *peer_buf);
+DLLM_API dllm_status dllm_cuda_peer_exchange_free(void *buf);
+DLLM_API dllm_status dllm_cuda_shard_candidates_peer(const dllm_batch_desc *desc, int64_t vocab_offset,
+                                                     int64_t vocab_total, int k, void *const *peer_bufs, int rank,
+                                                     int world, uint64_t epoch, void *stream);
+DLLM_API dllm_status dllm_cuda_merge_sample_peer(int rows, int world, int k, const void *local_buf, uint64_t epoch,
+                                                 const dllm_sampler_params *params,
+                                                 const dllm_sampler_params *row_params, const float *uniforms,
+                                                 int32_t *token, int32_t *status, void *stream);
+
 /* The step before the sampler (src/core/context.c:854-876): the final RMSNorm of `rows` hidden
  * states h [rows][hidden] (fp32; src/rmsnorm.c:4-27, norm_w may be NULL, add_one for Gemma's
  * (w + 1)), the logits matvec against unquantised output weights w [vocab][hidden]

@@ -1,4 +1,5 @@
-"""Multi-GPU run (2, 4 or 8 ranks) of vocabulary-sharded sampling through NCCL (launched by test_gpu_sharded.py with
+"""Multi-GPU run (2, 4 or 8 ranks; DLLM_TEST_EXCHANGE=peer for the NVLink peer exchange instead of
+the NCCL all-gather) of vocabulary-sharded sampling through NCCL (launched by test_gpu_sharded.py with
 torch.distributed.run).  Every rank builds the same seeded rows, samples from its own columns
 with sharded.sample_vocab_sharded, and checks that all ranks drew the same tokens; rank 0 checks
 them against the whole-row oracle."""
@@ -30,21 +31,35 @@ def main():
     mask = pack_mask(allow)
     s, e = sharded.shard_range(V, rank, world)
     hid, hoff = (torch.from_numpy(a).to(dev) for a in csr(hist))
-    tok = sharded.sample_vocab_sharded(
-        x[:, s:e].contiguous().to(dev), s, V, torch.from_numpy(uni).to(dev), params, k=64,
-        mask_shard=torch.from_numpy(mask[:, s // 32:(e + 31) // 32].copy().view(np.int32)).to(dev),
-        hist_ids=hid, hist_off=hoff)
-    allt = [torch.empty_like(tok) for _ in range(world)]
-    dist.all_gather(allt, tok)
-    same = all(torch.equal(allt[0], t) for t in allt)
-    if rank == 0:
-        ora = O.sample_restated(x.float().numpy(), params, uni, mask=mask, hist=hist, kept_cap=64, topk_cap=64)
-        t = tok.cpu().numpy()
-        bad = [r for r in range(rows) if not ids_match(int(t[r]), ora, uni, r)]
-        if same and not bad:
-            print("SHARDED_NCCL_OK", flush=True)
+    xs = x[:, s:e].contiguous().to(dev)
+    ms = torch.from_numpy(mask[:, s // 32:(e + 31) // 32].copy().view(np.int32)).to(dev)
+    peer = os.environ.get("DLLM_TEST_EXCHANGE") == "peer"
+    px = sharded.PeerExchange(rows, 64, dev) if peer else None
+    ok = True
+    # three steps with different uniforms (the peer exchange alternates its two slots)
+    for step in range(3):
+        us = np.roll(uni, step).copy()
+        ut = torch.from_numpy(us).to(dev)
+        if peer:
+            st = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+            tok = px.sample(xs, s, V, ut, params, mask_shard=ms, hist_ids=hid, hist_off=hoff, hist_max=128, status=st)
+            ok &= bool((st == 0).all().item())
         else:
-            print("MISMATCH same-on-all-ranks", same, "bad rows", bad[:8], flush=True)
+            tok = sharded.sample_vocab_sharded(xs, s, V, ut, params, k=64, mask_shard=ms, hist_ids=hid, hist_off=hoff)
+        allt = [torch.empty_like(tok) for _ in range(world)]
+        dist.all_gather(allt, tok)
+        same = all(torch.equal(allt[0], t) for t in allt)
+        if rank == 0:
+            ora = O.sample_restated(x.float().numpy(), params, us, mask=mask, hist=hist, kept_cap=64, topk_cap=64)
+            t = tok.cpu().numpy()
+            bad = [r for r in range(rows) if not ids_match(int(t[r]), ora, us, r)]
+            if not (same and not bad):
+                ok = False
+                print("MISMATCH step", step, "same-on-all-ranks", same, "bad rows", bad[:8], flush=True)
+    if px is not None:
+        px.close()
+    if rank == 0 and ok:
+        print("SHARDED_NCCL_OK", flush=True)
     dist.barrier()
     dist.destroy_process_group()
 

@@ -135,16 +135,20 @@ def test_greedy():
     _run(x, None, hist, params, 4, 8)
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_nccl_ranks(world):
-    """world ranks, one per GPU, each sampling from its own columns; candidates all-gathered by NCCL"""
+def test_nccl_ranks(world, exchange, shard_path):
+    """world ranks, one per GPU, each sampling from its own columns; candidates all-gathered by NCCL
+    or stored into every rank's buffer over NVLink (three steps each)"""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
+    if exchange == "peer" and shard_path == "chunked":
+        pytest.skip("the peer exchange is written by the streaming candidate kernel")
     script = os.path.join(ROOT, "tests", "sharded_nccl_worker.py")
     env = dict(os.environ, PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "tests"),
-                                                      os.path.join(ROOT, "oracle")]))
+                                                      os.path.join(ROOT, "oracle")]), DLLM_TEST_EXCHANGE=exchange)
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
-           "--master-addr=127.0.0.1", f"--master-port={29613 + world}", script]
+           "--master-addr=127.0.0.1", f"--master-port={29613 + world + (8 if exchange == 'peer' else 0)}", script]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-2000:]
     assert "SHARDED_NCCL_OK" in res.stdout
@@ -186,3 +190,64 @@ def test_merge_rejects_rows_the_candidates_cannot_serve():
         capi.merge_sample(torch.stack(vs).contiguous(), torch.stack(is_).contiguous(),
                           torch.from_numpy(uni).to(dev), dict(good, top_k=k + 1))
 
+
+
+def _peer_single(world, rows, k):
+    buf, _ = capi.peer_exchange_create(rows, k, world)
+    return buf
+
+
+def test_peer_exchange_on_one_gpu_matches_oracle(shard_path):
+    """world 1: the candidate kernel stores into this GPU's exchange buffer and the merge reads it,
+    for two steps (both slots)"""
+    if shard_path == "chunked":
+        pytest.skip("the peer exchange is written by the streaming candidate kernel")
+    rng = np.random.default_rng(17)
+    rows, V, k = 8, 20000, 40
+    x = _bf16_grid((rng.standard_normal((rows, V)) * 2.0).astype(np.float32))
+    hist = [rng.integers(0, V, 64) for _ in range(rows)]
+    params = dict(temperature=0.9, top_k=32, top_p=0.9, repetition=1.1)
+    dev = torch.device("cuda", 0)
+    xt = torch.from_numpy(x).to(dev).to(torch.bfloat16)
+    hid, hoff = (torch.from_numpy(a).to(dev) for a in csr(hist))
+    buf = _peer_single(1, rows, k)
+    peers = torch.tensor([buf], dtype=torch.int64, device=dev)
+    try:
+        for epoch in (1, 2):
+            uni = u24(rng, rows)
+            capi.shard_candidates_peer(xt, 0, V, k, params, peers, 0, 1, epoch, hist_ids=hid, hist_off=hoff,
+                                       hist_max=64)
+            st = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+            tok = capi.merge_sample_peer(rows, 1, k, buf, epoch, torch.from_numpy(uni).to(dev), params, status=st)
+            torch.cuda.synchronize()
+            ora = O.sample_restated(x, params, uni, hist=hist, kept_cap=k, topk_cap=k)
+            t = tok.cpu().numpy()
+            assert np.all(st.cpu().numpy() == 0)
+            assert all(ids_match(int(t[r]), ora, uni, r) for r in range(rows)), (t, ora.token)
+    finally:
+        capi.load_library().dllm_cuda_peer_exchange_free(buf)
+
+
+def test_peer_merge_times_out_when_a_rank_never_arrives(shard_path):
+    """a two-rank exchange in which nothing is ever stored: the merge's bounded wait gives up
+    (about 2 s), every row gets DLLM_ROW_ERR_TIMEOUT, and the context stays usable"""
+    import time
+
+    if shard_path == "chunked":
+        pytest.skip("one run is enough")
+    rows, k = 4, 16
+    dev = torch.device("cuda", 0)
+    buf = _peer_single(2, rows, k)
+    try:
+        st = torch.full((rows,), -1, dtype=torch.int32, device=dev)
+        t0 = time.time()
+        capi.merge_sample_peer(rows, 2, k, buf, 1, torch.zeros(rows, device=dev), dict(temperature=1.0, top_k=8),
+                               status=st)
+        torch.cuda.synchronize()
+        assert time.time() - t0 < 30
+        assert np.all(st.cpu().numpy() == capi.ROW_ERR_TIMEOUT)
+    finally:
+        capi.load_library().dllm_cuda_peer_exchange_free(buf)
+    x = torch.randn(2, 1000, device=dev)
+    capi.sample_batch(x, torch.full((2,), 0.5, device=dev), dict(temperature=1.0, top_k=5))
+    torch.cuda.synchronize()
