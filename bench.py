@@ -558,7 +558,14 @@ def cfg5_result(args, rank, world, dev):
     params = dict(w.params)
     w.logits = None  # the rank keeps only its shard
 
+    # N > 1: the NVLink peer exchange (the candidate kernel stores into every rank's buffer) unless
+    # --gather nccl asks for the all-gather
+    px = sharded.PeerExchange(CFG5_ROWS, CFG5_K, dev) if world > 1 and args.gather == "peer" else None
+
     def step():
+        if px is not None:
+            return px.sample(x, s, CFG5_VOCAB, w.uniforms, params, mask_shard=m, hist_ids=w.hist_ids,
+                             hist_off=w.hist_off, hist_max=CFG5_HIST)
         return sharded.sample_vocab_sharded(x, s, CFG5_VOCAB, w.uniforms, params, k=CFG5_K, mask_shard=m,
                                             hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=CFG5_HIST)
 
@@ -577,12 +584,32 @@ def cfg5_result(args, rank, world, dev):
     ms_step, _ = timed_steps(step, steps, dev, world, flush)
     clocks.stop()
 
-    # the three parts of a step, each timed with its own events (candidates, all-gather, merge)
+    # the parts of a step, each timed with its own events: candidates, all-gather, merge (with the
+    # peer exchange: candidates with their stores to every rank, then the merge with its wait)
     stream = torch.cuda.current_stream(dev)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
     parts = [0.0, 0.0, 0.0]
+    if px is not None:
+        for _ in range(steps):
+            if flush is not None:
+                flush()
+            torch.distributed.barrier()
+            px.epoch += 1
+            ev[0].record(stream)
+            capi.shard_candidates_peer(x, s, CFG5_VOCAB, CFG5_K, params, px.peers, px.rank, px.world, px.epoch,
+                                       mask=m, hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=CFG5_HIST)
+            ev[1].record(stream)
+            ev[2].record(stream)
+            capi.merge_sample_peer(CFG5_ROWS, px.world, CFG5_K, px.local, px.epoch, w.uniforms, params)
+            ev[3].record(stream)
+            torch.cuda.synchronize(dev)
+            for j in range(3):
+                parts[j] += ev[j].elapsed_time(ev[j + 1]) / steps
+        steps_parts = 0
+    else:
+        steps_parts = steps
     buf, vals, ids = sharded.candidate_buffer(CFG5_ROWS, CFG5_K, dev)
-    for _ in range(steps):
+    for _ in range(steps_parts):
         if flush is not None:
             flush()
         if world > 1:
@@ -610,8 +637,12 @@ def cfg5_result(args, rank, world, dev):
 
     def e2e_step():
         d_x.copy_(h_x, non_blocking=True)
-        tok = sharded.sample_vocab_sharded(d_x, s, CFG5_VOCAB, w.uniforms, params, k=CFG5_K, mask_shard=m,
-                                           hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=CFG5_HIST)
+        if px is not None:
+            tok = px.sample(d_x, s, CFG5_VOCAB, w.uniforms, params, mask_shard=m, hist_ids=w.hist_ids,
+                            hist_off=w.hist_off, hist_max=CFG5_HIST)
+        else:
+            tok = sharded.sample_vocab_sharded(d_x, s, CFG5_VOCAB, w.uniforms, params, k=CFG5_K, mask_shard=m,
+                                               hist_ids=w.hist_ids, hist_off=w.hist_off, hist_max=CFG5_HIST)
         h_tok.copy_(tok, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 20))
@@ -628,6 +659,8 @@ def cfg5_result(args, rank, world, dev):
     e1.record(stream)
     torch.cuda.synchronize(dev)
     ms_e2e = max_over_ranks(e0.elapsed_time(e1), dev, world)
+    if px is not None:
+        px.close()
     if rank != 0:
         return None
     cols = e - s
@@ -641,16 +674,19 @@ def cfg5_result(args, rank, world, dev):
         "data": "synthetic (seeded N(0,2^2) bf16 rows, 10% mask, uniform histories, Philox uniforms)",
         "config": {"workload": "cfg5_vocab_parallel_b512_v262144_bf16 (BASELINE config 5)",
                    "global_batch": CFG5_ROWS, "vocab": CFG5_VOCAB, "columns_per_gpu": cols, "top_k_per_shard": CFG5_K,
-                   "params": params, "parallelism": f"vocab-sharded x{world} (NCCL all-gather of candidates)",
+                   "params": params, "parallelism": f"vocab-sharded x{world}",
                    "l2_policy": ("L2 flushed (256 MB write) before each timed step: the shard is "
                                  f"{shard_bytes / 1e6:.0f} MB") if flush is not None else
                                 f"shard ({shard_bytes / 1e6:.0f} MB) larger than twice the L2; no flush"},
-        "parts_ms": {"candidates": parts[0], "all_gather": parts[1], "merge": parts[2]},
+        "parts_ms": ({"candidates_with_peer_stores": parts[0], "merge_with_arrival_wait": parts[2]}
+                     if px is not None else {"candidates": parts[0], "all_gather": parts[1], "merge": parts[2]}),
+        "exchange": "NVLink peer stores from the candidate kernel" if px is not None else
+                    ("NCCL all-gather" if world > 1 else "none (one GPU)"),
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                      else "fallback 6650 GB/s",
                      "traffic": None, "algorithmic_bytes_per_gpu_step": bytes_per_gpu,
-                     "kernel": "shard_stream_kernel + all-gather + merge_sample_kernel (whole step)"},
+                     "kernel": "shard_stream_kernel + exchange + merge_sample_kernel (whole step)"},
         "e2e": {"value": CFG5_ROWS / (ms_e2e / e2e_steps / 1e3), "unit": "rows/s",
                 "h2d_bytes_per_step": h_x.numel() * 2, "d2h_bytes_per_step": CFG5_ROWS * 4},
         "gpu_launches": 2 * steps,
@@ -800,6 +836,8 @@ def main():
                     help="headline only: skip the configuration 1, 2, 3 and 5 legs")
     ap.add_argument("--emulate-shards", type=int, default=1,
                     help="cfg5 on one GPU: take 1 of N column shards (no all-gather)")
+    ap.add_argument("--gather", choices=["peer", "nccl"], default="peer",
+                    help="cfg5 with N > 1: NVLink peer stores from the candidate kernel, or the NCCL all-gather")
     ap.add_argument("--profile-only", action="store_true",
                     help="cfg5: only warm-up and `steps` plain steps, no timing legs (for ncu captures)")
     ap.add_argument("--workload", choices=["cfg4", "cfg5", "cfg1", "cfg2", "cfg3", "sorted", "lmhead"],
