@@ -490,10 +490,13 @@ __global__ void __launch_bounds__(SH_T) shard_rowmerge_kernel(const ShardArgs a)
 // penalised value), because at most H of the K' best raw entries are history ids.  The union is
 // selected by (key desc, id asc) once more.  Used when k + the history bound <= SH_KMAX.
 constexpr int ST_T = 256;          // threads per row CTA
-constexpr int ST_U = 1;            // 16-byte vectors per thread per tile
+constexpr int ST_U = 2;            // 16-byte vectors per thread per tile
 constexpr int ST_PD = 12;          // tiles pulled into L2 ahead of the loads
 constexpr int ST_CAP = 4608;       // candidate buffer entries
 constexpr int ST_FIN = 2 * SH_KMAX;  // final union entries
+// A cut leaves at most SH_KMAX entries and a tile appends at most one per column (8 per bf16
+// vector), so the buffer never overflows when a tile starts at or below ST_CAP - E.
+static_assert(ST_CAP >= ST_T * ST_U * 8 + SH_KMAX, "candidate buffer smaller than a tile plus a cut");
 
 template <int DT>
 __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a, int kprime) {
