@@ -494,9 +494,85 @@ constexpr int ST_U = 2;            // 16-byte vectors per thread per tile
 constexpr int ST_PD = 12;          // tiles pulled into L2 ahead of the loads
 constexpr int ST_CAP = 4608;       // candidate buffer entries
 constexpr int ST_FIN = 2 * SH_KMAX;  // final union entries
+static_assert(ST_FIN <= 2 * ST_T, "union_select sorts 2 * ST_T entries, two per thread");
 // A cut leaves at most SH_KMAX entries and a tile appends at most one per column (8 per bf16
 // vector), so the buffer never overflows when a tile starts at or below ST_CAP - E.
 static_assert(ST_CAP >= ST_T * ST_U * 8 + SH_KMAX, "candidate buffer smaller than a tile plus a cut");
+
+// The K best of n <= ST_FIN entries by (key desc, id asc), written sorted to out_key / out_id
+// like block_select: a bitonic sort in shared memory (`tmp`, ST_FIN entries of 8 bytes) of the
+// composites key << 32 | ~id, whose descending order is exactly that ranking.  Keys below the
+// -inf key (negative NaN) are never taken by block_select, which runs instead when one is present.
+__device__ void union_select(const uint32_t *keys, const int *ids, int n, int K, unsigned long long *tmp,
+                             SelScratch &s, uint32_t *out_key, int *out_id) {
+    const int tid = threadIdx.x, NT = blockDim.x;
+    const uint32_t KNEG = okey(-INFINITY);
+    bool odd = false;
+    for (int i = tid; i < n; i += NT) odd |= keys[i] < KNEG;
+    if (__syncthreads_or(odd) || n > ST_FIN) {
+        block_select(keys, ids, 0, n, K, s, out_key, out_id);
+        return;
+    }
+    // 512 composites (zero padding, which sorts last), two per thread: thread t holds 2t and
+    // 2t + 1, so pairs closer than 64 apart are in one warp and are exchanged by shuffles; the
+    // stages with pairs 64 or more apart go through shared memory.
+    const int e0 = 2 * tid;
+    unsigned long long v[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = e0 + r;
+        v[r] = i < n ? ((unsigned long long)keys[i] << 32) | (uint32_t)~(uint32_t)ids[i] : 0ull;
+    }
+    auto reg_stages = [&](int k, int jtop) {
+        for (int j = jtop; j >= 2; j >>= 1) {
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const int e = e0 + r;
+                const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], j >> 1);
+                const bool desc = ((e & ~j) & k) == 0;  // descending runs where bit k of the pair is clear
+                const bool keep_max = ((e & j) == 0) == desc;
+                v[r] = keep_max ? (v[r] > o ? v[r] : o) : (v[r] < o ? v[r] : o);
+            }
+        }
+        const bool desc = (e0 & k) == 0;
+        if ((v[0] < v[1]) == desc) {
+            const unsigned long long t = v[0];
+            v[0] = v[1];
+            v[1] = t;
+        }
+    };
+    for (int k = 2; k <= 64; k <<= 1) reg_stages(k, k >> 1);
+    for (int k = 128; k <= 2 * ST_T; k <<= 1) {
+        tmp[e0] = v[0];
+        tmp[e0 + 1] = v[1];
+        __syncthreads();
+        for (int j = k >> 1; j >= 64; j >>= 1) {
+            const int i = tid;  // one pair per thread
+            const int lo = ((i & ~(j - 1)) << 1) | (i & (j - 1)), hi = lo + j;
+            const unsigned long long x = tmp[lo], y = tmp[hi];
+            if (((lo & k) == 0) == (x < y)) {
+                tmp[lo] = y;
+                tmp[hi] = x;
+            }
+            __syncthreads();
+        }
+        v[0] = tmp[e0];
+        v[1] = tmp[e0 + 1];
+        reg_stages(k, 32);
+        __syncthreads();  // every thread has read tmp before the next stores
+    }
+    tmp[e0] = v[0];
+    tmp[e0 + 1] = v[1];
+    __syncthreads();
+    // a real composite is never 0 (its low word ~id has the top bit set), so positions past n
+    // are the padding, written as block_select writes them
+    for (int i = tid; i < K; i += NT) {
+        const unsigned long long c = i < n ? tmp[i] : 0ull;
+        out_key[i] = i < n ? (uint32_t)(c >> 32) : 0u;
+        out_id[i] = i < n ? (int)~(uint32_t)c : INT_MAX;
+    }
+    __syncthreads();
+}
 
 template <int DT>
 __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a, int kprime) {
@@ -824,36 +900,59 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
     __syncthreads();
     const long long t_loop = a.dbg ? clock64() : 0;
     const long long t_cut_loop = t_cut;
-    cut();
+    // The buffer holds the K' best raw entries (and others that beat the threshold of their
+    // time), so the union below may take all of it: a final cut is needed only when the buffer
+    // and the history entries would not fit the union area.
+    if (s_nb + nhist > ST_FIN) cut();
     const long long t_fcut = a.dbg ? clock64() : 0;
     // the union: the K' best raw entries that are not history ids, and each history id of this
-    // shard once, with its penalised value (src/sampler.c:21-52, after the mask)
+    // shard once, with its penalised value (src/sampler.c:21-52, after the mask).  The shard's
+    // history ids go into an open-addressing set of local ids (HT_SLOTS slots, at most SH_KMAX
+    // used) over sel.hist and sel.ck, which are free here; the set also drops repeated ids.
+    constexpr int HT_SLOTS = 512;
+    static_assert(sizeof(sel.hist) + sizeof(sel.ck) >= HT_SLOTS * sizeof(int), "history set");
+    int *htab = reinterpret_cast<int *>(sel.hist);
+    auto hslot = [](int li) { return (int)(((uint32_t)li * 2654435761u) >> 23); };  // 9 bits
     const int nraw = s_nb;
     if (tid == 0) s_nh = 0;
-    __syncthreads();
     if (pen) {
+        for (int i = tid; i < HT_SLOTS; i += NT) htab[i] = -1;
+        __syncthreads();
         for (int j = tid; j < nhist; j += NT) {
             const int id = hall[j];
             if (id < 0 || id >= a.vtotal) continue;
-            const int64_t li = (int64_t)id - a.voff;
-            if (li < 0 || li >= n) continue;
-            // the first occurrence of the id stands for all of them
-            bool firstocc = true;
-            for (int q = 0; q < j && firstocc; q++) firstocc = hall[q] != id;
-            if (!firstocc) continue;
-            const int at = atomicAdd(&s_nh, 1);
-            if (at < SH_KMAX) hl[at] = (int)li;
+            const int64_t li64 = (int64_t)id - a.voff;
+            if (li64 < 0 || li64 >= n) continue;
+            const int li = (int)li64;
+            for (int h = hslot(li);; h = (h + 1) & (HT_SLOTS - 1)) {
+                const int prev = atomicCAS(&htab[h], -1, li);
+                if (prev == -1) {  // first occurrence: it stands for all of them
+                    hl[atomicAdd(&s_nh, 1)] = li;
+                    break;
+                }
+                if (prev == li) break;
+            }
         }
     }
     __syncthreads();
-    const int nh = min(s_nh, SH_KMAX);
+    const int nh = s_nh;
     // the raw entries that are not history ids (their order does not matter: the select ranks
     // by key and id)
     if (tid == 0) s_nb = 0;
     __syncthreads();
     for (int i = tid; i < nraw; i += NT) {
         bool inhist = false;
-        for (int q = 0; q < nh && !inhist; q++) inhist = hl[q] == bid[i];
+        if (nh > 0) {
+            const int li = bid[i];
+            for (int h = hslot(li);; h = (h + 1) & (HT_SLOTS - 1)) {
+                const int t = htab[h];
+                if (t == -1) break;
+                if (t == li) {
+                    inhist = true;
+                    break;
+                }
+            }
+        }
         if (!inhist) {
             const int at = atomicAdd(&s_nb, 1);
             fk[at] = bk[i];
@@ -876,7 +975,7 @@ __global__ void __launch_bounds__(ST_T, 4) shard_stream_kernel(const ShardArgs a
     }
     __syncthreads();
     const long long t_union = a.dbg ? clock64() : 0;
-    block_select(fk, fid, 0, nr + nh, a.k, sel, okey_s, oid_s);
+    union_select(fk, fid, nr + nh, a.k, reinterpret_cast<unsigned long long *>(bk), sel, okey_s, oid_s);
     if (a.peers) {
         // this row's candidates straight into every rank's exchange buffer (NVLink stores to the
         // peers, no collective), then one arrival per rank, released after the stores
