@@ -484,10 +484,12 @@ __global__ void __launch_bounds__(SH_T) shard_rowmerge_kernel(const ShardArgs a)
 //    only keys strictly above the K'-th (thr) can enter (an equal key arrives with a larger id and
 //    loses the tie), so after the first few tiles almost nothing is appended;
 //  * the first tile's threshold comes from group maxima (at least K' entries reach it);
-//  * one barrier per tile decides whether the buffer must be cut (block_select on it).
+//  * one barrier per tile decides whether the buffer must be cut (to the entries at or above its
+//    K'-th key);
 // History penalties are applied afterwards, exactly: the true top-k is contained in (the K' best
 // raw entries that are not history ids) united with (every history id of this shard, with its
-// penalised value), because at most H of the K' best raw entries are history ids.  The union is
+// penalised value), because at most H of the K' best raw entries are history ids.  The buffer
+// holds the K' best raw entries, so the union may take all of it when it fits.  The union is
 // selected by (key desc, id asc) once more.  Used when k + the history bound <= SH_KMAX.
 constexpr int ST_T = 256;          // threads per row CTA
 constexpr int ST_U = 2;            // 16-byte vectors per thread per tile
