@@ -493,7 +493,7 @@ __global__ void __launch_bounds__(SH_T) shard_rowmerge_kernel(const ShardArgs a)
 // selected by (key desc, id asc) once more.  Used when k + the history bound <= SH_KMAX.
 constexpr int ST_T = 256;          // threads per row CTA
 constexpr int ST_U = 2;            // 16-byte vectors per thread per tile
-constexpr int ST_PD = 12;          // tiles pulled into L2 ahead of the loads
+constexpr int ST_PD = 6;           // tiles pulled into L2 ahead of the loads
 constexpr int ST_CAP = 4608;       // candidate buffer entries
 constexpr int ST_FIN = 2 * SH_KMAX;  // final union entries
 static_assert(ST_FIN <= 2 * ST_T, "union_select sorts 2 * ST_T entries, two per thread");
