@@ -453,6 +453,15 @@ def shard_candidates_peer(logits, vocab_offset, vocab_total, k, params, peers_de
            "dllm_cuda_shard_candidates_peer")
 
 
+def shard_candidates_peer_desc(desc, vocab_offset, vocab_total, k, peers_dev, rank, world, epoch, stream):
+    """dllm_cuda_shard_candidates_peer on a batch descriptor already built by fill_desc (its
+    uniforms and token fields are not read); `stream` is a raw cudaStream_t value."""
+    _check(load_library().dllm_cuda_shard_candidates_peer(C.byref(desc), int(vocab_offset), int(vocab_total), int(k),
+                                                          peers_dev.data_ptr(), int(rank), int(world), int(epoch),
+                                                          stream),
+           "dllm_cuda_shard_candidates_peer")
+
+
 def merge_sample_peer(rows, world, k, local_buf, epoch, uniforms, params, *, row_params=None, token=None,
                       status=None, stream=None):
     """dllm_cuda_merge_sample_peer over this rank's exchange buffer for step `epoch`."""

@@ -20,6 +20,9 @@
 #include <cuda_runtime.h>
 #include <stdlib.h>
 
+#include <mutex>
+#include <vector>
+
 #include "dllm_chunk.cuh"
 
 namespace dllm {
@@ -1178,6 +1181,41 @@ size_t shard_part_bytes(int rows, int vlocal, int k) {
     return nch > 1 ? (size_t)rows * nch * k * 8 : 0;
 }
 
+
+// The dynamic shared memory limit of a shard kernel, raised once per (device, kernel) to the
+// largest size asked so far (a launch then costs no attribute call), and the DLLM_SHARD_CHUNKED
+// switch, read once per process.
+namespace {
+std::mutex g_shard_attr_mu;
+struct ShardAttr {
+    int dev;
+    const void *fn;
+    size_t smem;
+};
+std::vector<ShardAttr> g_shard_attr;
+}  // namespace
+
+static cudaError_t shard_smem_attr(const void *fn, size_t smem) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(g_shard_attr_mu);
+    ShardAttr *hit = nullptr;
+    for (auto &r : g_shard_attr)
+        if (r.dev == dev && r.fn == fn) hit = &r;
+    if (hit && hit->smem >= smem) return cudaSuccess;
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    if (hit) hit->smem = smem;
+    else g_shard_attr.push_back({dev, fn, smem});
+    return cudaSuccess;
+}
+
+static bool shard_chunked_env() {
+    static const bool on = getenv("DLLM_SHARD_CHUNKED") != nullptr;
+    return on;
+}
+
 dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int64_t vtotal, int k, float *cand_val,
                                     int32_t *cand_id, void *part, cudaStream_t stream, const PeerArgs *px) {
     if (k < 1 || k > SH_KMAX || k > d->vocab) return DLLM_ERR_UNSUPPORTED;
@@ -1211,26 +1249,25 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     if (a.rows == 0) return DLLM_OK;
     // the peer exchange is written by the streaming kernel only
     const int hb0 = (d->hist_ids && d->hist_off) ? (d->hist_max > 0 ? d->hist_max : 0) : 0;
-    if (px && (k + hb0 > SH_KMAX || getenv("DLLM_SHARD_CHUNKED"))) return DLLM_ERR_UNSUPPORTED;
+    if (px && (k + hb0 > SH_KMAX || shard_chunked_env())) return DLLM_ERR_UNSUPPORTED;
     if (a.nchunks > 1 && !px) {
         if (!part) return DLLM_ERR_OOM;
         a.part_key = reinterpret_cast<uint32_t *>(part);
         a.part_id = reinterpret_cast<int32_t *>(a.part_key + (size_t)a.rows * a.nchunks * k);
         const size_t rs = (size_t)a.nchunks * k * 8 + (size_t)SH_SURV * 8;
         if (rs > 200 * 1024) return DLLM_ERR_UNSUPPORTED;
-        if (cudaFuncSetAttribute((const void *)shard_rowmerge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)rs) != cudaSuccess)
+        if (shard_smem_attr((const void *)shard_rowmerge_kernel, rs) != cudaSuccess)
             return DLLM_ERR_CUDA;
     }
     if (a.status) cudaMemsetAsync(a.status, 0, (size_t)a.rows * sizeof(int32_t), stream);
     // one streaming CTA per row when the union of K' = k + history bound raw candidates and the
     // history entries fits the exact select
     const int hb = (d->hist_ids && d->hist_off) ? (d->hist_max > 0 ? d->hist_max : 0) : 0;
-    if (k + hb <= SH_KMAX && !getenv("DLLM_SHARD_CHUNKED")) {
+    if (k + hb <= SH_KMAX && !shard_chunked_env()) {
         const size_t ss = (size_t)ST_CAP * 8 + (size_t)ST_FIN * 8 + (size_t)SH_KMAX * 8;
         const void *fs = d->dtype == DLLM_DTYPE_BF16 ? (const void *)shard_stream_kernel<DLLM_DTYPE_BF16>
                                                      : (const void *)shard_stream_kernel<DLLM_DTYPE_F32>;
-        if (cudaFuncSetAttribute(fs, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ss) != cudaSuccess)
+        if (shard_smem_attr(fs, ss) != cudaSuccess)
             return DLLM_ERR_CUDA;
         if (d->dtype == DLLM_DTYPE_BF16)
             shard_stream_kernel<DLLM_DTYPE_BF16><<<a.rows, ST_T, ss, stream>>>(a, k + hb);
@@ -1242,7 +1279,7 @@ dllm_status launch_shard_candidates(const dllm_batch_desc *d, int64_t voff, int6
     const size_t ks = (size_t)SH_CHUNK * 4 + (size_t)SH_SURV * 8;  // keys, then the survivors
     const void *fn = d->dtype == DLLM_DTYPE_BF16 ? (const void *)shard_chunk_kernel<DLLM_DTYPE_BF16>
                                                  : (const void *)shard_chunk_kernel<DLLM_DTYPE_F32>;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ks) != cudaSuccess)
+    if (shard_smem_attr(fn, ks) != cudaSuccess)
         return DLLM_ERR_CUDA;
     if (d->dtype == DLLM_DTYPE_BF16)
         shard_chunk_kernel<DLLM_DTYPE_BF16><<<grid, SH_T, ks, stream>>>(a);
@@ -1274,8 +1311,7 @@ dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, con
     a.wait_ns = wait_ns;
     if (rows == 0) return DLLM_OK;
     const size_t smem = (size_t)nsh * k * 8 + (size_t)k * 8;
-    if (cudaFuncSetAttribute((const void *)merge_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)smem) != cudaSuccess)
+    if (shard_smem_attr((const void *)merge_sample_kernel, smem) != cudaSuccess)
         return DLLM_ERR_CUDA;
     merge_sample_kernel<<<rows, MG_THREADS, smem, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? DLLM_OK : DLLM_ERR_CUDA;

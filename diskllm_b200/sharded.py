@@ -110,17 +110,33 @@ class PeerExchange:
                 ptrs.append(p)
         self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
         self.epoch = 0
+        self._key = self._desc = self._prm = None
         dist.barrier(group=group)  # every rank has mapped every buffer before any store
 
     def sample(self, logits_shard, vocab_offset, vocab_total, uniforms, params, *, mask_shard=None, hist_ids=None,
                hist_off=None, hist_max=None, token=None, status=None):
-        """One step: this rank's candidates into every buffer, then the merge on this rank."""
+        """One step: this rank's candidates into every buffer, then the merge on this rank.  The
+        batch descriptor and the parameters are built once and kept while the tensors and settings
+        of later steps are the same (a decode loop over fixed buffers), so a step costs two
+        library calls on the host."""
+        ptr = lambda t: 0 if t is None else t.data_ptr()
+        pkey = tuple(sorted(params.items())) if isinstance(params, dict) else id(params)
+        key = (ptr(logits_shard), tuple(logits_shard.shape), tuple(logits_shard.stride()), logits_shard.dtype,
+               int(vocab_offset), int(vocab_total), ptr(mask_shard), ptr(hist_ids), ptr(hist_off), hist_max,
+               ptr(uniforms), pkey)
+        if key != self._key:
+            prm = capi.make_params(**params) if isinstance(params, dict) else params
+            desc, _ = capi.fill_desc(logits_shard, uniforms, prm, mask=mask_shard, hist_ids=hist_ids,
+                                     hist_off=hist_off, hist_max=hist_max)
+            self._key, self._desc, self._prm = key, desc, prm
+        if token is None:
+            token = torch.empty(self.rows, dtype=torch.int32, device=uniforms.device)
+        stream = torch.cuda.current_stream(uniforms.device).cuda_stream
         self.epoch += 1
-        capi.shard_candidates_peer(logits_shard, vocab_offset, vocab_total, self.k, params, self.peers, self.rank,
-                                   self.world, self.epoch, mask=mask_shard, hist_ids=hist_ids, hist_off=hist_off,
-                                   hist_max=hist_max)
-        return capi.merge_sample_peer(self.rows, self.world, self.k, self.local, self.epoch, uniforms, params,
-                                      token=token, status=status)
+        capi.shard_candidates_peer_desc(self._desc, vocab_offset, vocab_total, self.k, self.peers, self.rank,
+                                        self.world, self.epoch, stream)
+        return capi.merge_sample_peer(self.rows, self.world, self.k, self.local, self.epoch, uniforms, self._prm,
+                                      token=token, status=status, stream=stream)
 
     def close(self):
         torch.cuda.synchronize()
