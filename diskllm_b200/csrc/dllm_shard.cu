@@ -73,6 +73,9 @@ __host__ __device__ inline int32_t *px_ids(unsigned char *base, int slot, int wo
 
 // diagnostic counter slots of shard_stream_kernel (thread 0 of each row CTA adds its cycles)
 enum : int { SDBG_ROWS = 0, SDBG_LOOP = 1, SDBG_CUT = 2, SDBG_NCUT = 3, SDBG_FINAL = 4, SDBG_UNION = 5 };
+// and of merge_sample_kernel: rows, cycles to the transformed candidates, ranking, draw, and rows
+// that compared every pair
+enum : int { MDBG_ROWS = 8, MDBG_LOAD = 9, MDBG_RANK = 10, MDBG_DRAW = 11, MDBG_PAIRWISE = 12 };
 
 constexpr int SH_SURV = 1024;    // survivors of the threshold pre-filter kept for the exact select
 
@@ -504,30 +507,12 @@ static_assert(ST_FIN <= 2 * ST_T, "union_select sorts 2 * ST_T entries, two per 
 // vector), so the buffer never overflows when a tile starts at or below ST_CAP - E.
 static_assert(ST_CAP >= ST_T * ST_U * 8 + SH_KMAX, "candidate buffer smaller than a tile plus a cut");
 
-// The K best of n <= ST_FIN entries by (key desc, id asc), written sorted to out_key / out_id
-// like block_select: a bitonic sort in shared memory (`tmp`, ST_FIN entries of 8 bytes) of the
-// composites key << 32 | ~id, whose descending order is exactly that ranking.  Keys below the
-// -inf key (negative NaN) are never taken by block_select, which runs instead when one is present.
-__device__ void union_select(const uint32_t *keys, const int *ids, int n, int K, unsigned long long *tmp,
-                             SelScratch &s, uint32_t *out_key, int *out_id) {
-    const int tid = threadIdx.x, NT = blockDim.x;
-    const uint32_t KNEG = okey(-INFINITY);
-    bool odd = false;
-    for (int i = tid; i < n; i += NT) odd |= keys[i] < KNEG;
-    if (__syncthreads_or(odd) || n > ST_FIN) {
-        block_select(keys, ids, 0, n, K, s, out_key, out_id);
-        return;
-    }
-    // 512 composites (zero padding, which sorts last), two per thread: thread t holds 2t and
-    // 2t + 1, so pairs closer than 64 apart are in one warp and are exchanged by shuffles; the
-    // stages with pairs 64 or more apart go through shared memory.
-    const int e0 = 2 * tid;
-    unsigned long long v[2];
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        const int i = e0 + r;
-        v[r] = i < n ? ((unsigned long long)keys[i] << 32) | (uint32_t)~(uint32_t)ids[i] : 0ull;
-    }
+// Sorts 2 * blockDim.x (= 512) 64-bit values held two per thread (thread t holds positions 2t
+// and 2t + 1) into descending order, and writes them to tmp[0, 512) as well.  Bitonic network:
+// pairs closer than 64 apart are in one warp and are exchanged by shuffles, the stages with pairs
+// 64 or more apart go through `tmp`.  Every thread of a 256-thread block must call it.
+__device__ void sort_desc_2x(unsigned long long (&v)[2], unsigned long long *tmp) {
+    const int tid = threadIdx.x, e0 = 2 * tid, NT2 = 2 * blockDim.x;
     auto reg_stages = [&](int k, int jtop) {
         for (int j = jtop; j >= 2; j >>= 1) {
 #pragma unroll
@@ -547,7 +532,7 @@ __device__ void union_select(const uint32_t *keys, const int *ids, int n, int K,
         }
     };
     for (int k = 2; k <= 64; k <<= 1) reg_stages(k, k >> 1);
-    for (int k = 128; k <= 2 * ST_T; k <<= 1) {
+    for (int k = 128; k <= NT2; k <<= 1) {
         tmp[e0] = v[0];
         tmp[e0 + 1] = v[1];
         __syncthreads();
@@ -569,6 +554,31 @@ __device__ void union_select(const uint32_t *keys, const int *ids, int n, int K,
     tmp[e0] = v[0];
     tmp[e0 + 1] = v[1];
     __syncthreads();
+}
+
+// The K best of n <= ST_FIN entries by (key desc, id asc), written sorted to out_key / out_id
+// like block_select: a bitonic sort in shared memory (`tmp`, ST_FIN entries of 8 bytes) of the
+// composites key << 32 | ~id, whose descending order is exactly that ranking.  Keys below the
+// -inf key (negative NaN) are never taken by block_select, which runs instead when one is present.
+__device__ void union_select(const uint32_t *keys, const int *ids, int n, int K, unsigned long long *tmp,
+                             SelScratch &s, uint32_t *out_key, int *out_id) {
+    const int tid = threadIdx.x, NT = blockDim.x;
+    const uint32_t KNEG = okey(-INFINITY);
+    bool odd = false;
+    for (int i = tid; i < n; i += NT) odd |= keys[i] < KNEG;
+    if (__syncthreads_or(odd) || n > ST_FIN) {
+        block_select(keys, ids, 0, n, K, s, out_key, out_id);
+        return;
+    }
+    // 2 * ST_T composites (zero padding, which sorts last), two per thread
+    const int e0 = 2 * tid;
+    unsigned long long v[2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const int i = e0 + r;
+        v[r] = i < n ? ((unsigned long long)keys[i] << 32) | (uint32_t)~(uint32_t)ids[i] : 0ull;
+    }
+    sort_desc_2x(v, tmp);
     // a real composite is never 0 (its low word ~id has the top bit set), so positions past n
     // are the padding, written as block_select writes them
     for (int i = tid; i < K; i += NT) {
@@ -1026,21 +1036,29 @@ struct MergeArgs {
     const unsigned long long *arrive;
     unsigned long long target;
     long long wait_ns;
+    unsigned long long *dbg;  // diagnostic counters (MDBG_*) or null
 };
 
 constexpr int MG_THREADS = 256;
 constexpr int MG_MAX = 16 * SH_KMAX;  // candidates per row (shards x k)
+
+// 32-bit words of the merge kernel's shared memory before its top-k lists: the candidates' values
+// and ids, or the sort's staging area when the sort ranks them
+__host__ __device__ constexpr int merge_lists_words(int n) { return n <= 2 * MG_THREADS ? 4 * MG_THREADS : 2 * n; }
 
 __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArgs a) {
     extern __shared__ __align__(16) unsigned char mdyn[];
     const int n = a.nsh * a.k;
     float *v = reinterpret_cast<float *>(mdyn);
     int *id = reinterpret_cast<int *>(v + n);
-    float *tl = reinterpret_cast<float *>(id + n);
+    // up to 2 * MG_THREADS candidates are ranked by a sort whose staging area (8 bytes per
+    // position) overlays v and id, so the top-k lists start past it
+    float *tl = reinterpret_cast<float *>(mdyn) + merge_lists_words(n);
     int *il = reinterpret_cast<int *>(tl + a.k);
     __shared__ float red_f[MG_THREADS / 32];
     __shared__ int red_i[MG_THREADS / 32];
     const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, NT = blockDim.x;
+    const long long t0c = a.dbg ? clock64() : 0;
     if (a.arrive) {
         // every rank's candidates for this step have landed here once its counter reaches the
         // target; the wait is bounded (a rank that never arrives makes the row DLLM_ROW_ERR_TIMEOUT)
@@ -1118,59 +1136,88 @@ __global__ void __launch_bounds__(MG_THREADS) merge_sample_kernel(const MergeArg
     const float inv_temp = __fdiv_rn(1.0f, p.temperature);
     for (int i = tid; i < n; i += NT) v[i] = __fmul_rn(__fsub_rn(v[i], M), inv_temp);
     __syncthreads();
-    // the k best by (t desc, id asc).  Each shard's list is sorted by (value desc, id asc), and t
-    // is a non-decreasing function of the value, so the list is in (t desc, id asc) order unless
-    // two distinct values round to the same t with their ids the wrong way round.  In order, a
-    // candidate's rank is its position in its own list plus, for every other list, the number of
-    // entries ahead of it (a binary search); otherwise every pair is compared.
-    __shared__ int s_unsorted;
-    if (tid == 0) s_unsorted = 0;
-    __syncthreads();
-    for (int i = tid; i < n; i += NT) {
-        const int j = i % a.k;
-        if (j + 1 < a.k) {
-            const uint32_t k0 = okey(v[i]), k1 = okey(v[i + 1]);
-            if (k0 < k1 || (k0 == k1 && id[i] > id[i + 1])) s_unsorted = 1;
+    const long long t1c = a.dbg ? clock64() : 0;
+    bool pairwise = false;
+    if (n > MG_THREADS && n <= 2 * MG_THREADS) {
+        // more than one candidate per thread: a sort of the composites okey(t) << 32 | ~(id ^ 0x80000000), whose descending order is
+        // (t desc, id asc) with ids compared as signed integers
+        unsigned long long c[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const int i = 2 * tid + r;
+            c[r] = i < n ? ((unsigned long long)okey(v[i]) << 32) | (uint32_t)~((uint32_t)id[i] ^ 0x80000000u) : 0ull;
         }
-    }
-    __syncthreads();
-    const bool sorted_lists = s_unsorted == 0;
-    for (int i = tid; i < n; i += NT) {
-        const uint32_t ki = okey(v[i]);
-        const int ii = id[i];
-        int r = 0;
-        if (sorted_lists) {
-            const int own = i / a.k;
-            r = i - own * a.k;
-            for (int sh = 0; sh < a.nsh; sh++) {
-                if (sh == own) continue;
-                // entries of list sh ahead of (ki, ii): the first position not ahead
-                const float *vl = v + sh * a.k;
-                const int *il2 = id + sh * a.k;
-                int lo = 0, hi = a.k;
-                while (lo < hi) {
-                    const int mid = (lo + hi) >> 1;
-                    const uint32_t km = okey(vl[mid]);
-                    if (km > ki || (km == ki && il2[mid] < ii)) lo = mid + 1;
-                    else hi = mid;
+        __syncthreads();  // the sort's staging area overlays v and id
+        unsigned long long *srt = reinterpret_cast<unsigned long long *>(mdyn);
+        sort_desc_2x(c, srt);
+        for (int i = tid; i < k; i += NT) {
+            const unsigned long long x = srt[i];
+            tl[i] = okey_inv((uint32_t)(x >> 32));
+            il[i] = (int)(~(uint32_t)x ^ 0x80000000u);
+        }
+    } else {
+        // at most one candidate per thread (or more than two): the k best by (t desc, id asc).
+        // Each shard's list is sorted by (value desc, id asc), and t
+        // is a non-decreasing function of the value, so t never increases along a list; only two
+        // distinct values that round to the same t can leave a run of equal t with its ids out of
+        // order.  A candidate's rank is therefore, over every list, the number of entries with a
+        // larger t (a binary search) plus the entries of the equal-t run with a smaller id (a scan of
+        // the run, usually empty); the count stops once it reaches k.  A list whose t increases
+        // somewhere (not expected) makes the row compare every pair.
+        __shared__ int s_unsorted;
+        if (tid == 0) s_unsorted = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += NT) {
+            const int j = i % a.k;
+            if (j + 1 < a.k && okey(v[i]) < okey(v[i + 1])) s_unsorted = 1;
+        }
+        __syncthreads();
+        const bool sorted_lists = s_unsorted == 0;
+        pairwise = !sorted_lists;
+        for (int i = tid; i < n; i += NT) {
+            const uint32_t ki = okey(v[i]);
+            const int ii = id[i];
+            int r = 0;
+            if (sorted_lists) {
+                // its own list first; a count that reaches k already rules the candidate out
+                const int own = i / a.k;
+                for (int q = 0; q < a.nsh && r < k; q++) {
+                    const int sh = own + q < a.nsh ? own + q : own + q - a.nsh;
+                    const float *vl = v + sh * a.k;
+                    const int *il2 = id + sh * a.k;
+                    int lo = 0, hi = a.k;  // the first position whose t is not above ki
+                    while (lo < hi) {
+                        const int mid = (lo + hi) >> 1;
+                        if (okey(vl[mid]) > ki) lo = mid + 1;
+                        else hi = mid;
+                    }
+                    r += lo;
+                    for (int t = lo; t < a.k && okey(vl[t]) == ki; t++) r += il2[t] < ii;
                 }
-                r += lo;
+            } else {
+                for (int j = 0; j < n; j++) {
+                    const uint32_t kj = okey(v[j]);
+                    r += kj > ki || (kj == ki && id[j] < ii);
+                }
             }
-        } else {
-            for (int j = 0; j < n; j++) {
-                const uint32_t kj = okey(v[j]);
-                r += kj > ki || (kj == ki && id[j] < ii);
+            if (r < k) {
+                tl[r] = v[i];
+                il[r] = ii;
             }
-        }
-        if (r < k) {
-            tl[r] = v[i];
-            il[r] = ii;
         }
     }
     __syncthreads();
+    const long long t2c = a.dbg ? clock64() : 0;
     if (wid == 0) {
         const int tok = sample_sorted_list(tl, il, k, p, a.uniforms[row], nullptr, false);
         if (lane == 0) a.token[row] = tok;
+        if (a.dbg && lane == 0) {
+            atomicAdd(a.dbg + MDBG_ROWS, 1ull);
+            atomicAdd(a.dbg + MDBG_LOAD, (unsigned long long)(t1c - t0c));
+            atomicAdd(a.dbg + MDBG_RANK, (unsigned long long)(t2c - t1c));
+            atomicAdd(a.dbg + MDBG_DRAW, (unsigned long long)(clock64() - t2c));
+            if (pairwise) atomicAdd(a.dbg + MDBG_PAIRWISE, 1ull);
+        }
     }
 }
 
@@ -1309,8 +1356,9 @@ dllm_status launch_merge_sample(int rows, int nsh, int k, const float *vals, con
     a.arrive = arrive;
     a.target = target;
     a.wait_ns = wait_ns;
+    a.dbg = debug_counters();
     if (rows == 0) return DLLM_OK;
-    const size_t smem = (size_t)nsh * k * 8 + (size_t)k * 8;
+    const size_t smem = (size_t)merge_lists_words(nsh * k) * 4 + (size_t)k * 8;
     if (shard_smem_attr((const void *)merge_sample_kernel, smem) != cudaSuccess)
         return DLLM_ERR_CUDA;
     merge_sample_kernel<<<rows, MG_THREADS, smem, stream>>>(a);

@@ -96,24 +96,28 @@ def test_config5_shape_bf16(nsh):
     _run(x, allow, hist, params, nsh, 64, seed=nsh)
 
 
-def test_f32_penalties_minp_odd_vocab():
+# shard counts whose merges rank nsh * k <= 256 candidates by search and more than 256 by a sort
+@pytest.mark.parametrize("nsh", [3, 6])
+def test_f32_penalties_minp_odd_vocab(nsh):
     rng = np.random.default_rng(11)
     rows, V = 16, 5000
     x = (rng.standard_normal((rows, V)) * 3.0).astype(np.float32)
     hist = [rng.integers(0, V, 40) for _ in range(rows)]
     params = dict(temperature=0.7, top_k=50, top_p=0.95, min_p=0.01, repetition=1.2, presence=0.3)
-    _run(x, None, hist, params, 3, 64, dtype=torch.float32)
+    _run(x, None, hist, params, nsh, 64, dtype=torch.float32)
 
 
-def test_ties_take_lowest_ids():
+@pytest.mark.parametrize("nsh", [4, 8])
+def test_ties_take_lowest_ids(nsh):
     rng = np.random.default_rng(12)
     rows, V = 8, 8192
     x = rng.integers(-3, 3, (rows, V)).astype(np.float32)  # thousands of equal values
     params = dict(temperature=1.0, top_k=40, top_p=0.8)
-    _run(x, None, None, params, 4, 40, dtype=torch.float32)
+    _run(x, None, None, params, nsh, 40, dtype=torch.float32)
 
 
-def test_fewer_allowed_than_k_and_fully_masked_rows():
+@pytest.mark.parametrize("nsh", [2, 9])
+def test_fewer_allowed_than_k_and_fully_masked_rows(nsh):
     rng = np.random.default_rng(13)
     rows, V = 8, 4096
     x = (rng.standard_normal((rows, V))).astype(np.float32)
@@ -121,7 +125,7 @@ def test_fewer_allowed_than_k_and_fully_masked_rows():
     for r in range(1, rows):
         allow[r, rng.choice(V, size=r * 3, replace=False)] = True  # 3 .. 21 allowed, k = 32
     params = dict(temperature=1.0, top_k=32, top_p=0.9)
-    tok, ora = _run(x, allow, None, params, 2, 32, dtype=torch.float32)
+    tok, ora = _run(x, allow, None, params, nsh, 32, dtype=torch.float32)
     assert tok[0] == ora.token[0] == 31  # fully masked: the reference returns its list's last id
 
 
